@@ -1,0 +1,204 @@
+/*
+ * linattn_b200 — C ABI of the B200 (sm_100a) sparse-attention hot path.
+ *
+ * Plain pointers and sizes only.  Every buffer is device memory owned by the
+ * caller; the library allocates nothing.  Kernels are enqueued on the caller's
+ * `stream` (a cudaStream_t passed as void*; NULL = legacy default stream).
+ * Functions return LINATTN_OK or an error code; linattn_last_error() gives the
+ * message (thread-local).  Device-side problems (a page id outside the page
+ * table, a bounded wait that gave up) are OR-ed into the optional `status`
+ * word (int32 in device memory) as LINATTN_DEV_* bits and never trap.
+ *
+ * Each entry point names the reference function it replaces (paths inside the
+ * tongxin/linattn project).
+ */
+#ifndef LINATTN_B200_H
+#define LINATTN_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types */
+enum {
+  LINATTN_F32 = 0,
+  LINATTN_F16 = 1,
+  LINATTN_BF16 = 2,
+  LINATTN_FP8E4M3 = 3, /* float8_e4m3fn codes + fp32 scales */
+  LINATTN_I32 = 4,
+  LINATTN_I64 = 5
+};
+
+/* host return codes */
+enum { LINATTN_OK = 0, LINATTN_EINVAL = 1, LINATTN_EUNSUPPORTED = 2, LINATTN_ECUDA = 3 };
+
+/* device status bits */
+enum { LINATTN_DEV_BAD_ID = 1, LINATTN_DEV_TIMEOUT = 2, LINATTN_DEV_OVERFLOW = 4 };
+
+/*
+ * KV pages.  Page `p` of (batch b, kv head h) holds `page_size` contiguous rows of
+ * `head_dim` elements at
+ *     base + b*stride_b + phys*stride_page + h*stride_head        (elements)
+ * with phys = page_table[b*page_table_stride + p] (paged pool, stride_b = 0) or
+ * phys = p (no page table).  The reference's contiguous cache (B, H_kv, T, D) is
+ * stride_b = H_kv*T*D, stride_page = page_size*D, stride_head = T*D; the paged pool
+ * [N_phys, H_kv, P, D] is stride_page = H_kv*P*D, stride_head = P*D.
+ * Rows at positions >= seq_lens[b] (or seq_len) are never read.
+ * fp8: k_scale/v_scale hold one fp32 scale per (phys page, kv head).
+ */
+typedef struct {
+  const void* k;
+  const void* v;
+  int64_t stride_b;
+  int64_t stride_page;
+  int64_t stride_head;
+  const int32_t* page_table; /* [B, page_table_stride] or NULL */
+  int64_t page_table_stride;
+  int64_t num_phys_pages; /* bound on page_table entries (device-checked) */
+  const float* k_scale;
+  const float* v_scale;
+  int64_t scale_stride_page;
+  int64_t scale_stride_head;
+  const int32_t* seq_lens; /* [B] or NULL */
+  int64_t seq_len;         /* used when seq_lens is NULL */
+  int32_t dtype;
+  int32_t page_size;
+  int32_t head_dim;
+  int32_t n_kv_heads;
+} linattn_kv_t;
+
+/*
+ * Quest page metadata (channel-wise min and max of K per page and kv head).
+ * Entry (b, page p, head h) at base + b*stride_b + phys*stride_page + h*stride_head
+ * with the same page-table rule as linattn_kv_t.  The reference layout
+ * (B, H, n_pages, D) is stride_b = H*n_pages*D, stride_page = D, stride_head = n_pages*D.
+ */
+typedef struct {
+  const void* mins;
+  const void* maxs;
+  int64_t stride_b;
+  int64_t stride_page;
+  int64_t stride_head;
+  const int32_t* page_table;
+  int64_t page_table_stride;
+  int64_t num_phys_pages;
+  int32_t dtype;
+  int32_t n_heads; /* metadata heads: H_kv (GQA) or H_q (one per query head) */
+} linattn_meta_t;
+
+/* Per-(batch, list head, query) id lists: entry j of list (b, h, t) at
+ * ids[b*stride_b + h*stride_h + t*stride_t + j]; its length is
+ * counts[b*cstride_b + h*cstride_h + t*cstride_t] (or max_len when counts is NULL).
+ * Negative ids are padding and are skipped. */
+typedef struct {
+  const void* ids;
+  int32_t ids_dtype; /* LINATTN_I32 or LINATTN_I64 */
+  int32_t n_heads;   /* list heads; query heads [h*G, (h+1)*G) share list h, G = H_q / n_heads */
+  int64_t stride_b;
+  int64_t stride_h;
+  int64_t stride_t;
+  int64_t max_len;
+  const int32_t* counts;
+  int64_t cstride_b;
+  int64_t cstride_h;
+  int64_t cstride_t;
+} linattn_lists_t;
+
+const char* linattn_last_error(void);
+int linattn_version(void);
+
+/*
+ * Page bounds of a (B, H, T, D) key tensor (any strides, unit stride on D) into
+ * contiguous (B, H, ceil(T/P), D) mins/maxs of the same dtype; the tail page
+ * ignores rows past T.
+ * Replaces page_bounds_torch / page_update_triton,
+ * src/linattn/kernels/triton/quest_pages.py:38-48 and :134-142.
+ */
+int linattn_page_bounds(const void* k, int32_t dtype, int64_t B, int64_t H, int64_t T, int64_t D,
+                        const int64_t* k_strides /*[4] elements*/, int64_t page_size, void* mins, void* maxs,
+                        void* stream);
+
+/*
+ * Refresh the metadata of a paged pool for the pages touched by an append: for
+ * every batch b, pages [first_page[b], ceil(seq_len_b / P)) (first_page NULL = all).
+ * Metadata is written to `meta` (mins/maxs through the same page table); for fp8
+ * pools the bounds are taken over the dequantised keys and rounded outward when
+ * the metadata dtype is narrower than fp32.
+ * Replaces QuestAttention._refresh_pages, src/linattn/variants/selection.py:181-201,
+ * and the paged form of _page_update_kernel, quest_pages.py:84-100.
+ */
+int linattn_paged_page_bounds(const linattn_kv_t* kv, int64_t B, const int32_t* first_page, int64_t max_pages,
+                              const linattn_meta_t* meta, int32_t* status, void* stream);
+
+/*
+ * Quest upper-bound scores s[b,h,t,p] = sum_d max(q_d*min_d, q_d*max_d) in fp32,
+ * written to scores (B, H_q, T_q, n_pages) contiguous, with the selection masks of
+ * the reference applied: pages starting after the query position (offset + t), or
+ * past a ragged sequence end (n_pages_b[b]), are -inf; the query's own page and the
+ * first `sink_pages` pages are +inf.  Query head h reads metadata head
+ * h / (H_q / meta->n_heads).
+ * Replaces page_scores_torch + the masking of page_select_torch,
+ * src/linattn/kernels/triton/quest_pages.py:51-75 (own page per row as in
+ * src/linattn/variants/selection.py:220-230), and _page_score_kernel :103-131.
+ */
+int linattn_quest_scores(const void* q, int32_t q_dtype, int64_t B, int64_t Hq, int64_t Tq, int64_t D,
+                         const int64_t* q_strides /*[4]*/, const linattn_meta_t* meta, int64_t page_size,
+                         int64_t n_pages, int64_t offset, int32_t sink_pages, const int32_t* n_pages_b,
+                         float* scores, int32_t* status, void* stream);
+
+/*
+ * Top-k of every score row (B, H_q, T_q, n_pages), sorted by descending score with
+ * ties broken by the lowest page index, k_b = max(1, min(topk, n_pages_b)).
+ * ids_i64 / ids_i32 (B, H_q, T_q, topk), slots >= k_b set to -1.  When union_ids is
+ * given, also the sorted union of the selected pages (score > -inf) over each group
+ * of `group` consecutive query heads: union_ids (B, H_q/group, T_q, max_union),
+ * union_count (B, H_q/group, T_q), and optionally union_tokens = tokens of those
+ * pages at positions <= offset + t and < seq_len (page_size, seq_lens needed).
+ * Replaces torch.topk in page_select_torch (quest_pages.py:76-77), topk_blocks
+ * (selection.py:51-59) and the GQA union (selection.py:232-235).
+ */
+int linattn_page_topk(const float* scores, int64_t B, int64_t Hq, int64_t Tq, int64_t n_pages, int64_t topk,
+                      const int32_t* n_pages_b, int64_t* ids_i64, int32_t* ids_i32, int64_t group,
+                      int32_t* union_ids, int32_t* union_count, int64_t max_union, int32_t* union_tokens,
+                      int64_t page_size, int64_t offset, const int32_t* seq_lens, int64_t seq_len,
+                      int32_t* status, void* stream);
+
+/*
+ * Exact softmax attention of each query over the KV rows of its list's pages.
+ * q and out are (B, H_q, T_q, D) with element strides; out has q's dtype.  Rows at
+ * positions >= seq_len_b are skipped; with `causal`, rows after offset + t too.
+ * A page list may be split over `n_splits` CTAs (split-KV); the partial (o, lse)
+ * then go to `workspace` (fp32, linattn_sparse_attention_workspace() bytes) and are
+ * merged by the log-sum-exp combine.  lse_out (B, H_q, T_q) optional (natural log).
+ * Replaces block_sparse_attention_torch / _block_sparse_fwd_kernel,
+ * src/linattn/kernels/triton/block_sparse.py:40-163, the C paged decode
+ * src/linattn/kernels/c/decode_attn.c:72-133, and the masked dense attention of
+ * BlockSelectionAttention.attend, src/linattn/variants/selection.py:110-116.
+ */
+int linattn_sparse_attention(const void* q, int32_t q_dtype, int64_t B, int64_t Hq, int64_t Tq,
+                             const int64_t* q_strides /*[4]*/, const linattn_kv_t* kv,
+                             const linattn_lists_t* lists, int32_t causal, int64_t offset, float scale,
+                             void* out, const int64_t* out_strides /*[4]*/, float* lse_out, int32_t n_splits,
+                             float* workspace, int64_t workspace_bytes, int32_t* status, void* stream);
+
+/* Workspace bytes linattn_sparse_attention needs for n_splits > 1. */
+int64_t linattn_sparse_attention_workspace(int64_t B, int64_t Hq, int64_t Tq, int64_t D, int32_t n_splits);
+
+/*
+ * Split-KV merge: o = sum_s exp(lse_s - L) o_s, L = logsumexp_s lse_s, for `rows`
+ * rows of D channels.  o_parts [S, rows, D] fp32, lse_parts [S, rows] (natural log,
+ * -inf for an empty part).  out [rows, D] in out_dtype (f32/f16/bf16); lse_out
+ * [rows] optional.  A row whose parts are all empty gives o = 0, L = -inf.
+ * No reference counterpart (the reference never splits the KV axis); it merges the
+ * per-GPU partials of the sequence-sharded decode after an NCCL all-gather.
+ */
+int linattn_lse_combine(const float* o_parts, const float* lse_parts, int64_t S, int64_t rows, int64_t D,
+                        void* out, int32_t out_dtype, float* lse_out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LINATTN_B200_H */

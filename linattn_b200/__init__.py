@@ -1,0 +1,19 @@
+"""linattn_b200: the sparse-attention hot path of tongxin/linattn on NVIDIA B200 (sm_100a).
+
+Operators (same names and semantics as ``linattn.kernels.triton.*``):
+``page_bounds``, ``page_select``, ``block_sparse_attention``, ``lse_combine``.
+Plugin: ``build("cuda_quest", cfg)`` returns an ``AttentionVariant`` like
+``linattn.registry.build``.  Serving path: ``PagedKVCache`` + ``QuestDecoder``.
+
+Every call runs hand-written CUDA in ``_native/liblinattn_b200.so`` through the C
+ABI of ``include/linattn_b200.h``; there is no CPU fallback.
+"""
+
+from linattn_b200.block_sparse import block_sparse_attention, sparse_attention  # noqa: F401
+from linattn_b200.core import AttnConfig, AttentionVariant  # noqa: F401
+from linattn_b200.merge import lse_combine  # noqa: F401
+from linattn_b200.paged import PagedKVCache, QuestDecoder  # noqa: F401
+from linattn_b200.quest_pages import page_bounds, page_select, quest_select  # noqa: F401
+from linattn_b200.registry import KERNEL_VARIANTS, build, build_cuda, describe_kernel, list_kernel_variants  # noqa: F401
+
+__version__ = "0.1.0"

@@ -1,0 +1,9 @@
+// sparse_attention_kernel instances for __nv_bfloat16 KV.
+#include "attn_dispatch.cuh"
+
+namespace linattn {
+cudaError_t launch_sparse_attention_bf16(const AttnParams& p, int D, int G, unsigned grid, cudaStream_t stream) {
+  return launch_dg<__nv_bfloat16>(p, D, G, grid, stream);
+}
+int tile_rows_bf16(int D) { return tile_rows<__nv_bfloat16>(D); }
+}  // namespace linattn

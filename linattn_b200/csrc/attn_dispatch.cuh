@@ -1,0 +1,54 @@
+// Instantiation helper: one translation unit per KV element type includes this
+// with ATTN_T set, so the template instances compile in parallel.
+#pragma once
+#include "launchers.cuh"
+
+namespace linattn {
+
+template <typename T, int D, int G>
+static cudaError_t launch_one(const AttnParams& p, unsigned grid, cudaStream_t stream) {
+  using S = AttnShape<T, D, G>;
+  static bool configured[64] = {};
+  const int dev = device_index();
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(sparse_attention_kernel<T, D, G>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(S::SMEM_BYTES));
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  sparse_attention_kernel<T, D, G><<<grid, 256, S::SMEM_BYTES, stream>>>(p);
+  return cudaGetLastError();
+}
+
+template <typename T, int D>
+static cudaError_t launch_g(const AttnParams& p, int G, unsigned grid, cudaStream_t stream) {
+  switch (G) {
+    case 1: return launch_one<T, D, 1>(p, grid, stream);
+    case 2: return launch_one<T, D, 2>(p, grid, stream);
+    case 4: return launch_one<T, D, 4>(p, grid, stream);
+    case 8: return launch_one<T, D, 8>(p, grid, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <typename T>
+static cudaError_t launch_dg(const AttnParams& p, int D, int G, unsigned grid, cudaStream_t stream) {
+  switch (D) {
+    case 8: if constexpr (sizeof(T) >= 2) return launch_g<T, 8>(p, G, grid, stream); else return cudaErrorInvalidValue;
+    case 16: return launch_g<T, 16>(p, G, grid, stream);
+    case 32: return launch_g<T, 32>(p, G, grid, stream);
+    case 64: return launch_g<T, 64>(p, G, grid, stream);
+    case 128: return launch_g<T, 128>(p, G, grid, stream);
+    case 256: return launch_g<T, 256>(p, G, grid, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <typename T>
+constexpr int tile_rows(int D) {
+  return (16384 / (D * static_cast<int>(sizeof(T)))) < 64 ? (16384 / (D * static_cast<int>(sizeof(T)))) : 64;
+}
+
+}  // namespace linattn

@@ -1,0 +1,9 @@
+// sparse_attention_kernel instances for __half KV.
+#include "attn_dispatch.cuh"
+
+namespace linattn {
+cudaError_t launch_sparse_attention_f16(const AttnParams& p, int D, int G, unsigned grid, cudaStream_t stream) {
+  return launch_dg<__half>(p, D, G, grid, stream);
+}
+int tile_rows_f16(int D) { return tile_rows<__half>(D); }
+}  // namespace linattn

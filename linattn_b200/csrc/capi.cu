@@ -1,0 +1,255 @@
+// extern "C" entry points: argument validation, template dispatch, launch.
+// Nothing here allocates device memory; every buffer comes from the caller.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "launchers.cuh"
+
+namespace linattn {
+int device_index() {
+  int d = -1;
+  if (cudaGetDevice(&d) != cudaSuccess) return -1;
+  return d;
+}
+}  // namespace linattn
+
+using namespace linattn;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return LINATTN_OK;
+  return fail(LINATTN_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+int elem_bytes(int dtype) {
+  switch (dtype) {
+    case LINATTN_F32: return 4;
+    case LINATTN_F16: return 2;
+    case LINATTN_BF16: return 2;
+    case LINATTN_FP8E4M3: return 1;
+    case LINATTN_I32: return 4;
+    case LINATTN_I64: return 8;
+    default: return 0;
+  }
+}
+
+bool is_float16_32(int dtype) { return dtype == LINATTN_F32 || dtype == LINATTN_F16 || dtype == LINATTN_BF16; }
+
+bool aligned(const void* p, int64_t a) { return (reinterpret_cast<uintptr_t>(p) % static_cast<uintptr_t>(a)) == 0; }
+
+bool head_dim_ok(int64_t D) { return D == 8 || D == 16 || D == 32 || D == 64 || D == 128 || D == 256; }
+
+int attn_tile_rows(int dtype, int D) {
+  switch (dtype) {
+    case LINATTN_F32: return tile_rows_f32(D);
+    case LINATTN_F16: return tile_rows_f16(D);
+    case LINATTN_BF16: return tile_rows_bf16(D);
+    case LINATTN_FP8E4M3: return tile_rows_fp8(D);
+    default: return 0;
+  }
+}
+
+int check_kv(const linattn_kv_t* kv) {
+  if (!kv) return fail(LINATTN_EINVAL, "kv descriptor is NULL");
+  const int eb = elem_bytes(kv->dtype);
+  if (!(is_float16_32(kv->dtype) || kv->dtype == LINATTN_FP8E4M3))
+    return fail(LINATTN_EUNSUPPORTED, "kv dtype %d not supported", kv->dtype);
+  if (!kv->k || !kv->v) return fail(LINATTN_EINVAL, "kv base pointers must be non-NULL");
+  if (kv->page_size <= 0 || kv->n_kv_heads <= 0) return fail(LINATTN_EINVAL, "page_size and n_kv_heads must be > 0");
+  if (!head_dim_ok(kv->head_dim)) return fail(LINATTN_EUNSUPPORTED, "head_dim %d not in {8,...,256}", kv->head_dim);
+  if ((static_cast<int64_t>(kv->head_dim) * eb) % 16 != 0)
+    return fail(LINATTN_EUNSUPPORTED, "head_dim*elem_bytes must be a multiple of 16 (got %d*%d)", kv->head_dim, eb);
+  if (!aligned(kv->k, 16) || !aligned(kv->v, 16)) return fail(LINATTN_EINVAL, "K/V base pointers must be 16-byte aligned");
+  if ((kv->stride_b * eb) % 16 || (kv->stride_page * eb) % 16 || (kv->stride_head * eb) % 16)
+    return fail(LINATTN_EINVAL, "K/V strides must be multiples of 16 bytes");
+  if (kv->page_table && (kv->page_table_stride <= 0 || kv->num_phys_pages <= 0))
+    return fail(LINATTN_EINVAL, "page_table_stride and num_phys_pages must be > 0 with a page table");
+  if (kv->dtype == LINATTN_FP8E4M3 && (!kv->k_scale || !kv->v_scale))
+    return fail(LINATTN_EINVAL, "fp8 KV needs k_scale and v_scale");
+  if (!kv->seq_lens && kv->seq_len < 0) return fail(LINATTN_EINVAL, "seq_len must be >= 0");
+  return LINATTN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* linattn_last_error(void) { return g_err.c_str(); }
+
+int linattn_version(void) { return 1; }
+
+int linattn_page_bounds(const void* k, int32_t dtype, int64_t B, int64_t H, int64_t T, int64_t D,
+                        const int64_t* k_strides, int64_t page_size, void* mins, void* maxs, void* stream) {
+  if (!is_float16_32(dtype)) return fail(LINATTN_EUNSUPPORTED, "page_bounds: dtype %d not supported", dtype);
+  if (!k || !mins || !maxs || !k_strides) return fail(LINATTN_EINVAL, "page_bounds: NULL pointer");
+  if (B < 0 || H < 0 || T < 0 || D <= 0 || page_size <= 0)
+    return fail(LINATTN_EINVAL, "page_bounds: bad shape B=%lld H=%lld T=%lld D=%lld P=%lld", (long long)B,
+                (long long)H, (long long)T, (long long)D, (long long)page_size);
+  return cuda_status(launch_page_bounds(k, dtype, B, H, T, D, k_strides, page_size, mins, maxs,
+                                        static_cast<cudaStream_t>(stream)),
+                     "page_bounds");
+}
+
+int linattn_paged_page_bounds(const linattn_kv_t* kv, int64_t B, const int32_t* first_page, int64_t max_pages,
+                              const linattn_meta_t* meta, int32_t* status, void* stream) {
+  int rc = check_kv(kv);
+  if (rc) return rc;
+  if (!meta || !meta->mins || !meta->maxs) return fail(LINATTN_EINVAL, "paged_page_bounds: metadata pointers NULL");
+  if (!is_float16_32(meta->dtype)) return fail(LINATTN_EUNSUPPORTED, "metadata dtype %d not supported", meta->dtype);
+  if (meta->page_table && (meta->page_table_stride <= 0 || meta->num_phys_pages <= 0))
+    return fail(LINATTN_EINVAL, "metadata page table needs a stride and num_phys_pages");
+  if (B < 0 || max_pages < 0) return fail(LINATTN_EINVAL, "paged_page_bounds: B and max_pages must be >= 0");
+  return cuda_status(launch_paged_page_bounds(*kv, B, first_page, max_pages, *meta, status,
+                                              static_cast<cudaStream_t>(stream)),
+                     "paged_page_bounds");
+}
+
+int linattn_quest_scores(const void* q, int32_t q_dtype, int64_t B, int64_t Hq, int64_t Tq, int64_t D,
+                         const int64_t* q_strides, const linattn_meta_t* meta, int64_t page_size, int64_t n_pages,
+                         int64_t offset, int32_t sink_pages, const int32_t* n_pages_b, float* scores,
+                         int32_t* status, void* stream) {
+  if (!q || !q_strides || !meta || !scores) return fail(LINATTN_EINVAL, "quest_scores: NULL pointer");
+  if (!is_float16_32(q_dtype)) return fail(LINATTN_EUNSUPPORTED, "quest_scores: q dtype %d not supported", q_dtype);
+  if (!is_float16_32(meta->dtype))
+    return fail(LINATTN_EUNSUPPORTED, "quest_scores: metadata dtype %d not supported", meta->dtype);
+  if (!head_dim_ok(D)) return fail(LINATTN_EUNSUPPORTED, "quest_scores: head_dim %lld not in {8,...,256}", (long long)D);
+  if (meta->n_heads <= 0 || Hq % meta->n_heads)
+    return fail(LINATTN_EINVAL, "quest_scores: metadata heads (%d) must divide query heads (%lld)", meta->n_heads,
+                (long long)Hq);
+  const int eb = elem_bytes(meta->dtype);
+  if (!aligned(meta->mins, 16) || !aligned(meta->maxs, 16) || (meta->stride_b * eb) % 16 ||
+      (meta->stride_page * eb) % 16 || (meta->stride_head * eb) % 16)
+    return fail(LINATTN_EINVAL, "quest_scores: metadata rows must be 16-byte aligned");
+  if (meta->page_table && (meta->page_table_stride < n_pages || meta->num_phys_pages <= 0))
+    return fail(LINATTN_EINVAL, "quest_scores: page table stride must cover n_pages");
+  if (page_size <= 0 || n_pages < 0 || B < 0 || Tq < 0 || offset < 0)
+    return fail(LINATTN_EINVAL, "quest_scores: bad sizes");
+  return cuda_status(launch_quest_scores(q, q_dtype, B, Hq, Tq, D, q_strides, *meta, page_size, n_pages, offset,
+                                         sink_pages, n_pages_b, scores, status, static_cast<cudaStream_t>(stream)),
+                     "quest_scores");
+}
+
+int linattn_page_topk(const float* scores, int64_t B, int64_t Hq, int64_t Tq, int64_t n_pages, int64_t topk,
+                      const int32_t* n_pages_b, int64_t* ids_i64, int32_t* ids_i32, int64_t group,
+                      int32_t* union_ids, int32_t* union_count, int64_t max_union, int32_t* union_tokens,
+                      int64_t page_size, int64_t offset, const int32_t* seq_lens, int64_t seq_len, int32_t* status,
+                      void* stream) {
+  if (!scores) return fail(LINATTN_EINVAL, "page_topk: scores is NULL");
+  if (n_pages <= 0 || n_pages > 32768)
+    return fail(LINATTN_EUNSUPPORTED, "page_topk: n_pages %lld outside [1, 32768]", (long long)n_pages);
+  if (topk < 1 || topk > 4096) return fail(LINATTN_EUNSUPPORTED, "page_topk: topk %lld outside [1, 4096]", (long long)topk);
+  if (group < 1 || Hq % group) return fail(LINATTN_EINVAL, "page_topk: group must divide Hq");
+  if (union_ids && (!union_count || max_union < 1))
+    return fail(LINATTN_EINVAL, "page_topk: union needs union_count and max_union >= 1");
+  if (union_tokens && page_size <= 0) return fail(LINATTN_EINVAL, "page_topk: union_tokens needs page_size");
+  const size_t smem = page_topk_smem_bytes(n_pages, topk);
+  if (smem > 200 * 1024) return fail(LINATTN_EUNSUPPORTED, "page_topk: n_pages/topk too large for shared memory");
+  TopkParams p;
+  p.scores = scores; p.B = B; p.Hq = Hq; p.Tq = Tq; p.n = n_pages; p.topk = topk; p.n_pages_b = n_pages_b;
+  p.ids64 = ids_i64; p.ids32 = ids_i32; p.group = group; p.union_ids = union_ids; p.union_count = union_count;
+  p.max_union = max_union; p.union_tokens = union_tokens; p.P = page_size > 0 ? page_size : 1; p.offset = offset;
+  p.seq_lens = seq_lens; p.seq_len = seq_len; p.status = status;
+  return cuda_status(launch_page_topk(p, static_cast<cudaStream_t>(stream)), "page_topk");
+}
+
+int64_t linattn_sparse_attention_workspace(int64_t B, int64_t Hq, int64_t Tq, int64_t D, int32_t n_splits) {
+  if (n_splits <= 1) return 0;
+  return static_cast<int64_t>(n_splits) * B * Hq * Tq * (D + 1) * static_cast<int64_t>(sizeof(float));
+}
+
+int linattn_sparse_attention(const void* q, int32_t q_dtype, int64_t B, int64_t Hq, int64_t Tq,
+                             const int64_t* q_strides, const linattn_kv_t* kv, const linattn_lists_t* lists,
+                             int32_t causal, int64_t offset, float scale, void* out, const int64_t* out_strides,
+                             float* lse_out, int32_t n_splits, float* workspace, int64_t workspace_bytes,
+                             int32_t* status, void* stream) {
+  int rc = check_kv(kv);
+  if (rc) return rc;
+  if (!q || !q_strides || !out || !out_strides || !lists || !lists->ids)
+    return fail(LINATTN_EINVAL, "sparse_attention: NULL pointer");
+  if (!is_float16_32(q_dtype)) return fail(LINATTN_EUNSUPPORTED, "sparse_attention: q dtype %d not supported", q_dtype);
+  if (lists->ids_dtype != LINATTN_I32 && lists->ids_dtype != LINATTN_I64)
+    return fail(LINATTN_EINVAL, "sparse_attention: list ids must be int32 or int64");
+  if (B < 0 || Tq < 0 || Hq <= 0) return fail(LINATTN_EINVAL, "sparse_attention: bad sizes");
+  if (Hq % kv->n_kv_heads) return fail(LINATTN_EINVAL, "sparse_attention: H_kv must divide H_q");
+  if (lists->n_heads <= 0 || Hq % lists->n_heads || lists->n_heads % kv->n_kv_heads)
+    return fail(LINATTN_EINVAL,
+                "sparse_attention: list heads (%d) must divide H_q (%lld) and be a multiple of H_kv (%d)",
+                lists->n_heads, (long long)Hq, kv->n_kv_heads);
+  if (lists->max_len < 0) return fail(LINATTN_EINVAL, "sparse_attention: max_len < 0");
+  const int D = kv->head_dim;
+  const int TR = attn_tile_rows(kv->dtype, D);
+  if (kv->page_size > TR && kv->page_size % TR)
+    return fail(LINATTN_EUNSUPPORTED, "sparse_attention: page_size %d > %d must be a multiple of %d", kv->page_size,
+                TR, TR);
+  if (n_splits < 1) return fail(LINATTN_EINVAL, "sparse_attention: n_splits must be >= 1");
+  const int64_t rows = B * Hq * Tq;
+  if (rows == 0) return LINATTN_OK;
+  AttnParams p;
+  p.q = q; p.q_dtype = q_dtype; p.B = B; p.Hq = Hq; p.Tq = Tq;
+  for (int i = 0; i < 4; ++i) { p.qs[i] = q_strides[i]; p.os[i] = out_strides[i]; }
+  p.kv = *kv; p.lists = *lists; p.causal = causal; p.offset = offset;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.out = out; p.lse_out = lse_out; p.n_splits = n_splits; p.status = status;
+  const int64_t g_total = Hq / lists->n_heads;
+  int G = 1;
+  while (G < g_total && G < 8) G <<= 1;
+  p.heads_per_list = static_cast<int>(g_total);
+  p.n_head_chunks = static_cast<int>((g_total + G - 1) / G);
+  p.ws_o = nullptr;
+  p.ws_lse = nullptr;
+  if (n_splits > 1) {
+    const int64_t need = linattn_sparse_attention_workspace(B, Hq, Tq, D, n_splits);
+    if (!workspace || workspace_bytes < need)
+      return fail(LINATTN_EINVAL, "sparse_attention: workspace of %lld bytes needed", (long long)need);
+    if (!aligned(workspace, 16)) return fail(LINATTN_EINVAL, "sparse_attention: workspace must be 16-byte aligned");
+    p.ws_o = workspace;
+    p.ws_lse = workspace + static_cast<int64_t>(n_splits) * rows * D;
+  }
+  const int64_t units = B * static_cast<int64_t>(lists->n_heads) * Tq;
+  const int64_t blocks = units * p.n_head_chunks * n_splits;
+  if (blocks > 0x7fffffffLL) return fail(LINATTN_EUNSUPPORTED, "sparse_attention: grid too large");
+  const unsigned grid = static_cast<unsigned>(blocks);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  switch (kv->dtype) {
+    case LINATTN_F32: e = launch_sparse_attention_f32(p, D, G, grid, st); break;
+    case LINATTN_F16: e = launch_sparse_attention_f16(p, D, G, grid, st); break;
+    case LINATTN_BF16: e = launch_sparse_attention_bf16(p, D, G, grid, st); break;
+    case LINATTN_FP8E4M3: e = launch_sparse_attention_fp8(p, D, G, grid, st); break;
+    default: return fail(LINATTN_EUNSUPPORTED, "sparse_attention: kv dtype");
+  }
+  rc = cuda_status(e, "sparse_attention");
+  if (rc || n_splits == 1) return rc;
+  return cuda_status(launch_lse_combine(p.ws_o, p.ws_lse, n_splits, rows, D, out, q_dtype, Hq, Tq, out_strides,
+                                        lse_out, st),
+                     "sparse_attention combine");
+}
+
+int linattn_lse_combine(const float* o_parts, const float* lse_parts, int64_t S, int64_t rows, int64_t D, void* out,
+                        int32_t out_dtype, float* lse_out, void* stream) {
+  if (!o_parts || !lse_parts || !out) return fail(LINATTN_EINVAL, "lse_combine: NULL pointer");
+  if (!is_float16_32(out_dtype)) return fail(LINATTN_EUNSUPPORTED, "lse_combine: out dtype %d", out_dtype);
+  if (S < 1 || rows < 0 || D < 1 || D > 256) return fail(LINATTN_EINVAL, "lse_combine: bad sizes (D <= 256)");
+  const int64_t os[4] = {0, 0, D, 1};
+  return cuda_status(launch_lse_combine(o_parts, lse_parts, S, rows, D, out, out_dtype, 1, rows > 0 ? rows : 1, os,
+                                        lse_out, static_cast<cudaStream_t>(stream)),
+                     "lse_combine");
+}
+
+}  // extern "C"

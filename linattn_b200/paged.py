@@ -1,0 +1,223 @@
+"""Paged KV pool with Quest metadata, and the allocation-free Quest decode step.
+
+The reference has no physical paged cache (``src/linattn/kv/cache.py`` is a hit-rate
+simulator); its only page layout is logical: page ``p`` of ``(b, h)`` is
+``K[b, h, p*P:(p+1)*P]`` of a contiguous cache (``quest_pages.py:38-48``,
+``c_attention.py:124-125``).  This module keeps that logical contract and stores it
+B200-first:
+
+* ``k_pool, v_pool [N_phys, H_kv, P, D]`` - each (page, head) is one contiguous
+  ``P*D`` chunk (16 KiB in bf16 at P=64, D=128), moved by one TMA bulk copy;
+* ``page_table int32 [B, max_pages]`` maps logical to physical pages;
+* ``meta_min/meta_max [N_phys, H_kv, D]`` - Quest's channel bounds per page;
+* fp8 e4m3 pools add ``k_scale/v_scale fp32 [N_phys, H_kv]`` (``kv/quant.py:90-93``
+  applied per (page, head)); the metadata then bounds the dequantised keys, rounded
+  outward to the metadata dtype.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from linattn_b200 import _lib as L
+from linattn_b200.block_sparse import choose_splits, sparse_attention, tile_rows
+from linattn_b200.quest_pages import DECODE_OFFSET, QuestSelection
+
+__all__ = ["PagedKVCache", "QuestDecoder"]
+
+
+class PagedKVCache:
+    """Physical paged KV pool (one per layer) with a host-side page allocator."""
+
+    def __init__(self, batch: int, n_kv_heads: int, head_dim: int, page_size: int, max_pages: int, *,
+                 num_phys_pages: Optional[int] = None, dtype: torch.dtype = torch.bfloat16,
+                 meta_dtype: Optional[torch.dtype] = None, device="cuda"):
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise ValueError("PagedKVCache lives in device memory (cuda)")
+        self.batch, self.n_kv_heads, self.head_dim, self.page_size = batch, n_kv_heads, head_dim, page_size
+        self.max_pages = max_pages
+        self.num_phys_pages = num_phys_pages or batch * max_pages
+        self.fp8 = dtype in (torch.float8_e4m3fn, torch.uint8)
+        self.dtype = dtype
+        pool_dtype = torch.uint8 if self.fp8 else dtype
+        shape = (self.num_phys_pages, n_kv_heads, page_size, head_dim)
+        self.k_pool = torch.zeros(shape, dtype=pool_dtype, device=self.device)
+        self.v_pool = torch.zeros(shape, dtype=pool_dtype, device=self.device)
+        self.meta_dtype = meta_dtype or (torch.bfloat16 if self.fp8 else dtype)
+        mshape = (self.num_phys_pages, n_kv_heads, head_dim)
+        self.meta_min = torch.zeros(mshape, dtype=self.meta_dtype, device=self.device)
+        self.meta_max = torch.zeros(mshape, dtype=self.meta_dtype, device=self.device)
+        if self.fp8:
+            self.k_scale = torch.ones(self.num_phys_pages, n_kv_heads, dtype=torch.float32, device=self.device)
+            self.v_scale = torch.ones_like(self.k_scale)
+        else:
+            self.k_scale = self.v_scale = None
+        self.page_table = torch.full((batch, max_pages), -1, dtype=torch.int32, device=self.device)
+        self.seq_lens = torch.zeros(batch, dtype=torch.int32, device=self.device)
+        self.n_pages_b = torch.zeros(batch, dtype=torch.int32, device=self.device)
+        self._host_lens = [0] * batch
+        self._host_table = [[] for _ in range(batch)]
+        self._free = list(range(self.num_phys_pages - 1, -1, -1))
+
+    # -- descriptors ---------------------------------------------------------------
+    def kv_desc(self) -> L.KV:
+        hk, p, d = self.n_kv_heads, self.page_size, self.head_dim
+        return L.KV(self.k_pool.data_ptr(), self.v_pool.data_ptr(), 0, hk * p * d, p * d,
+                    self.page_table.data_ptr(), self.max_pages, self.num_phys_pages,
+                    L.ptr(self.k_scale), L.ptr(self.v_scale), hk, 1,
+                    self.seq_lens.data_ptr(), 0, L.FP8E4M3 if self.fp8 else L.dtype_code(self.k_pool), p, d, hk)
+
+    def meta_desc(self) -> L.Meta:
+        hk, d = self.n_kv_heads, self.head_dim
+        return L.Meta(self.meta_min.data_ptr(), self.meta_max.data_ptr(), 0, hk * d, d, self.page_table.data_ptr(),
+                      self.max_pages, self.num_phys_pages, L.dtype_code(self.meta_min), hk)
+
+    # -- page allocation (host) ----------------------------------------------------
+    def _ensure_pages(self, b: int, n_pages: int) -> None:
+        table = self._host_table[b]
+        if n_pages > self.max_pages:
+            raise ValueError(f"sequence {b} needs {n_pages} pages > max_pages {self.max_pages}")
+        new = []
+        while len(table) < n_pages:
+            if not self._free:
+                raise RuntimeError("paged KV pool is full")
+            phys = self._free.pop()
+            table.append(phys)
+            new.append(phys)
+        if new:
+            start = len(table) - len(new)
+            self.page_table[b, start:len(table)] = torch.tensor(new, dtype=torch.int32, device=self.device)
+
+    def set_page_table(self, table: torch.Tensor, seq_lens) -> None:
+        """Install an externally built page table (e.g. a permutation) and lengths."""
+        if table.shape != (self.batch, self.max_pages):
+            raise ValueError("page table shape must be (batch, max_pages)")
+        self.page_table.copy_(table.to(torch.int32))
+        lens = [int(x) for x in seq_lens]
+        self._host_lens = lens
+        host = table.cpu().tolist()
+        used = set()
+        for b in range(self.batch):
+            n = math.ceil(lens[b] / self.page_size)
+            self._host_table[b] = [int(x) for x in host[b][:n]]
+            used.update(self._host_table[b])
+        self._free = [p for p in range(self.num_phys_pages - 1, -1, -1) if p not in used]
+        self._sync_lens()
+
+    def _sync_lens(self) -> None:
+        lens = torch.tensor(self._host_lens, dtype=torch.int32)
+        self.seq_lens.copy_(lens)
+        self.n_pages_b.copy_((lens + self.page_size - 1) // self.page_size)
+
+    # -- writes ----------------------------------------------------------------------
+    def append(self, k: torch.Tensor, v: torch.Tensor) -> None:
+        """Append ``(B, H_kv, T_new, D)`` keys/values to every sequence and refresh the
+        metadata of the touched pages (``QuestAttention._refresh_pages``,
+        ``src/linattn/variants/selection.py:181-201``).  16/32-bit pools only."""
+        if self.fp8:
+            raise NotImplementedError("fp8 pools are written a page at a time (write_pages)")
+        L.require_cuda(k, v)
+        b_, hk, tn, d = k.shape
+        if (b_, hk, d) != (self.batch, self.n_kv_heads, self.head_dim):
+            raise ValueError("append shape mismatch")
+        first = []
+        for b in range(self.batch):
+            start = self._host_lens[b]
+            end = start + tn
+            self._ensure_pages(b, math.ceil(end / self.page_size))
+            first.append(start // self.page_size)
+            pos = torch.arange(start, end, device=self.device)
+            phys = self.page_table[b].long()[pos // self.page_size]
+            rows = pos % self.page_size
+            self.k_pool[phys, :, rows] = k[b].transpose(0, 1).to(self.k_pool.dtype)
+            self.v_pool[phys, :, rows] = v[b].transpose(0, 1).to(self.v_pool.dtype)
+            self._host_lens[b] = end
+        self._sync_lens()
+        self.refresh_meta(torch.tensor(first, dtype=torch.int32, device=self.device))
+
+    def refresh_meta(self, first_page: Optional[torch.Tensor] = None) -> None:
+        """Recompute page bounds for pages ``[first_page[b], n_pages_b)`` (all if None)."""
+        status = L.status_word(self.device)
+        kv, meta = self.kv_desc(), self.meta_desc()
+        L.check(L.lib().linattn_paged_page_bounds(kv, self.batch, L.ptr(first_page), self.max_pages, meta,
+                                                  status.data_ptr(), torch.cuda.current_stream(self.device).cuda_stream))
+        if L.strict():
+            L.check_status(self.device)
+
+
+class QuestDecoder:
+    """One Quest decode step over a :class:`PagedKVCache`, with every buffer allocated
+    once: page scores -> top-k + GQA union -> sparse attention (split-KV + merge).
+
+    ``step(q)`` takes ``q (B, H_q, 1, D)`` (one new token per sequence, at position
+    ``seq_len_b - 1``) and returns ``o (B, H_q, 1, D)`` in q's dtype.  The budget is
+    ``topk`` pages per query head including the forced pages (own page and
+    ``sink_pages`` leading pages), as in ``page_select_torch``.
+    """
+
+    def __init__(self, cache: PagedKVCache, n_heads: int, topk: int, *, sink_pages: int = 0,
+                 scale: Optional[float] = None, gqa_union: bool = True, n_splits: Optional[int] = None,
+                 q_dtype: torch.dtype = torch.bfloat16):
+        self.cache = cache
+        self.n_heads = n_heads
+        self.group = n_heads // cache.n_kv_heads if gqa_union else 1
+        self.topk = max(1, min(topk, cache.max_pages))
+        self.sink_pages = sink_pages
+        self.scale = scale if scale is not None else 1.0 / math.sqrt(cache.head_dim)
+        dev = cache.device
+        b, n = cache.batch, cache.max_pages
+        self.scores = torch.empty(b, n_heads, 1, n, dtype=torch.float32, device=dev)
+        self.ids = torch.empty(b, n_heads, 1, self.topk, dtype=torch.int32, device=dev)
+        self.max_union = min(self.group * self.topk, n)
+        n_lists = n_heads // self.group
+        self.union_ids = torch.empty(b, n_lists, 1, self.max_union, dtype=torch.int32, device=dev)
+        self.union_count = torch.empty(b, n_lists, 1, dtype=torch.int32, device=dev)
+        self.union_tokens = torch.empty_like(self.union_count)
+        self.out = torch.empty(b, n_heads, 1, cache.head_dim, dtype=q_dtype, device=dev)
+        eb = 1 if cache.fp8 else cache.k_pool.element_size()
+        tr = tile_rows(eb, cache.head_dim)
+        tiles = max(1, (self.max_union * cache.page_size + tr - 1) // tr)
+        g_t = 1
+        while g_t < min(self.group, 8):
+            g_t <<= 1
+        units = b * n_lists * ((self.group + g_t - 1) // g_t)
+        self.n_splits = n_splits or choose_splits(units, tiles, dev)
+        need = L.lib().linattn_sparse_attention_workspace(b, n_heads, 1, cache.head_dim, self.n_splits)
+        self.workspace = torch.empty(max(1, (need + 3) // 4), dtype=torch.float32, device=dev)
+        self._lists = L.Lists(self.union_ids.data_ptr(), L.I32, n_lists, *self.union_ids.stride()[:3],
+                              self.max_union, self.union_count.data_ptr(), *self.union_count.stride())
+
+    def select(self, q: torch.Tensor) -> QuestSelection:
+        c = self.cache
+        dev = c.device
+        status = L.status_word(dev)
+        stream = L.stream_of(q)
+        b, hq, tq, d = q.shape
+        lib = L.lib()
+        L.check(lib.linattn_quest_scores(q.data_ptr(), L.dtype_code(q), b, hq, tq, d, L.strides4(q), c.meta_desc(),
+                                         c.page_size, c.max_pages, DECODE_OFFSET, self.sink_pages,
+                                         c.n_pages_b.data_ptr(), self.scores.data_ptr(), status.data_ptr(), stream))
+        L.check(lib.linattn_page_topk(self.scores.data_ptr(), b, hq, tq, c.max_pages, self.topk,
+                                      c.n_pages_b.data_ptr(), None, self.ids.data_ptr(), self.group,
+                                      self.union_ids.data_ptr(), self.union_count.data_ptr(), self.max_union,
+                                      self.union_tokens.data_ptr(), c.page_size, DECODE_OFFSET,
+                                      c.seq_lens.data_ptr(), 0, status.data_ptr(), stream))
+        return QuestSelection(self.ids, self.scores, self.union_ids, self.union_count, self.union_tokens)
+
+    def attend(self, q: torch.Tensor) -> torch.Tensor:
+        sparse_attention(q, self.cache.kv_desc(), self._lists, causal=False, scale=self.scale, out=self.out,
+                         n_splits=self.n_splits, workspace=self.workspace)
+        return self.out
+
+    def step(self, q: torch.Tensor) -> torch.Tensor:
+        if q.shape != (self.cache.batch, self.n_heads, 1, self.cache.head_dim):
+            raise ValueError(f"q must be (B, H_q, 1, D) = {(self.cache.batch, self.n_heads, 1, self.cache.head_dim)}")
+        self.select(q)
+        out = self.attend(q)
+        if L.strict():
+            L.check_status(self.cache.device)
+        return out
