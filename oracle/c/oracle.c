@@ -78,6 +78,77 @@ static inline void topk_push(float s, int idx, float* ts, int* ti, int* n, int k
   ti[pos] = idx;
 }
 
+/* Page selection of one (batch, kv head) unit: top-k per query head of the group,
+   union written ascending to ul[0..*cnt).  Returns 2 when the union overflowed. */
+static int quest_select_unit(int dtype, const void* q, const void* meta_min, const void* meta_max,
+                             const int32_t* page_table, const int32_t* seq_lens, int Hq, int Hkv, int D, int P,
+                             int max_pages, int topk, int sink_pages, int unit, int32_t* ul, int32_t* cnt_out,
+                             int max_union) {
+  const int group = Hq / Hkv;
+  const int b = unit / Hkv, kh = unit % Hkv;
+  const int len = seq_lens[b];
+  const int nb = (len + P - 1) / P;
+  const int kb = topk < nb ? topk : nb;
+  float qv[512], mn[512], mx[512];
+  float* ts = (float*)malloc(sizeof(float) * (size_t)(kb > 0 ? kb : 1));
+  int* ti = (int*)malloc(sizeof(int) * (size_t)(kb > 0 ? kb : 1));
+  uint8_t* in_union = (uint8_t*)calloc((size_t)(nb > 0 ? nb : 1), 1);
+  for (int g = 0; g < group && nb > 0; ++g) {
+    const int h = kh * group + g;
+    load_row(dtype, q, ((int64_t)b * Hq + h) * D, D, qv);
+    int n = 0;
+    for (int p = 0; p < nb; ++p) {
+      float s;
+      if (p == nb - 1 || p < sink_pages) {
+        s = INFINITY;
+      } else {
+        const int phys = page_table[(int64_t)b * max_pages + p];
+        const int64_t mo = ((int64_t)phys * Hkv + kh) * D;
+        load_row(dtype, meta_min, mo, D, mn);
+        load_row(dtype, meta_max, mo, D, mx);
+        s = 0.f;
+        for (int d = 0; d < D; ++d) {
+          const float a = qv[d] * mn[d], c = qv[d] * mx[d];
+          s += a > c ? a : c;
+        }
+      }
+      topk_push(s, p, ts, ti, &n, kb);
+    }
+    for (int i = 0; i < n; ++i) in_union[ti[i]] = 1;
+  }
+  int cnt = 0, bad = 0;
+  for (int p = 0; p < nb; ++p)
+    if (in_union[p]) {
+      if (cnt < max_union) ul[cnt] = p;
+      ++cnt;
+    }
+  if (cnt > max_union) {
+    bad = 2;
+    cnt = max_union;
+  }
+  *cnt_out = cnt;
+  free(ts);
+  free(ti);
+  free(in_union);
+  return bad;
+}
+
+/* Selection only, for units [unit_begin, unit_end) of the B*Hkv (batch, kv head) units. */
+int oracle_quest_select(int dtype, const void* q, const void* meta_min, const void* meta_max,
+                        const int32_t* page_table, const int32_t* seq_lens, int B, int Hq, int Hkv, int D, int P,
+                        int max_pages, int topk, int sink_pages, int32_t* union_ids, int32_t* union_cnt,
+                        int max_union, int unit_begin, int unit_end) {
+  if (Hq % Hkv || D > 512 || topk < 1) return 1;
+  if (unit_end > B * Hkv) unit_end = B * Hkv;
+  int bad = 0;
+  for (int unit = unit_begin; unit < unit_end; ++unit)
+    bad |= quest_select_unit(dtype, q, meta_min, meta_max, page_table, seq_lens, Hq, Hkv, D, P, max_pages, topk,
+                             sink_pages, unit, union_ids + (int64_t)unit * max_union, union_cnt + unit, max_union);
+  return bad;
+}
+
+/* Selection + attention for units [unit_begin, unit_end); callers run disjoint
+   ranges on several threads. */
 int oracle_quest_decode(int dtype, const void* q, const void* k_pool, const void* v_pool, const void* meta_min,
                         const void* meta_max, const int32_t* page_table, const int32_t* seq_lens, int B, int Hq,
                         int Hkv, int D, int P, int max_pages, int topk, int sink_pages, float scale, float* out,
@@ -86,52 +157,14 @@ int oracle_quest_decode(int dtype, const void* q, const void* k_pool, const void
   if (group * Hkv != Hq || D > 512 || topk < 1) return 1;
   if (unit_end > B * Hkv) unit_end = B * Hkv;
   int bad = 0;
-  /* units [unit_begin, unit_end) of the B*Hkv (batch, kv head) units; callers run
-     disjoint ranges on several threads */
   for (int unit = unit_begin; unit < unit_end; ++unit) {
     const int b = unit / Hkv, kh = unit % Hkv;
     const int len = seq_lens[b];
-    const int nb = (len + P - 1) / P;
-    const int kb = topk < nb ? topk : nb;
-    float qv[512], mn[512], mx[512], krow[512], vrow[512], acc[512];
-    float* ts = (float*)malloc(sizeof(float) * (size_t)(kb > 0 ? kb : 1));
-    int* ti = (int*)malloc(sizeof(int) * (size_t)(kb > 0 ? kb : 1));
-    uint8_t* in_union = (uint8_t*)calloc((size_t)(nb > 0 ? nb : 1), 1);
-    for (int g = 0; g < group && nb > 0; ++g) {
-      const int h = kh * group + g;
-      load_row(dtype, q, ((int64_t)b * Hq + h) * D, D, qv);
-      int n = 0;
-      for (int p = 0; p < nb; ++p) {
-        float s;
-        if (p == nb - 1 || p < sink_pages) {
-          s = INFINITY;
-        } else {
-          const int phys = page_table[(int64_t)b * max_pages + p];
-          const int64_t mo = ((int64_t)phys * Hkv + kh) * D;
-          load_row(dtype, meta_min, mo, D, mn);
-          load_row(dtype, meta_max, mo, D, mx);
-          s = 0.f;
-          for (int d = 0; d < D; ++d) {
-            const float a = qv[d] * mn[d], c = qv[d] * mx[d];
-            s += a > c ? a : c;
-          }
-        }
-        topk_push(s, p, ts, ti, &n, kb);
-      }
-      for (int i = 0; i < n; ++i) in_union[ti[i]] = 1;
-    }
-    int cnt = 0;
     int32_t* ul = union_ids + (int64_t)unit * max_union;
-    for (int p = 0; p < nb; ++p)
-      if (in_union[p]) {
-        if (cnt < max_union) ul[cnt] = p;
-        ++cnt;
-      }
-    if (cnt > max_union) {
-      bad |= 2;
-      cnt = max_union;
-    }
-    union_cnt[unit] = cnt;
+    bad |= quest_select_unit(dtype, q, meta_min, meta_max, page_table, seq_lens, Hq, Hkv, D, P, max_pages, topk,
+                             sink_pages, unit, ul, union_cnt + unit, max_union);
+    const int cnt = union_cnt[unit];
+    float qv[512], krow[512], vrow[512], acc[512];
     /* attention of each query head of the group over the union's rows */
     for (int g = 0; g < group; ++g) {
       const int h = kh * group + g;
@@ -160,9 +193,6 @@ int oracle_quest_decode(int dtype, const void* q, const void* k_pool, const void
       float* o = out + ((int64_t)b * Hq + h) * D;
       for (int d = 0; d < D; ++d) o[d] = l > 0.f ? acc[d] / l : 0.f;
     }
-    free(ts);
-    free(ti);
-    free(in_union);
   }
   return bad;
 }
