@@ -20,15 +20,11 @@ from __future__ import annotations
 
 import argparse
 import ctypes
-import csv
-import io
 import json
 import math
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import time
 from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
@@ -71,56 +67,62 @@ def profile_traffic(name: str):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+    """SM clock and clock-event (throttle) reasons polled through NVML every ~2 ms
+    while the timed region runs (the region can be far shorter than nvidia-smi's
+    200 ms sampling period)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap", 0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.file = None
+    def __init__(self, gpu_index: int, period_s: float = 0.002):
+        self.gpu, self.period = gpu_index, period_s
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = None
+        self._thread = None
+        self.error = None
 
     def __enter__(self):
-        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        import threading
+
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=self.file, stderr=subprocess.DEVNULL)
-        except OSError:
-            self.proc = None
+            import pynvml
+
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+        except Exception as exc:  # noqa: BLE001
+            self.error = f"nvml unavailable: {exc}"
+            return self
+        self._stop = threading.Event()
+
+        def poll():
+            while not self._stop.is_set():
+                try:
+                    self.samples.append(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                    bits = get_reasons(h)
+                    for bit, name in self.REASONS.items():
+                        if bits & bit:
+                            self.reasons.add(name)
+                except Exception:  # noqa: BLE001
+                    pass
+                time.sleep(self.period)
+
+        self._thread = threading.Thread(target=poll, daemon=True)
+        self._thread.start()
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
 
     def summary(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.file.flush()
-        rows = list(csv.reader(io.StringIO(Path(self.file.name).read_text())))
-        sm, smax, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            if len(r) < 9:
-                continue
-            try:
-                sm.append(float(r[1]))
-                smax = float(r[2])
-            except ValueError:
-                continue
-            for name, val in zip(names, r[5:9]):
-                if val.strip().lower() == "active":
-                    reasons.add(name)
-        os.unlink(self.file.name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "samples": len(sm),
-                "reasons": sorted(reasons)}
+        if self.error:
+            return {"sm_mhz": None, "sm_max_mhz": None, "samples": 0, "reasons": [self.error]}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "samples": len(self.samples), "reasons": sorted(self.reasons)}
 
 
 # ---------------------------------------------------------------------------------
@@ -438,8 +440,8 @@ def run_reference(args):
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
