@@ -197,6 +197,26 @@ int64_t linattn_sparse_attention_workspace(int64_t B, int64_t Hq, int64_t Tq, in
 int linattn_lse_combine(const float* o_parts, const float* lse_parts, int64_t S, int64_t rows, int64_t D,
                         void* out, int32_t out_dtype, float* lse_out, void* stream);
 
+/*
+ * linattn_sparse_attention without a workspace argument, for callers that cannot
+ * allocate device memory where they run attention (an engine that owns all of HBM
+ * through its own pool and forbids side allocations, or a latency-critical path
+ * that cannot take cudaMalloc's implicit device synchronisation).  No counterpart in
+ * the reference.  The split-KV scratch is a 64 MiB device array inside this library
+ * (linattn_sparse_attention_noalloc_limit() bytes), held by every GPU that loads it
+ * until exit; a call whose scratch need (linattn_sparse_attention_workspace) exceeds
+ * it fails with LINATTN_EINVAL.  The first call on a device resolves the array's
+ * device address (cudaGetSymbolAddress) with that device current; make that first
+ * call before any stream capture.  All calls share the array: calls that overlap on
+ * the GPU race.  Allocates nothing (no cudaMalloc / cudaFree).
+ */
+int linattn_sparse_attention_noalloc(const void* q, int32_t q_dtype, int64_t B, int64_t Hq, int64_t Tq,
+                                     const int64_t* q_strides, const linattn_kv_t* kv, const linattn_lists_t* lists,
+                                     int32_t causal, int64_t offset, float scale, void* out,
+                                     const int64_t* out_strides, float* lse_out, int32_t n_splits, int32_t* status,
+                                     void* stream);
+int64_t linattn_sparse_attention_noalloc_limit(void);
+
 #ifdef __cplusplus
 }
 #endif

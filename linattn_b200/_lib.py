@@ -85,6 +85,11 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.linattn_sparse_attention_workspace.argtypes = [c_i64, c_i64, c_i64, c_i64, c_i32]
     lib.linattn_sparse_attention_workspace.restype = c_i64
     lib.linattn_lse_combine.argtypes = [c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_i32, c_vp, c_vp]
+    lib.linattn_sparse_attention_noalloc.argtypes = [c_vp, c_i32, c_i64, c_i64, c_i64, P(c_i64), P(KV), P(Lists),
+                                                     c_i32, c_i64, ctypes.c_float, c_vp, P(c_i64), c_vp, c_i32,
+                                                     c_vp, c_vp]
+    lib.linattn_sparse_attention_noalloc.restype = ctypes.c_int
+    lib.linattn_sparse_attention_noalloc_limit.restype = c_i64
     for name in ("linattn_page_bounds", "linattn_paged_page_bounds", "linattn_quest_scores", "linattn_page_topk",
                  "linattn_sparse_attention", "linattn_lse_combine"):
         getattr(lib, name).restype = ctypes.c_int

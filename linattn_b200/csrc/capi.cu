@@ -18,8 +18,17 @@ int device_index() {
 using namespace linattn;
 
 namespace {
-
 thread_local std::string g_err;
+}  // namespace
+
+namespace linattn {
+int set_error(int code, const char* msg) {
+  g_err = msg;
+  return code;
+}
+}  // namespace linattn
+
+namespace {
 
 int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
 int fail(int code, const char* fmt, ...) {

@@ -23,6 +23,8 @@ struct TopkParams {
 };
 
 int device_index();
+// Record `msg` as linattn_last_error() and return `code` (host side).
+int set_error(int code, const char* msg);
 
 cudaError_t launch_page_bounds(const void* k, int dtype, int64_t B, int64_t H, int64_t T_, int64_t D,
                                const int64_t* s, int64_t P, void* mins, void* maxs, cudaStream_t stream);
