@@ -47,6 +47,9 @@ enum { LINATTN_DEV_BAD_ID = 1, LINATTN_DEV_TIMEOUT = 2, LINATTN_DEV_OVERFLOW = 4
  * [N_phys, H_kv, P, D] is stride_page = H_kv*P*D, stride_head = P*D.
  * Rows at positions >= seq_lens[b] (or seq_len) are never read.
  * fp8: k_scale/v_scale hold one fp32 scale per (phys page, kv head).
+ * The 16-bit tensor-core path reads K/V through TMA tensor maps over the 2-D view
+ * [total_rows, head_dim] of each allocation, so every stride must be a multiple of
+ * head_dim.
  */
 typedef struct {
   const void* k;
@@ -67,6 +70,8 @@ typedef struct {
   int32_t page_size;
   int32_t head_dim;
   int32_t n_kv_heads;
+  int64_t total_rows; /* D-element rows addressable from k (and from v); 0 = derive from the pool
+                         (page table set) or from B * stride_b / head_dim */
 } linattn_kv_t;
 
 /*

@@ -45,7 +45,14 @@ class KV(ctypes.Structure):
         ("k_scale", c_vp), ("v_scale", c_vp), ("scale_stride_page", c_i64), ("scale_stride_head", c_i64),
         ("seq_lens", c_vp), ("seq_len", c_i64),
         ("dtype", c_i32), ("page_size", c_i32), ("head_dim", c_i32), ("n_kv_heads", c_i32),
+        ("total_rows", c_i64),
     ]
+
+
+def rows_addressable(t: torch.Tensor, head_dim: int) -> int:
+    """D-element rows reachable from ``t.data_ptr()`` to the end of its storage."""
+    nbytes = t.untyped_storage().nbytes() - t.storage_offset() * t.element_size()
+    return nbytes // (head_dim * t.element_size())
 
 
 class Meta(ctypes.Structure):

@@ -21,13 +21,47 @@ import torch
 
 from linattn_b200 import _lib as L
 
-__all__ = ["block_sparse_attention", "sparse_attention", "kv_contiguous", "lists_desc", "choose_splits"]
-
-_TILE_ROWS = {1: 64, 2: 64, 4: 64}
-
+__all__ = ["block_sparse_attention", "sparse_attention", "kv_contiguous", "lists_desc", "plan_splits",
+           "uses_tensor_cores"]
 
 def tile_rows(elem_bytes: int, head_dim: int) -> int:
+    """Rows per tile of the CUDA-core kernel (fp32 / fp8 / mixed dtypes / other D)."""
     return min(64, 16384 // (head_dim * elem_bytes))
+
+
+def uses_tensor_cores(kv_dtype: int, q_dtype: int, head_dim: int) -> bool:
+    """The C ABI's dispatch rule: 16-bit KV with q of the same dtype and D in {64, 128}
+    run the tensor-core kernel (persistent grid, 2048/D rows per warp tile)."""
+    return kv_dtype in (L.F16, L.BF16) and q_dtype == kv_dtype and head_dim in (64, 128)
+
+
+def plan_splits(b: int, hq: int, tq: int, d: int, kv_dtype: int, q_dtype: int, list_heads: int, max_len: int,
+                page_size: int, device: torch.device) -> int:
+    """Split-KV factor for a call.
+
+    Tensor-core path: about 2 work items per resident warp (148 SMs x 8 warps), each
+    item keeping at least 4 tiles (and at most 128 list entries).  CUDA-core path: about 4 CTAs per SM, each split
+    keeping at least 2 tiles."""
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    g_total = hq // list_heads
+    if uses_tensor_cores(kv_dtype, q_dtype, d):
+        tr = 2048 // d
+        units = b * list_heads * tq * ((g_total + 7) // 8)
+        tiles = max(1, (max_len * page_size + tr - 1) // tr) if page_size <= tr else max_len * -(-page_size // tr)
+        target, min_tiles = 16 * sms, 4
+    else:
+        eb = {L.F32: 4, L.F16: 2, L.BF16: 2, L.FP8E4M3: 1}[kv_dtype]
+        tr = tile_rows(eb, d)
+        g_t = 1
+        while g_t < g_total and g_t < 8:
+            g_t <<= 1
+        units = b * list_heads * tq * ((g_total + g_t - 1) // g_t)
+        tiles = max(1, (max_len * page_size + tr - 1) // tr)
+        target, min_tiles = 4 * sms, 2
+    floor = -(-max_len // 128) if uses_tensor_cores(kv_dtype, q_dtype, d) else 1  # <= 128 entries per split
+    if units >= target or tiles < 2 * min_tiles:
+        return max(1, floor)
+    return int(max(floor, min(math.ceil(target / max(units, 1)), tiles // min_tiles, 64)))
 
 
 def kv_contiguous(k: torch.Tensor, v: torch.Tensor, block_size: int) -> L.KV:
@@ -38,8 +72,9 @@ def kv_contiguous(k: torch.Tensor, v: torch.Tensor, block_size: int) -> L.KV:
     b, h, t, d = k.shape
     if k.stride(3) != 1 or k.stride(2) != d:
         raise ValueError("k/v rows must be contiguous (stride (.., .., D, 1))")
+    rows = min(L.rows_addressable(k, d), L.rows_addressable(v, d))
     return L.KV(k.data_ptr(), v.data_ptr(), k.stride(0), block_size * d, k.stride(1), None, 0, 0, None, None, 0, 0,
-                None, t, L.dtype_code(k), block_size, d, h)
+                None, t, L.dtype_code(k), block_size, d, h, rows)
 
 
 def lists_desc(ids: torch.Tensor, n_heads: int, counts: Optional[torch.Tensor] = None) -> L.Lists:
@@ -60,22 +95,10 @@ def lists_desc(ids: torch.Tensor, n_heads: int, counts: Optional[torch.Tensor] =
     return L.Lists(ids.data_ptr(), L.dtype_code(ids), n_heads, sb, sh, st, ids.shape[-1], L.ptr(counts), *cs)
 
 
-def choose_splits(units: int, tiles_per_unit: int, device: torch.device) -> int:
-    """Split-KV factor: enough CTAs for ~2 waves of 2 CTAs per SM, each split keeping
-    at least 2 tiles of work."""
-    sms = torch.cuda.get_device_properties(device).multi_processor_count
-    target = 4 * sms
-    if units >= target or tiles_per_unit <= 2:
-        return 1
-    s = math.ceil(target / max(units, 1))
-    return int(max(1, min(s, tiles_per_unit // 2, 64)))
-
-
 def sparse_attention(q: torch.Tensor, kv: L.KV, lists: L.Lists, *, causal: bool = False, offset: int = 0,
                      scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
                      lse_out: Optional[torch.Tensor] = None, n_splits: Optional[int] = None,
-                     workspace: Optional[torch.Tensor] = None, tiles_per_unit: Optional[int] = None,
-                     _keepalive=()) -> torch.Tensor:
+                     workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Attention of ``q (B,H_q,T_q,D)`` over the listed pages of ``kv``."""
     dev = L.require_cuda(q)
     b, hq, tq, d = q.shape
@@ -84,26 +107,17 @@ def sparse_attention(q: torch.Tensor, kv: L.KV, lists: L.Lists, *, causal: bool 
     if out is None:
         out = torch.empty_like(q, memory_format=torch.contiguous_format)
     scale = (1.0 / math.sqrt(d)) if scale is None else float(scale)
-    g_total = hq // lists.n_heads
-    g_t = 1
-    while g_t < g_total and g_t < 8:
-        g_t <<= 1
-    n_hc = (g_total + g_t - 1) // g_t
-    units = b * lists.n_heads * tq * n_hc
     if n_splits is None:
-        if tiles_per_unit is None:
-            eb = {L.F32: 4, L.F16: 2, L.BF16: 2, L.FP8E4M3: 1}[kv.dtype]
-            tr = tile_rows(eb, d)
-            tiles_per_unit = max(1, (lists.max_len * kv.page_size + tr - 1) // tr)
-        n_splits = choose_splits(units, tiles_per_unit, dev)
+        n_splits = plan_splits(b, hq, tq, d, kv.dtype, L.dtype_code(q), lists.n_heads, lists.max_len, kv.page_size,
+                               dev)
     need = L.lib().linattn_sparse_attention_workspace(b, hq, tq, d, n_splits)
-    if n_splits > 1 and (workspace is None or workspace.numel() * workspace.element_size() < need):
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
         workspace = torch.empty((need + 3) // 4, dtype=torch.float32, device=dev)
     status = L.status_word(dev)
     L.check(L.lib().linattn_sparse_attention(
         q.data_ptr(), L.dtype_code(q), b, hq, tq, L.strides4(q), kv, lists, int(causal), offset, scale,
-        out.data_ptr(), L.strides4(out), L.ptr(lse_out), n_splits, L.ptr(workspace) if n_splits > 1 else None,
-        need, status.data_ptr(), L.stream_of(q)))
+        out.data_ptr(), L.strides4(out), L.ptr(lse_out), n_splits, workspace.data_ptr(), need,
+        status.data_ptr(), L.stream_of(q)))
     if L.strict():
         L.check_status(dev)
     return out

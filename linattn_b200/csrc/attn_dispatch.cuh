@@ -2,6 +2,7 @@
 // with ATTN_T set, so the template instances compile in parallel.
 #pragma once
 #include "launchers.cuh"
+#include "sparse_attention_mma.cuh"
 
 namespace linattn {
 
@@ -42,6 +43,39 @@ static cudaError_t launch_dg(const AttnParams& p, int D, int G, unsigned grid, c
     case 64: return launch_g<T, 64>(p, G, grid, stream);
     case 128: return launch_g<T, 128>(p, G, grid, stream);
     case 256: return launch_g<T, 256>(p, G, grid, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+int sm_count();
+
+template <typename T, int D>
+static cudaError_t launch_mma_d(const AttnParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv, int box_rows,
+                                int* counter, int64_t n_items, cudaStream_t stream) {
+  using S = MmaShape<D>;
+  static bool configured[64] = {};
+  const int dev = device_index();
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(sparse_attention_mma_kernel<T, D>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(S::SMEM_BYTES));
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  const int64_t want = (n_items + S::NW - 1) / S::NW;
+  const int grid = static_cast<int>(lmax(1, lmin(sm_count(), want)));
+  sparse_attention_mma_kernel<T, D><<<grid, 32 * S::NW, S::SMEM_BYTES, stream>>>(p, tmk, tmv, box_rows, counter,
+                                                                             n_items);
+  return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t launch_mma(const AttnParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv, int box_rows, int D,
+                              int* counter, int64_t n_items, cudaStream_t stream) {
+  switch (D) {
+    case 64: return launch_mma_d<T, 64>(p, tmk, tmv, box_rows, counter, n_items, stream);
+    case 128: return launch_mma_d<T, 128>(p, tmk, tmv, box_rows, counter, n_items, stream);
     default: return cudaErrorInvalidValue;
   }
 }

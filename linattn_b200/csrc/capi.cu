@@ -3,7 +3,11 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
 
 #include "launchers.cuh"
 
@@ -12,6 +16,17 @@ int device_index() {
   int d = -1;
   if (cudaGetDevice(&d) != cudaSuccess) return -1;
   return d;
+}
+int sm_count() {
+  static int cache[64] = {};
+  const int d = device_index();
+  if (d < 0 || d >= 64) return 1;
+  if (cache[d] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d) != cudaSuccess || n <= 0) n = 1;
+    cache[d] = n;
+  }
+  return cache[d];
 }
 }  // namespace linattn
 
@@ -93,6 +108,65 @@ int check_kv(const linattn_kv_t* kv) {
     return fail(LINATTN_EINVAL, "fp8 KV needs k_scale and v_scale");
   if (!kv->seq_lens && kv->seq_len < 0) return fail(LINATTN_EINVAL, "seq_len must be >= 0");
   return LINATTN_OK;
+}
+
+// ---- TMA tensor maps over the [rows, D] view of a 16-bit K or V pool --------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+struct TmapEntry {
+  const void* base;
+  int64_t rows;
+  int d, dtype, box_rows;
+  bool used;
+  CUtensorMap map;
+};
+std::mutex g_tmap_mu;
+TmapEntry g_tmaps[32];
+int g_tmap_next = 0;
+
+// 2-D map {D, rows} with 64 x box_rows boxes and 128-byte swizzle; a map only encodes
+// these values, so a cached one is valid whenever they match.
+bool kv_tensor_map(CUtensorMap* out, const void* base, int64_t rows, int d, int dtype, int box_rows) {
+  std::lock_guard<std::mutex> lock(g_tmap_mu);
+  for (const TmapEntry& e : g_tmaps)
+    if (e.used && e.base == base && e.rows == rows && e.d == d && e.dtype == dtype && e.box_rows == box_rows) {
+      *out = e.map;
+      return true;
+    }
+  PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(d) * 2};
+  const cuuint32_t box[2] = {64u, static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t elem_strides[2] = {1u, 1u};
+  TmapEntry& e = g_tmaps[g_tmap_next];
+  const CUresult r = fn(&e.map, dtype == LINATTN_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                        2, const_cast<void*>(base), dims, strides, box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    e.used = false;
+    return false;
+  }
+  e.base = base;
+  e.rows = rows;
+  e.d = d;
+  e.dtype = dtype;
+  e.box_rows = box_rows;
+  e.used = true;
+  *out = e.map;
+  g_tmap_next = (g_tmap_next + 1) % 32;
+  return true;
 }
 
 }  // namespace
@@ -177,9 +251,13 @@ int linattn_page_topk(const float* scores, int64_t B, int64_t Hq, int64_t Tq, in
   return cuda_status(launch_page_topk(p, static_cast<cudaStream_t>(stream)), "page_topk");
 }
 
+// workspace: [256-byte header: the work counter of the tensor-core path]
+//            [n_splits > 1: o partials fp32 (S, rows, D)][lse partials fp32 (S, rows)]
+static constexpr int64_t kWsHeader = 256;
+
 int64_t linattn_sparse_attention_workspace(int64_t B, int64_t Hq, int64_t Tq, int64_t D, int32_t n_splits) {
-  if (n_splits <= 1) return 0;
-  return static_cast<int64_t>(n_splits) * B * Hq * Tq * (D + 1) * static_cast<int64_t>(sizeof(float));
+  if (n_splits <= 1) return kWsHeader;
+  return kWsHeader + static_cast<int64_t>(n_splits) * B * Hq * Tq * (D + 1) * static_cast<int64_t>(sizeof(float));
 }
 
 int linattn_sparse_attention(const void* q, int32_t q_dtype, int64_t B, int64_t Hq, int64_t Tq,
@@ -216,32 +294,66 @@ int linattn_sparse_attention(const void* q, int32_t q_dtype, int64_t B, int64_t 
   p.scale_log2 = scale * 1.4426950408889634f;
   p.out = out; p.lse_out = lse_out; p.n_splits = n_splits; p.status = status;
   const int64_t g_total = Hq / lists->n_heads;
+  // tensor-core path: 16-bit KV, q of the same dtype, D in {64, 128}, at most 128 list
+  // entries per split (the producer's per-item table), and K/V describable as TMA
+  // tensor maps over their [rows, D] views: strides multiples of D, pages either at
+  // least one 2048/D-row tile or a power of two >= 8 rows (box starts stay 1024-byte
+  // aligned for the 128-byte swizzle), rows below 2^31 (32-bit coordinates).
+  bool mma_path = (kv->dtype == LINATTN_BF16 || kv->dtype == LINATTN_F16) && q_dtype == kv->dtype &&
+                  (D == 64 || D == 128) && (lists->max_len + n_splits - 1) / n_splits <= 128;
+  const int tile_rows_mma = 2048 / D;
+  const int64_t P = kv->page_size;
+  const int box_rows = static_cast<int>(P >= tile_rows_mma ? tile_rows_mma : P);
+  mma_path = mma_path && (P >= tile_rows_mma || (P >= 8 && (P & (P - 1)) == 0)) && kv->stride_b % D == 0 &&
+             kv->stride_page % D == 0 && kv->stride_head % D == 0;
+  int64_t total_rows = kv->total_rows;
+  if (total_rows <= 0) {
+    if (kv->page_table)
+      total_rows = ((kv->num_phys_pages - 1) * kv->stride_page + (kv->n_kv_heads - 1) * kv->stride_head) / D + P;
+    else if (kv->stride_b > 0)
+      total_rows = B * kv->stride_b / D;
+  }
+  mma_path = mma_path && total_rows > 0 && total_rows < (1ll << 31) - 4096;
+  CUtensorMap tmk, tmv;
+  if (mma_path)
+    mma_path = kv_tensor_map(&tmk, kv->k, total_rows, D, kv->dtype, box_rows) &&
+               kv_tensor_map(&tmv, kv->v, total_rows, D, kv->dtype, box_rows);
   int G = 1;
   while (G < g_total && G < 8) G <<= 1;
+  const int head_chunk = mma_path ? 8 : G;
   p.heads_per_list = static_cast<int>(g_total);
-  p.n_head_chunks = static_cast<int>((g_total + G - 1) / G);
+  p.n_head_chunks = static_cast<int>((g_total + head_chunk - 1) / head_chunk);
+  const int64_t need = linattn_sparse_attention_workspace(B, Hq, Tq, D, n_splits);
+  if (!workspace || workspace_bytes < need)
+    return fail(LINATTN_EINVAL, "sparse_attention: workspace of %lld bytes needed", (long long)need);
+  if (!aligned(workspace, 256)) return fail(LINATTN_EINVAL, "sparse_attention: workspace must be 256-byte aligned");
+  int* counter = reinterpret_cast<int*>(workspace);
   p.ws_o = nullptr;
   p.ws_lse = nullptr;
   if (n_splits > 1) {
-    const int64_t need = linattn_sparse_attention_workspace(B, Hq, Tq, D, n_splits);
-    if (!workspace || workspace_bytes < need)
-      return fail(LINATTN_EINVAL, "sparse_attention: workspace of %lld bytes needed", (long long)need);
-    if (!aligned(workspace, 16)) return fail(LINATTN_EINVAL, "sparse_attention: workspace must be 16-byte aligned");
-    p.ws_o = workspace;
-    p.ws_lse = workspace + static_cast<int64_t>(n_splits) * rows * D;
+    p.ws_o = workspace + kWsHeader / 4;
+    p.ws_lse = p.ws_o + static_cast<int64_t>(n_splits) * rows * D;
   }
   const int64_t units = B * static_cast<int64_t>(lists->n_heads) * Tq;
   const int64_t blocks = units * p.n_head_chunks * n_splits;
-  if (blocks > 0x7fffffffLL) return fail(LINATTN_EUNSUPPORTED, "sparse_attention: grid too large");
-  const unsigned grid = static_cast<unsigned>(blocks);
+  if (blocks > 0x7fffffffLL) return fail(LINATTN_EUNSUPPORTED, "sparse_attention: too many work items");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e;
-  switch (kv->dtype) {
-    case LINATTN_F32: e = launch_sparse_attention_f32(p, D, G, grid, st); break;
-    case LINATTN_F16: e = launch_sparse_attention_f16(p, D, G, grid, st); break;
-    case LINATTN_BF16: e = launch_sparse_attention_bf16(p, D, G, grid, st); break;
-    case LINATTN_FP8E4M3: e = launch_sparse_attention_fp8(p, D, G, grid, st); break;
-    default: return fail(LINATTN_EUNSUPPORTED, "sparse_attention: kv dtype");
+  if (mma_path) {
+    e = cudaMemsetAsync(counter, 0, sizeof(int), st);
+    if (e == cudaSuccess)
+      e = kv->dtype == LINATTN_BF16
+              ? launch_sparse_attention_mma_bf16(p, tmk, tmv, box_rows, D, counter, blocks, st)
+              : launch_sparse_attention_mma_f16(p, tmk, tmv, box_rows, D, counter, blocks, st);
+  } else {
+    const unsigned grid = static_cast<unsigned>(blocks);
+    switch (kv->dtype) {
+      case LINATTN_F32: e = launch_sparse_attention_f32(p, D, G, grid, st); break;
+      case LINATTN_F16: e = launch_sparse_attention_f16(p, D, G, grid, st); break;
+      case LINATTN_BF16: e = launch_sparse_attention_bf16(p, D, G, grid, st); break;
+      case LINATTN_FP8E4M3: e = launch_sparse_attention_fp8(p, D, G, grid, st); break;
+      default: return fail(LINATTN_EUNSUPPORTED, "sparse_attention: kv dtype");
+    }
   }
   rc = cuda_status(e, "sparse_attention");
   if (rc || n_splits == 1) return rc;

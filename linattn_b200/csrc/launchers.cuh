@@ -1,5 +1,7 @@
 // Host-side launcher declarations shared by the kernel units and the C ABI.
 #pragma once
+#include <cuda.h>
+
 #include "common.cuh"
 #include "sparse_attention.cuh"
 
@@ -44,6 +46,11 @@ cudaError_t launch_sparse_attention_f32(const AttnParams& p, int D, int G, unsig
 cudaError_t launch_sparse_attention_f16(const AttnParams& p, int D, int G, unsigned grid, cudaStream_t stream);
 cudaError_t launch_sparse_attention_bf16(const AttnParams& p, int D, int G, unsigned grid, cudaStream_t stream);
 cudaError_t launch_sparse_attention_fp8(const AttnParams& p, int D, int G, unsigned grid, cudaStream_t stream);
+cudaError_t launch_sparse_attention_mma_bf16(const AttnParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv,
+                                            int box_rows, int D, int* counter, int64_t n_items, cudaStream_t stream);
+cudaError_t launch_sparse_attention_mma_f16(const AttnParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv,
+                                           int box_rows, int D, int* counter, int64_t n_items, cudaStream_t stream);
+int sm_count();
 int tile_rows_f32(int D);
 int tile_rows_f16(int D);
 int tile_rows_bf16(int D);

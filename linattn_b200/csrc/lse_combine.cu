@@ -23,7 +23,8 @@ __global__ void __launch_bounds__(256) lse_combine_kernel(const float* __restric
   if (L != -INFINITY) {
     for (int64_t s = 0; s < S; ++s) {
       const float ls = lse_parts[s * rows + row];
-      const float w = ls == -INFINITY ? 0.f : __expf(ls - L);
+      if (ls == -INFINITY) continue;  // empty part: its o is not read (it may be unwritten)
+      const float w = __expf(ls - L);
       W += w;
       const float* op = o_parts + (s * rows + row) * D;
 #pragma unroll

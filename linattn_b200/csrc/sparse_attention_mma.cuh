@@ -1,0 +1,514 @@
+// Sparse (paged, block-list) attention on the tensor cores, for 16-bit KV.
+//
+// Work: the (batch, list head, query, head chunk) units of linattn_sparse_attention,
+// each cut into `n_splits` equal slices of its page list ("items").  A persistent
+// grid (one CTA of NW warps per SM) hands items out through an atomic counter, so
+// ragged lists (GQA unions of different sizes) leave no tail.
+//
+// Every warp is self-contained (no inter-warp signalling after set-up):
+// * it grabs items and resolves each item's list entries once (list id -> page
+//   table -> physical page -> row of the [rows, D] view of the pool) into one of two
+//   shared-memory table slots, one item ahead and while its ring is full, so the
+//   global-load latency overlaps the copies in flight;
+// * it keeps its STG-stage ring of TRW-row tiles full from the tables: per tile,
+//   one lane per row decides whether the row is read (position < the causal or
+//   sequence limit), lane 0 arms the stage's mbarrier with the byte count, and the
+//   first lane of each page segment issues TMA tiled loads through tensor maps over
+//   the K and V pools (64-column x box_rows boxes, 128-byte swizzle, no multicast);
+// * it computes with the heads as the narrow dimension: S^T = K Q^T and
+//   O^T += V^T P^T with mma.sync m16n8k16, tokens / channels as the 16-row M side and
+//   up to 8 query heads of the GQA group as N = 8.  K and V^T fragments come from
+//   ldmatrix (plain / .trans) on the swizzled tiles (the swizzle XORs each 16-byte
+//   chunk index with the row mod 8, so every phase hits eight bank groups); P^T moves
+//   from the accumulator layout to the B-operand layout with movmatrix.trans.  The
+//   online softmax runs per head (column) in the log2 domain; P is split into two
+//   16-bit parts (hi + lo) so its rounding stays near fp32 precision, and the running
+//   sum uses the unrounded fp32 P.
+// Every wait is bounded (a give-up reports LINATTN_DEV_TIMEOUT and unwinds after
+// waiting, bounded, for the copies in flight).
+#pragma once
+
+#include <cuda.h>
+
+#include "sparse_attention.cuh"
+
+namespace linattn {
+
+template <typename T> struct MmaOp;
+template <> struct MmaOp<__nv_bfloat16> {
+  __device__ static void mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+  __device__ static uint32_t pack(float lo, float hi) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+  }
+  __device__ static float2 unpack(uint32_t v) {
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v));
+  }
+};
+template <> struct MmaOp<__half> {
+  __device__ static void mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+  __device__ static uint32_t pack(float lo, float hi) {
+    const __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+  }
+  __device__ static float2 unpack(uint32_t v) { return __half22float2(*reinterpret_cast<const __half2*>(&v)); }
+};
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+template <int D>
+struct MmaShape {
+  static constexpr int TRW = 2048 / D;            // tile rows (D=128: 16, D=64: 32)
+  static constexpr int NHALF = D / 64;            // 64-channel (128-byte) column blocks
+  static constexpr int HALF_BYTES = TRW * 128;    // one column block of a tile
+  static constexpr int TILE_BYTES = NHALF * HALF_BYTES;  // one of K or V (4 KiB)
+  static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
+  static constexpr int STG = 3;                   // stages per warp
+  static constexpr int NW = 8;                    // warps per CTA
+  static constexpr int ITEM_MAX = 128;            // list entries per item (host guarantees)
+  static constexpr size_t RING_BYTES = static_cast<size_t>(NW) * STG * STAGE_BYTES;
+  static constexpr size_t TABLE_BYTES = static_cast<size_t>(NW) * 2 * ITEM_MAX * 8;
+  static constexpr size_t SMEM_BYTES = 1024 + RING_BYTES + TABLE_BYTES;  // + alignment slack
+  static constexpr int MT = TRW / 16;             // token 16-blocks per tile
+  static constexpr int KS = D / 16;               // channel 16-blocks
+};
+
+// An item as resolved by its warp (one of two slots per warp).
+struct MmaItem {
+  int32_t b, t, h0, n_heads, split, n, n_tiles, limit;
+};
+
+struct MmaStage {
+  uint32_t rows;    // valid-row mask of the tile
+  uint32_t loaded;  // rows written by this tile's boxes
+  int32_t b, t, h0, n_heads, split;
+  int32_t first, last;
+};
+
+// Swizzled byte offset of 16-byte chunk `chunk` (0 .. D/8-1) of tile row `row`.
+template <int D>
+__device__ __forceinline__ uint32_t swz(int row, int chunk) {
+  return static_cast<uint32_t>((chunk >> 3) * MmaShape<D>::HALF_BYTES + row * 128 + (((chunk & 7) ^ (row & 7)) << 4));
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;\n" : "=r"(y) : "r"(x));
+  return y;
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(32 * MmaShape<D>::NW, 1)
+    sparse_attention_mma_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmk,
+                                const __grid_constant__ CUtensorMap tmv, int box_rows, int* __restrict__ counter,
+                                int64_t n_items) {
+  using S = MmaShape<D>;
+  using M = MmaOp<T>;
+  constexpr int TRW = S::TRW, STG = S::STG;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  // 128-byte swizzled TMA destinations want 1024-byte alignment
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  __shared__ __align__(8) uint64_t full_bar[S::NW][STG];
+  __shared__ MmaStage st[S::NW][STG];
+  __shared__ MmaItem items[S::NW][2];
+
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  uint8_t* ring = smem + static_cast<size_t>(w) * STG * S::STAGE_BYTES;
+  int2* tables = reinterpret_cast<int2*>(smem + S::RING_BYTES) + w * 2 * S::ITEM_MAX;
+  if (lane == 0) {
+    for (int s = 0; s < STG; ++s) mbar_init(&full_bar[w][s], 1);
+    mbar_fence_init();
+  }
+  // rows never copied must hold finite values
+  for (int i = lane; i < STG * S::STAGE_BYTES / 16; i += 32)
+    reinterpret_cast<uint4*>(ring)[i] = make_uint4(0u, 0u, 0u, 0u);
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  __syncwarp();
+
+  const int64_t S_ = p.n_splits;
+  const int64_t P = p.kv.page_size;
+  const int64_t heads_per_kv = p.Hq / p.kv.n_kv_heads;
+  const int64_t rows_total = p.B * p.Hq * p.Tq;
+  const bool small_pages = P <= TRW;
+  const int64_t PPT = small_pages ? TRW / P : 1;
+  const int64_t segs = small_pages ? 1 : (P + TRW - 1) / TRW;
+
+  // ---- item resolution: grab items until one has tiles (writing empty ones)
+  int res_count = 0;           // items resolved into slots so far
+  bool exhausted = false;      // the counter ran past n_items
+  auto resolve = [&]() {
+    const int k = res_count & 1;
+    while (true) {
+      int v = 0;
+      if (lane == 0) v = atomicAdd(counter, 1);
+      const int64_t item = static_cast<int64_t>(__shfl_sync(0xffffffffu, v, 0));
+      if (item >= n_items) {
+        exhausted = true;
+        return;
+      }
+      int64_t x = item;
+      const int split = static_cast<int>(x % S_);
+      x /= S_;
+      const int hc = static_cast<int>(x % p.n_head_chunks);
+      const int64_t unit = x / p.n_head_chunks;
+      const int64_t t = unit % p.Tq;
+      const int64_t lh = (unit / p.Tq) % p.lists.n_heads;
+      const int64_t b = unit / (p.Tq * p.lists.n_heads);
+      const int64_t h0 = lh * p.heads_per_list + hc * 8;
+      const int nh = static_cast<int>(lmin(8, p.heads_per_list - hc * 8));
+      const int64_t lbase = b * p.lists.stride_b + lh * p.lists.stride_h + t * p.lists.stride_t;
+      int64_t len = p.lists.max_len;
+      if (p.lists.counts)
+        len = lmin(len, p.lists.counts[b * p.lists.cstride_b + lh * p.lists.cstride_h + t * p.lists.cstride_t]);
+      const int64_t per = (len + S_ - 1) / S_;
+      const int64_t j0 = lmin(len, split * per);
+      const int64_t n = lmin(lmin(len, j0 + per) - j0, S::ITEM_MAX);
+      const int64_t ntiles = small_pages ? (n + PPT - 1) / PPT : n * segs;
+      if (ntiles == 0) {
+        // empty item: (o, lse) = (0, -inf)
+        for (int g = 0; g < nh; ++g) {
+          const int64_t h = h0 + g;
+          const int64_t row = (b * p.Hq + h) * p.Tq + t;
+          if (p.n_splits == 1) {
+            for (int cc = lane; cc < D; cc += 32)
+              store_any(p.out, b * p.os[0] + h * p.os[1] + t * p.os[2] + cc * p.os[3], p.q_dtype, 0.f);
+            if (p.lse_out && lane == 0) p.lse_out[row] = -INFINITY;
+          } else if (lane == 0) {
+            p.ws_lse[static_cast<int64_t>(split) * rows_total + row] = -INFINITY;
+          }
+        }
+        continue;
+      }
+      const int64_t len_b = p.kv.seq_lens ? static_cast<int64_t>(p.kv.seq_lens[b]) : p.kv.seq_len;
+      const int64_t kvh = h0 / heads_per_kv;
+      int2* table = tables + k * S::ITEM_MAX;
+      for (int64_t e = lane; e < n; e += 32) {
+        const int64_t id = p.lists.ids_dtype == LINATTN_I64
+                               ? static_cast<const int64_t*>(p.lists.ids)[lbase + j0 + e]
+                               : static_cast<int64_t>(static_cast<const int32_t*>(p.lists.ids)[lbase + j0 + e]);
+        int rowpos = -1, y0 = 0;
+        if (id >= 0 && id * P < len_b) {
+          int64_t ph = id;
+          if (p.kv.page_table) {
+            ph = id < p.kv.page_table_stride ? p.kv.page_table[b * p.kv.page_table_stride + id] : -1;
+            if (ph < 0 || ph >= p.kv.num_phys_pages) {
+              report(p.status, LINATTN_DEV_BAD_ID);
+              ph = -1;
+            }
+          }
+          if (ph >= 0) {
+            rowpos = static_cast<int>(id * P);
+            // first row of this (page, kv head) in the [rows, D] view of the pool
+            y0 = static_cast<int>((b * p.kv.stride_b + ph * p.kv.stride_page + kvh * p.kv.stride_head) / D);
+          }
+        }
+        table[e] = make_int2(rowpos, y0);
+      }
+      if (lane == 0) {
+        MmaItem& d = items[w][k];
+        d.b = static_cast<int32_t>(b);
+        d.t = static_cast<int32_t>(t);
+        d.h0 = static_cast<int32_t>(h0);
+        d.n_heads = nh;
+        d.split = split;
+        d.n = static_cast<int32_t>(n);
+        d.n_tiles = static_cast<int32_t>(ntiles);
+        d.limit = static_cast<int32_t>(p.causal ? lmin(len_b, p.offset + t + 1) : len_b);
+      }
+      __syncwarp();
+      ++res_count;
+      return;
+    }
+  };
+
+  // ---- production: item pi of the resolved sequence, tile ptile of it
+  int pi = 0, ptile = 0;
+  int64_t produced = 0;
+  bool pending = false;  // a slot was freed: resolve the next item when the ring is full
+  auto issue = [&]() -> bool {
+    while (true) {
+      if (pi >= res_count) {
+        if (exhausted) return false;
+        resolve();
+        continue;
+      }
+      if (ptile < items[w][pi & 1].n_tiles) break;
+      ++pi;  // the slot of item pi-1 is free again
+      ptile = 0;
+      if (!exhausted && res_count == pi + 1) pending = true;
+    }
+    const MmaItem& it = items[w][pi & 1];
+    const int2* table = tables + (pi & 1) * S::ITEM_MAX;
+    const int s = static_cast<int>(produced % STG);
+    uint8_t* kdst = ring + static_cast<size_t>(s) * S::STAGE_BYTES;
+    uint8_t* vdst = kdst + S::TILE_BYTES;
+    const int k = ptile;
+    const int r = lane;
+    int64_t e, rp;
+    if (small_pages) {
+      e = k * PPT + r / P;
+      rp = r % P;
+    } else {
+      e = k / segs;
+      rp = (k % segs) * TRW + r;
+    }
+    bool valid = false;
+    int y = 0;
+    if (r < TRW && (small_pages ? r / P < PPT : true) && e < it.n && rp < P) {
+      const int2 ent = table[e];
+      valid = ent.x >= 0 && ent.x + rp < it.limit;
+      y = ent.y + static_cast<int>(rp);
+    }
+    const uint32_t mask = __ballot_sync(0xffffffffu, valid);
+    const uint32_t box_mask = box_rows >= 32 ? 0xffffffffu : ((1u << box_rows) - 1u);
+    int n_boxes = 0;
+    uint32_t loaded = 0u;
+    for (int r0b = 0; r0b < TRW; r0b += box_rows)
+      if ((mask >> r0b) & box_mask) {
+        ++n_boxes;
+        loaded |= box_mask << r0b;
+      }
+    if (lane == 0) {
+      MmaStage& m = st[w][s];
+      m.rows = mask;
+      m.loaded = loaded;
+      m.b = it.b;
+      m.t = it.t;
+      m.h0 = it.h0;
+      m.n_heads = it.n_heads;
+      m.split = it.split;
+      m.first = k == 0;
+      m.last = k + 1 == it.n_tiles;
+      mbar_arrive_expect_tx(&full_bar[w][s], static_cast<uint32_t>(n_boxes) * S::NHALF * box_rows * 128u * 2u);
+    }
+    __syncwarp();
+    if (r < TRW && r % box_rows == 0 && ((mask >> r) & box_mask)) {
+#pragma unroll
+      for (int h = 0; h < S::NHALF; ++h) {
+        tma_load_2d(kdst + h * S::HALF_BYTES + r * 128, &tmk, h * 64, y, &full_bar[w][s]);
+        tma_load_2d(vdst + h * S::HALF_BYTES + r * 128, &tmv, h * 64, y, &full_bar[w][s]);
+      }
+    }
+    ++ptile;
+    ++produced;
+    return true;
+  };
+
+  resolve();
+  if (!exhausted) resolve();
+  for (int i = 0; i < STG; ++i)
+    if (!issue()) break;
+
+  // ---- consumer state
+  const int mi = lane >> 3, ri = lane & 7;
+  const int hA = (lane & 3) * 2;   // this thread's two heads (accumulator columns)
+  const int tk = lane >> 2;        // its token / channel row within a 16-row block
+  uint32_t qb[S::KS][2];
+  float o[S::KS][4];               // O^T: channel blocks x (row tk, tk+8) x heads (hA, hA+1)
+  float mA = -INFINITY, mB = -INFINITY, lA = 0.f, lB = 0.f;
+  int32_t cb = 0, ct = 0, ch0 = 0, cnh = 0, csplit = 0;
+  const float sl2 = p.scale_log2;
+  const uint32_t ring_s = smem_u32(ring);
+
+  int64_t consumed = 0;
+  bool abort = false;
+  while (consumed < produced) {
+    const int s = static_cast<int>(consumed % STG);
+    if (!mbar_wait_bounded(&full_bar[w][s], static_cast<uint32_t>((consumed / STG) & 1))) {
+      report(p.status, LINATTN_DEV_TIMEOUT);
+      abort = true;
+      break;
+    }
+    const MmaStage sd = st[w][s];
+    if (sd.first) {
+      cb = sd.b;
+      ct = sd.t;
+      ch0 = sd.h0;
+      cnh = sd.n_heads;
+      csplit = sd.split;
+      const T* qrow = static_cast<const T*>(p.q) + static_cast<int64_t>(cb) * p.qs[0] +
+                      static_cast<int64_t>(ch0 + tk) * p.qs[1] + static_cast<int64_t>(ct) * p.qs[2];
+#pragma unroll
+      for (int kk = 0; kk < S::KS; ++kk) {
+        float v[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int col = kk * 16 + hA + (e >> 1) * 8 + (e & 1);  // B fragment: k = channels, n = head tk
+          v[e] = tk < cnh ? to_float(qrow[col * p.qs[3]]) : 0.f;
+        }
+        qb[kk][0] = M::pack(v[0], v[1]);
+        qb[kk][1] = M::pack(v[2], v[3]);
+      }
+#pragma unroll
+      for (int n = 0; n < S::KS; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+      mA = mB = -INFINITY;
+      lA = lB = 0.f;
+    }
+    const uint32_t kst = ring_s + static_cast<uint32_t>(s) * S::STAGE_BYTES;
+    const uint32_t vst = kst + S::TILE_BYTES;
+    // rows a box brought in but the tile does not use: zero their V so that P = 0
+    // meets finite values in P V
+    const uint32_t holes = sd.loaded & ~sd.rows;
+    if (holes) {
+      uint8_t* vrows = ring + static_cast<size_t>(s) * S::STAGE_BYTES + S::TILE_BYTES;
+      for (int i = lane; i < TRW * (D / 8); i += 32) {
+        const int row = i / (D / 8), chunk = i % (D / 8);
+        if ((holes >> row) & 1u)
+          *reinterpret_cast<uint4*>(vrows + swz<D>(row, chunk)) = make_uint4(0u, 0u, 0u, 0u);
+      }
+      __syncwarp();
+    }
+    // ---- S^T = K Q^T: tokens (16 per block) x heads (8)
+    float sc[S::MT][4];
+#pragma unroll
+    for (int mt = 0; mt < S::MT; ++mt) sc[mt][0] = sc[mt][1] = sc[mt][2] = sc[mt][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < S::KS; ++kk) {
+#pragma unroll
+      for (int mt = 0; mt < S::MT; ++mt) {
+        uint32_t a[4];
+        ldsm_x4(kst + swz<D>(mt * 16 + (mi & 1) * 8 + ri, kk * 2 + (mi >> 1)), a[0], a[1], a[2], a[3]);
+        M::mma(sc[mt], a, qb[kk][0], qb[kk][1]);
+      }
+    }
+    // ---- online softmax per head (column); unread rows -> -inf
+    float tA = -INFINITY, tB = -INFINITY;
+#pragma unroll
+    for (int mt = 0; mt < S::MT; ++mt) {
+      const bool v0 = (sd.rows >> (mt * 16 + tk)) & 1u;
+      const bool v1 = (sd.rows >> (mt * 16 + tk + 8)) & 1u;
+      sc[mt][0] = v0 ? sc[mt][0] * sl2 : -INFINITY;
+      sc[mt][1] = v0 ? sc[mt][1] * sl2 : -INFINITY;
+      sc[mt][2] = v1 ? sc[mt][2] * sl2 : -INFINITY;
+      sc[mt][3] = v1 ? sc[mt][3] * sl2 : -INFINITY;
+      tA = fmaxf(tA, fmaxf(sc[mt][0], sc[mt][2]));
+      tB = fmaxf(tB, fmaxf(sc[mt][1], sc[mt][3]));
+    }
+#pragma unroll
+    for (int off = 4; off <= 16; off <<= 1) {
+      tA = fmaxf(tA, __shfl_xor_sync(0xffffffffu, tA, off));
+      tB = fmaxf(tB, __shfl_xor_sync(0xffffffffu, tB, off));
+    }
+    const float nA = fmaxf(mA, tA), nB = fmaxf(mB, tB);
+    const float aA = nA == -INFINITY ? 1.f : exp2f(mA - nA);
+    const float aB = nB == -INFINITY ? 1.f : exp2f(mB - nB);
+    float sA = 0.f, sB = 0.f;
+#pragma unroll
+    for (int mt = 0; mt < S::MT; ++mt) {
+      sc[mt][0] = nA == -INFINITY ? 0.f : exp2f(sc[mt][0] - nA);
+      sc[mt][2] = nA == -INFINITY ? 0.f : exp2f(sc[mt][2] - nA);
+      sc[mt][1] = nB == -INFINITY ? 0.f : exp2f(sc[mt][1] - nB);
+      sc[mt][3] = nB == -INFINITY ? 0.f : exp2f(sc[mt][3] - nB);
+      sA += sc[mt][0] + sc[mt][2];
+      sB += sc[mt][1] + sc[mt][3];
+    }
+#pragma unroll
+    for (int off = 4; off <= 16; off <<= 1) {
+      sA += __shfl_xor_sync(0xffffffffu, sA, off);
+      sB += __shfl_xor_sync(0xffffffffu, sB, off);
+    }
+    lA = lA * aA + sA;
+    lB = lB * aB + sB;
+    mA = nA;
+    mB = nB;
+#pragma unroll
+    for (int n = 0; n < S::KS; ++n) {
+      o[n][0] *= aA;
+      o[n][1] *= aB;
+      o[n][2] *= aA;
+      o[n][3] *= aB;
+    }
+    // ---- O^T += V^T P^T  (P = hi + lo in the 16-bit type)
+#pragma unroll
+    for (int mt = 0; mt < S::MT; ++mt) {
+      const uint32_t h0 = M::pack(sc[mt][0], sc[mt][1]);  // tokens tk,   heads hA, hA+1
+      const uint32_t h1 = M::pack(sc[mt][2], sc[mt][3]);  // tokens tk+8
+      const float2 r0 = M::unpack(h0), r1 = M::unpack(h1);
+      const uint32_t l0 = M::pack(sc[mt][0] - r0.x, sc[mt][1] - r0.y);
+      const uint32_t l1 = M::pack(sc[mt][2] - r1.x, sc[mt][3] - r1.y);
+      const uint32_t bh0 = movmatrix_t(h0), bh1 = movmatrix_t(h1);
+      const uint32_t bl0 = movmatrix_t(l0), bl1 = movmatrix_t(l1);
+#pragma unroll
+      for (int dm = 0; dm < S::KS; ++dm) {
+        uint32_t a[4];
+        ldsm_x4_t(vst + swz<D>(mt * 16 + (mi >> 1) * 8 + ri, dm * 2 + (mi & 1)), a[0], a[1], a[2], a[3]);
+        M::mma(o[dm], a, bh0, bh1);
+        M::mma(o[dm], a, bl0, bl1);
+      }
+    }
+    __syncwarp();
+    if (holes) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // before the next TMA fill
+    ++consumed;
+    // ---- item finished: write (o, lse) for its heads
+    if (sd.last) {
+      const float iA = lA > 0.f ? 1.f / lA : 0.f, iB = lB > 0.f ? 1.f / lB : 0.f;
+      const float lseA = lA > 0.f ? (mA + log2f(lA)) * 0.69314718055994531f : -INFINITY;
+      const float lseB = lB > 0.f ? (mB + log2f(lB)) * 0.69314718055994531f : -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int g = hA + j;
+        if (g >= cnh) continue;
+        const int64_t h = ch0 + g;
+        const int64_t row = (static_cast<int64_t>(cb) * p.Hq + h) * p.Tq + ct;
+        const float inv = j ? iB : iA;
+        if (p.n_splits == 1) {
+          const int64_t ob = static_cast<int64_t>(cb) * p.os[0] + h * p.os[1] + static_cast<int64_t>(ct) * p.os[2];
+#pragma unroll
+          for (int dm = 0; dm < S::KS; ++dm) {
+            store_any(p.out, ob + (dm * 16 + tk) * p.os[3], p.q_dtype, o[dm][j] * inv);
+            store_any(p.out, ob + (dm * 16 + tk + 8) * p.os[3], p.q_dtype, o[dm][2 + j] * inv);
+          }
+          if (p.lse_out && tk == 0) p.lse_out[row] = j ? lseB : lseA;
+        } else {
+          float* wo = p.ws_o + (static_cast<int64_t>(csplit) * rows_total + row) * D;
+#pragma unroll
+          for (int dm = 0; dm < S::KS; ++dm) {
+            wo[dm * 16 + tk] = o[dm][j] * inv;
+            wo[dm * 16 + tk + 8] = o[dm][2 + j] * inv;
+          }
+          if (tk == 0) p.ws_lse[static_cast<int64_t>(csplit) * rows_total + row] = j ? lseB : lseA;
+        }
+      }
+    }
+    issue();
+    if (pending) {
+      pending = false;
+      if (!exhausted) resolve();  // the ring is full: the loads overlap the copies in flight
+    }
+  }
+  if (abort) {
+    for (int64_t c2 = consumed; c2 < produced; ++c2)
+      (void)mbar_wait_bounded(&full_bar[w][c2 % STG], static_cast<uint32_t>((c2 / STG) & 1));
+  }
+}
+
+}  // namespace linattn

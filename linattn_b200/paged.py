@@ -23,7 +23,7 @@ from typing import Optional
 import torch
 
 from linattn_b200 import _lib as L
-from linattn_b200.block_sparse import choose_splits, sparse_attention, tile_rows
+from linattn_b200.block_sparse import plan_splits, sparse_attention
 from linattn_b200.quest_pages import DECODE_OFFSET, QuestSelection
 
 __all__ = ["PagedKVCache", "QuestDecoder"]
@@ -69,7 +69,8 @@ class PagedKVCache:
         return L.KV(self.k_pool.data_ptr(), self.v_pool.data_ptr(), 0, hk * p * d, p * d,
                     self.page_table.data_ptr(), self.max_pages, self.num_phys_pages,
                     L.ptr(self.k_scale), L.ptr(self.v_scale), hk, 1,
-                    self.seq_lens.data_ptr(), 0, L.FP8E4M3 if self.fp8 else L.dtype_code(self.k_pool), p, d, hk)
+                    self.seq_lens.data_ptr(), 0, L.FP8E4M3 if self.fp8 else L.dtype_code(self.k_pool), p, d, hk,
+                    self.num_phys_pages * hk * p)
 
     def meta_desc(self) -> L.Meta:
         hk, d = self.n_kv_heads, self.head_dim
@@ -178,14 +179,10 @@ class QuestDecoder:
         self.union_count = torch.empty(b, n_lists, 1, dtype=torch.int32, device=dev)
         self.union_tokens = torch.empty_like(self.union_count)
         self.out = torch.empty(b, n_heads, 1, cache.head_dim, dtype=q_dtype, device=dev)
-        eb = 1 if cache.fp8 else cache.k_pool.element_size()
-        tr = tile_rows(eb, cache.head_dim)
-        tiles = max(1, (self.max_union * cache.page_size + tr - 1) // tr)
-        g_t = 1
-        while g_t < min(self.group, 8):
-            g_t <<= 1
-        units = b * n_lists * ((self.group + g_t - 1) // g_t)
-        self.n_splits = n_splits or choose_splits(units, tiles, dev)
+        kv_code = L.FP8E4M3 if cache.fp8 else L.dtype_code(cache.k_pool)
+        q_code = {torch.float32: L.F32, torch.float16: L.F16, torch.bfloat16: L.BF16}[q_dtype]
+        self.n_splits = n_splits or plan_splits(b, n_heads, 1, cache.head_dim, kv_code, q_code, n_lists,
+                                                self.max_union, cache.page_size, dev)
         need = L.lib().linattn_sparse_attention_workspace(b, n_heads, 1, cache.head_dim, self.n_splits)
         self.workspace = torch.empty(max(1, (need + 3) // 4), dtype=torch.float32, device=dev)
         self._lists = L.Lists(self.union_ids.data_ptr(), L.I32, n_lists, *self.union_ids.stride()[:3],

@@ -52,8 +52,8 @@ def test_host_validation_without_gpu():
                                       0, 1.0, ctypes.c_void_p(16), (L.c_i64 * 4)(0, 0, 0, 1), None, 1, None, 0, None,
                                       None)
     assert rc == 2 and b"kv dtype" in lib.linattn_last_error()
-    assert lib.linattn_sparse_attention_workspace(2, 8, 1, 128, 1) == 0
-    assert lib.linattn_sparse_attention_workspace(2, 8, 1, 128, 4) == 4 * 2 * 8 * 129 * 4
+    assert lib.linattn_sparse_attention_workspace(2, 8, 1, 128, 1) == 256
+    assert lib.linattn_sparse_attention_workspace(2, 8, 1, 128, 4) == 256 + 4 * 2 * 8 * 129 * 4
 
 
 def test_operators_refuse_cpu_tensors():

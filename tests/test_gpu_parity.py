@@ -447,3 +447,90 @@ def test_paged_bad_page_id_reports_status(cuda, monkeypatch):
     dec.step(q)
     bits = L.read_status(cache.device)
     assert bits & L.DEV_BAD_ID
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("bs", [1, 16, 48, 128])
+def test_block_sparse_page_sizes(cuda, dtype, bs):
+    """Per-token lists (block 1, the DSA form), blocks smaller than, not dividing, and
+    larger than a warp tile; -1 padding in the lists."""
+    from linattn_b200 import block_sparse_attention
+
+    gen = torch.Generator().manual_seed(bs)
+    b, hq, hkv, tq, tk, d = 2, 8, 2, 4, 700, 128
+    n_blocks = (tk + bs - 1) // bs
+    n = min(n_blocks, 300 if bs == 1 else 9)
+    q = torch.randn(b, hq, tq, d, generator=gen).to(dtype)
+    k = torch.randn(b, hkv, tk, d, generator=gen).to(dtype)
+    v = torch.randn(b, hkv, tk, d, generator=gen).to(dtype)
+    ids = torch.stack([torch.randperm(n_blocks, generator=gen)[:n] for _ in range(b * hkv * tq)]).view(b, hkv, tq, n)
+    ids[..., -2:] = -1  # padding
+    out = block_sparse_attention(q.to(cuda), k.to(cuda), v.to(cuda), ids.to(cuda), block_size=bs)
+    ref = oracle.block_sparse_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(),
+                                        np.where(ids.numpy() < 0, 10 ** 9, ids.numpy()), block_size=bs)
+    assert_close_16(out, ref)
+
+
+@pytest.mark.parametrize("union", [True, False])
+def test_cuda_quest_variant_bf16_d128_chunked(cuda, union):
+    """Chunked prefill + decode through cuda_quest at the BASELINE head size (the
+    tensor-core path with the causal limit inside pages)."""
+    from linattn_b200 import AttnConfig, build
+
+    gen = torch.Generator().manual_seed(5)
+    b, hq, hkv, t, d, page, topk = 2, 8, 2, 700, 128, 16, 7
+    q = torch.randn(b, hq, t, d, generator=gen).to(torch.bfloat16)
+    k = torch.randn(b, hkv, t, d, generator=gen).to(torch.bfloat16)
+    v = torch.randn(b, hkv, t, d, generator=gen).to(torch.bfloat16)
+    cfg = AttnConfig(n_heads=hq, n_kv_heads=hkv, head_dim=d, block_size=page, topk_blocks=topk,
+                     extras={} if union else {"gqa_union": False})
+    out, _ = build("cuda_quest", cfg).forward(q.to(cuda), k.to(cuda), v.to(cuda), chunk=256)
+    qf, kf, vf = (x.float().numpy() for x in (q, k, v))
+    outs, ambiguous = [], []
+    group = hq // hkv
+    for start in range(0, t, 256):
+        qc = qf[:, :, start:start + 256]
+        kc, vc = kf[:, :, : start + 256], vf[:, :, : start + 256]
+        mask = oracle.quest_effective_mask(qc, kc, page, topk, offset=start, group=group, gqa_union_mode=union)
+        outs.append(oracle.dense_attention(qc, kc, vc, mask=mask))
+        # rows whose k-th and (k+1)-th float64 page bounds are within 1e-2: the kernel's
+        # fp32 sums may legitimately pick the other page there
+        mins, maxs = oracle.page_bounds(kc, page)
+        _, sc = oracle.page_select(qc, mins, maxs, page, topk, offset=start)
+        srt = -np.sort(-np.where(np.isfinite(sc), sc, np.where(sc > 0, 1e30, -1e30)), axis=-1)
+        kk = min(topk, sc.shape[-1])
+        gap = np.abs(srt[..., kk - 1] - srt[..., kk]) if kk < sc.shape[-1] else np.full(sc.shape[:-1], np.inf)
+        gap = np.where(srt[..., min(kk, sc.shape[-1] - 1)] > -1e29, gap, np.inf)  # < k+1 visible: no choice
+        amb = gap < 1e-2
+        if union:
+            amb = np.repeat(amb.reshape(b, hkv, group, -1).any(2), group, axis=1)
+        ambiguous.append(amb)
+    ref = np.concatenate(outs, axis=2)
+    amb = np.concatenate(ambiguous, axis=2)
+    got = out.float().cpu().numpy()
+    ok = np.all(np.abs(got - ref) <= TOL_16 + 2.0 ** -8 * np.abs(ref), axis=-1)
+    assert amb.mean() < 0.1  # the check must cover most rows
+    assert np.all(ok | amb), f"{int((~ok & ~amb).sum())} unambiguous rows differ"
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_rows_past_sequence_end_are_never_used(cuda, dtype):
+    """K/V views into a larger buffer whose rows past T_k hold NaN: the tail page's
+    box brings those rows in, and the result must still be the oracle's."""
+    from linattn_b200 import block_sparse_attention
+
+    gen = torch.Generator().manual_seed(9)
+    b, hq, hkv, tq, tk, t_alloc, d, bs = 2, 8, 2, 3, 700, 1024, 128, 64
+    kbuf = torch.full((b, hkv, t_alloc, d), float("nan"), dtype=dtype)
+    vbuf = torch.full((b, hkv, t_alloc, d), float("nan"), dtype=dtype)
+    kbuf[:, :, :tk] = torch.randn(b, hkv, tk, d, generator=gen).to(dtype)
+    vbuf[:, :, :tk] = torch.randn(b, hkv, tk, d, generator=gen).to(dtype)
+    q = torch.randn(b, hq, tq, d, generator=gen).to(dtype)
+    ids = torch.tensor([10, 3, 0, 7]).view(1, 1, 1, 4).expand(b, hkv, tq, 4).contiguous()  # 10 = the tail page
+    kd, vd = kbuf.to(cuda), vbuf.to(cuda)
+    out = block_sparse_attention(q.to(cuda), kd[:, :, :tk], vd[:, :, :tk], ids.to(cuda), block_size=bs)
+    k, v = kbuf[:, :, :tk], vbuf[:, :, :tk]
+    ref = oracle.block_sparse_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), ids.numpy(),
+                                        block_size=bs)
+    assert torch.isfinite(out).all()
+    assert_close_16(out, ref)

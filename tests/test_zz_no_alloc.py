@@ -76,8 +76,10 @@ def test_noalloc_rejects_oversized_scratch(cuda):
     q, k, v, ids, bs = _case(13, cuda)
     limit = L.lib().linattn_sparse_attention_noalloc_limit()
     b, hq, tq, d = q.shape
-    per_split = L.lib().linattn_sparse_attention_workspace(b, hq, tq, d, 2) // 2
+    ws = L.lib().linattn_sparse_attention_workspace
+    per_split = ws(b, hq, tq, d, 3) - ws(b, hq, tq, d, 2)
     too_many = int(limit // per_split) + 2
+    assert ws(b, hq, tq, d, too_many) > limit
     rc, _ = _call("noalloc", q, k, v, ids, bs, too_many)
     assert rc == 1
     assert b"limit" in L.lib().linattn_last_error()
