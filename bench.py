@@ -166,8 +166,9 @@ def _cpu_sample(cache, q, n_seq: int):
     tab = cache.page_table[:n_seq].long()
     kp = cache.k_pool[tab.flatten()].view(torch.int16).cpu().numpy()  # (n_seq*n_pages, Hkv, P, D)
     vp = cache.v_pool[tab.flatten()].view(torch.int16).cpu().numpy()
-    mn = cache.meta_min[tab.flatten()].view(torch.int16).cpu().numpy()
-    mx = cache.meta_max[tab.flatten()].view(torch.int16).cpu().numpy()
+    # metadata is stored per sequence in logical page order: (n_seq, H_kv, pages, D)
+    mn = cache.meta_min[:n_seq].transpose(1, 2).contiguous().view(torch.int16).cpu().numpy()
+    mx = cache.meta_max[:n_seq].transpose(1, 2).contiguous().view(torch.int16).cpu().numpy()
     qh = q[:n_seq, :, 0].contiguous().view(torch.int16).cpu().numpy()
     return kp, vp, mn, mx, qh
 

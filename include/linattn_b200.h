@@ -171,6 +171,26 @@ int linattn_page_topk(const float* scores, int64_t B, int64_t Hq, int64_t Tq, in
                       int32_t* status, void* stream);
 
 /*
+ * Fused Quest selection for one decode step of B sequences: page scores, top-k per
+ * query head and the union per kv head in one kernel (one CTA per sequence and kv
+ * head).  Metadata is [B, H_kv, max_pages, 2, D] (logical page order, min row then
+ * max row, f16/bf16).  The query of sequence b sits at position seq_lens[b] - 1: pages
+ * below n_pages_b[b] are visible, the last one and the first `sink_pages` are forced
+ * in.  ids (B, H_q, topk) int32 sorted by (score desc, page asc), -1 padded; scores
+ * (B, H_q, max_pages) optional; union_ids (B, H_kv, max_union) ascending with counts
+ * and token counts.  Group size H_q / H_kv in {1, 2, 4, 8}; D in {64, 128}.
+ * Replaces, for T_q == 1, page_select_torch (src/linattn/kernels/triton/quest_pages.py:57-78)
+ * followed by the GQA union of QuestAttention.page_selection
+ * (src/linattn/variants/selection.py:214-237).
+ */
+int linattn_quest_decode_select(const void* q, int32_t q_dtype, int64_t B, int64_t Hq, int64_t D,
+                                const int64_t* q_strides /*[4]*/, const void* meta, int32_t meta_dtype,
+                                int64_t n_kv_heads, int64_t max_pages, const int32_t* n_pages_b,
+                                const int32_t* seq_lens, int64_t page_size, int64_t topk, int32_t sink_pages,
+                                int32_t* ids, float* scores, int32_t* union_ids, int32_t* union_count,
+                                int64_t max_union, int32_t* union_tokens, int32_t* status, void* stream);
+
+/*
  * Exact softmax attention of each query over the KV rows of its list's pages.
  * q and out are (B, H_q, T_q, D) with element strides; out has q's dtype.  Rows at
  * positions >= seq_len_b are skipped; with `causal`, rows after offset + t too.

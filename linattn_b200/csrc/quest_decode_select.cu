@@ -1,0 +1,382 @@
+// Fused Quest selection for decode: page scores -> top-k per query head -> GQA union,
+// one CTA per (sequence, kv head), no intermediate buffer in HBM.
+//
+// Metadata layout: [B, H_kv, max_pages, 2, D] (logical page order per sequence and
+// kv head, min row then max row), so one (sequence, kv head) is a single contiguous
+// stream of n_pages * 2 * D elements.  Thread 0 streams it through an NSTG-deep ring
+// of CH-page chunks with 1-D TMA bulk copies (no tensor map, no multicast); all warps
+// score each chunk for the G query heads of the group (q in registers, D/8 lanes per
+// page, transposing butterfly over the head partials) into shared memory.  Then warp
+// g runs a radix select (4 x 8-bit passes over order-preserving keys, warp-private
+// histogram) for head g, takes ties at the k-th value by lowest page index, sorts its
+// k pages by (score desc, index asc), writes them and sets the group's union bitmap;
+// the CTA compacts the bitmap into an ascending page list.
+//
+// Decode semantics: the query sits at position seq_len_b - 1, so every page below
+// n_pages_b is visible, the own page is n_pages_b - 1, and it and the first
+// `sink_pages` pages are forced to +inf (quest_pages.py:67-75 at T_q == 1).
+#include <cstdio>
+
+#include "launchers.cuh"
+
+namespace linattn {
+
+namespace {
+
+constexpr int NSTG = 8;   // ring stages
+constexpr int CH = 32;    // pages per chunk
+
+template <int G, int LPR>
+__device__ __forceinline__ void group_reduce(float (&v)[G], int lane) {
+  int n = G;
+#pragma unroll
+  for (int off = LPR / 2; off >= 1; off >>= 1) {
+    if (n > 1) {
+      const bool upper = (lane & off) != 0;
+#pragma unroll
+      for (int i = 0; i < G / 2; ++i) {
+        if (i < n / 2) {
+          const float send = upper ? v[i] : v[i + n / 2];
+          const float keep = upper ? v[i + n / 2] : v[i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+      }
+      n >>= 1;
+    } else {
+      v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
+    }
+  }
+}
+
+struct DecodeSelectParams {
+  const void* q;
+  int q_dtype;
+  int64_t B, Hq, Hkv;
+  int64_t qs[4];
+  const void* meta;
+  int64_t max_pages;
+  const int32_t* n_pages_b;
+  const int32_t* seq_lens;
+  int64_t P;
+  int topk;
+  int sink_pages;
+  int32_t* ids;      // (B, Hq, topk)
+  float* scores;     // optional (B, Hq, max_pages)
+  int32_t* union_ids;
+  int32_t* union_count;
+  int64_t max_union;
+  int32_t* union_tokens;
+  int32_t* status;
+};
+
+}  // namespace
+
+template <typename TM, int D, int G>
+__global__ void __launch_bounds__(256, 1) quest_decode_select_kernel(const DecodeSelectParams p) {
+  constexpr int LPR = D / 8;               // lanes per page
+  constexpr int PPW = 32 / LPR;            // pages per warp step
+  constexpr int PAGE_ELEMS = 2 * D;
+  constexpr int CHUNK_BYTES = CH * PAGE_ELEMS * static_cast<int>(sizeof(TM));
+  constexpr int NV = G >= LPR ? G / LPR : 1;
+  constexpr int REP = G >= LPR ? 1 : LPR / G;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* ring = smem;                                                   // NSTG chunks
+  float* sc = reinterpret_cast<float*>(smem + NSTG * CHUNK_BYTES);        // [G][max_pages]
+  uint32_t* hist = reinterpret_cast<uint32_t*>(sc + G * p.max_pages);     // [8 warps][256]
+  uint32_t* bitmap = hist + 8 * 256;                                      // [ceil(max_pages/32)]
+  uint32_t* sel = bitmap + (p.max_pages + 31) / 32;                       // [8 warps][2][topk]
+  __shared__ __align__(8) uint64_t bar[NSTG];
+  __shared__ uint32_t scan_tmp[9];
+  __shared__ uint32_t sh_tokens;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t kvh = blockIdx.x % p.Hkv, b = blockIdx.x / p.Hkv;
+  const int64_t nb = lmin(p.n_pages_b[b], p.max_pages);
+  const int64_t W = (p.max_pages + 31) / 32;
+  for (int64_t w = tid; w < W; w += 256) bitmap[w] = 0u;
+  if (tid == 0) {
+    for (int s = 0; s < NSTG; ++s) mbar_init(&bar[s], 1);
+    mbar_fence_init();
+    sh_tokens = 0u;
+  }
+  __syncthreads();
+
+  const TM* base = static_cast<const TM*>(p.meta) + (b * p.Hkv + kvh) * p.max_pages * PAGE_ELEMS;
+  const int64_t n_chunks = (nb + CH - 1) / CH;
+  auto issue = [&](int64_t c) {
+    const int s = static_cast<int>(c % NSTG);
+    const uint32_t pages = static_cast<uint32_t>(lmin(CH, nb - c * CH));
+    const uint32_t bytes = pages * PAGE_ELEMS * static_cast<uint32_t>(sizeof(TM));
+    mbar_arrive_expect_tx(&bar[s], bytes);
+    bulk_g2s(ring + s * CHUNK_BYTES, base + c * CH * PAGE_ELEMS, bytes, &bar[s]);
+  };
+  if (tid == 0)
+    for (int64_t c = 0; c < n_chunks && c < NSTG; ++c) issue(c);
+
+  // q of the G heads: lane covers channels [cl*8, cl*8+8)
+  const int sub = lane / LPR, cl = lane % LPR;
+  float qv[G][8];
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      qv[g][c] = load_any(p.q, b * p.qs[0] + (kvh * G + g) * p.qs[1] + (cl * 8 + c) * p.qs[3], p.q_dtype);
+
+  bool abort = false;
+  for (int64_t c = 0; c < n_chunks; ++c) {
+    const int s = static_cast<int>(c % NSTG);
+    if (!mbar_wait_bounded(&bar[s], static_cast<uint32_t>((c / NSTG) & 1))) {
+      report(p.status, LINATTN_DEV_TIMEOUT);
+      abort = true;
+    }
+    if (__syncthreads_or(abort)) {
+      abort = true;
+      break;
+    }
+    const TM* chunk = reinterpret_cast<const TM*>(ring + s * CHUNK_BYTES);
+    const int64_t pages = lmin(CH, nb - c * CH);
+    for (int pp = warp * PPW; pp < CH; pp += 8 * PPW) {
+      const int pg = pp + sub;
+      float acc[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) acc[g] = 0.f;
+      if (pg < pages) {
+        float mn[8], mx[8];
+        load8(chunk + pg * PAGE_ELEMS + cl * 8, mn);
+        load8(chunk + pg * PAGE_ELEMS + D + cl * 8, mx);
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[g] = fmaf(qv[g][e], qv[g][e] >= 0.f ? mx[e] : mn[e], acc[g]);
+      }
+      group_reduce<G, LPR>(acc, lane);
+      if (pg < pages && (cl % REP) == 0) {
+        const int64_t page = c * CH + pg;
+        const bool forced = page == nb - 1 || page < p.sink_pages;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          const int g = G >= LPR ? cl * NV + i : cl / REP;
+          sc[g * p.max_pages + page] = forced ? INFINITY : acc[i];
+        }
+      }
+    }
+    __syncthreads();  // chunk s consumed
+    if (tid == 0 && c + NSTG < n_chunks) issue(c + NSTG);
+  }
+  if (abort) {
+    if (tid == 0)  // bounded wait for copies still in flight
+      for (int64_t c = 0; c < n_chunks && c < NSTG; ++c)
+        (void)mbar_wait_bounded(&bar[c % NSTG], static_cast<uint32_t>((c / NSTG) & 1));
+    __syncthreads();
+    return;
+  }
+
+  // ---- per-head top-k: warp g selects for query head kvh*G + g
+  const int64_t kb = nb > 0 ? lmax(1, lmin(p.topk, nb)) : 0;
+  const uint32_t neg_inf_key = float_key(-INFINITY);
+  if (warp < G) {
+    const int g = warp;
+    const int64_t h = kvh * G + g;
+    const float* srow = sc + g * p.max_pages;
+    uint32_t* hw = hist + warp * 256;
+    uint32_t* sel_idx = sel + warp * 2 * p.topk;
+    uint32_t* sel_key = sel_idx + p.topk;
+    if (p.scores) {
+      float* dst = p.scores + (b * p.Hq + h) * p.max_pages;
+      for (int64_t i = lane; i < p.max_pages; i += 32) dst[i] = i < nb ? srow[i] : -INFINITY;
+    }
+    uint32_t prefix = 0u, mask = 0u, remaining = static_cast<uint32_t>(kb);
+    for (int shift = 24; shift >= 0 && kb > 0; shift -= 8) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) hw[lane * 8 + j] = 0u;
+      __syncwarp();
+      for (int64_t i = lane; i < nb; i += 32) {
+        const uint32_t key = float_key(srow[i]);
+        if ((key & mask) == prefix) atomicAdd(&hw[(key >> shift) & 255u], 1u);
+      }
+      __syncwarp();
+      // lane owns the 8 bins 255 - (lane*8 + j): counts in descending bin order
+      uint32_t cnt[8], local = 0u;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        cnt[j] = hw[255 - (lane * 8 + j)];
+        local += cnt[j];
+      }
+      uint32_t incl = local;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      uint32_t above = incl - local;  // keys in higher bins than this lane's
+      int found = -1;
+      uint32_t rem_new = 0u;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (found < 0 && above < remaining && above + cnt[j] >= remaining) {
+          found = 255 - (lane * 8 + j);
+          rem_new = remaining - above;
+        }
+        above += cnt[j];
+      }
+      const unsigned who = __ballot_sync(0xffffffffu, found >= 0);
+      const int src = __ffs(who) - 1;
+      const uint32_t digit = static_cast<uint32_t>(__shfl_sync(0xffffffffu, found, src));
+      remaining = __shfl_sync(0xffffffffu, rem_new, src);
+      prefix |= digit << shift;
+      mask |= 0xffu << shift;
+      __syncwarp();
+    }
+    // gather: every key > kstar, and the first `remaining` keys == kstar (index order)
+    const uint32_t kstar = prefix;
+    uint32_t n_sel = 0u, eq_taken = 0u;
+    for (int64_t i0 = 0; i0 < nb && kb > 0; i0 += 32) {
+      const int64_t i = i0 + lane;
+      const uint32_t key = i < nb ? float_key(srow[i]) : 0u;
+      const bool gt = i < nb && key > kstar;
+      const bool eq = i < nb && key == kstar;
+      const unsigned eq_mask = __ballot_sync(0xffffffffu, eq);
+      const uint32_t eq_rank = eq_taken + __popc(eq_mask & ((1u << lane) - 1u));
+      const bool take = gt || (eq && eq_rank < remaining);
+      const unsigned take_mask = __ballot_sync(0xffffffffu, take);
+      if (take) {
+        const uint32_t pos = n_sel + __popc(take_mask & ((1u << lane) - 1u));
+        sel_idx[pos] = static_cast<uint32_t>(i);
+        sel_key[pos] = key;
+      }
+      n_sel += __popc(take_mask);
+      eq_taken += __popc(eq_mask);
+    }
+    __syncwarp();
+    // rank sort (score desc, index asc), write ids, mark the union
+    int32_t* out = p.ids + (b * p.Hq + h) * p.topk;
+    for (int64_t i = lane; i < kb; i += 32) {
+      const uint32_t ki = sel_key[i], ii = sel_idx[i];
+      int rank = 0;
+      for (int64_t j = 0; j < kb; ++j) {
+        const uint32_t kj = sel_key[j], ij = sel_idx[j];
+        rank += (kj > ki || (kj == ki && ij < ii)) ? 1 : 0;
+      }
+      out[rank] = static_cast<int32_t>(ii);
+      if (ki > neg_inf_key) atomicOr(&bitmap[ii >> 5], 1u << (ii & 31u));
+    }
+    for (int64_t r = kb + lane; r < p.topk; r += 32) out[r] = -1;
+  }
+  __syncthreads();
+  // ---- compact the union into an ascending page list
+  const int64_t wpt = (W + 255) / 256;
+  const int64_t w0 = lmin(W, tid * wpt), w1 = lmin(W, w0 + wpt);
+  uint32_t cnt = 0u;
+  for (int64_t w = w0; w < w1; ++w) cnt += __popc(bitmap[w]);
+  uint32_t total = 0u;
+  uint32_t pos = block_exclusive_scan<256>(cnt, scan_tmp, &total);
+  const int64_t len = p.seq_lens[b];
+  const int64_t uoff = (b * p.Hkv + kvh) * p.max_union;
+  uint32_t tokens = 0u;
+  for (int64_t w = w0; w < w1; ++w) {
+    uint32_t bits = bitmap[w];
+    while (bits) {
+      const int bit = __ffs(bits) - 1;
+      bits &= bits - 1u;
+      const int64_t pg = w * 32 + bit;
+      if (pos < p.max_union) p.union_ids[uoff + pos] = static_cast<int32_t>(pg);
+      ++pos;
+      tokens += static_cast<uint32_t>(lmin(p.P, lmax(0, len - pg * p.P)));
+    }
+  }
+  for (int64_t j = total + tid; j < p.max_union; j += 256) p.union_ids[uoff + j] = -1;
+  atomicAdd(&sh_tokens, tokens);
+  __syncthreads();
+  if (tid == 0) {
+    if (total > p.max_union) report(p.status, LINATTN_DEV_OVERFLOW);
+    p.union_count[b * p.Hkv + kvh] = static_cast<int32_t>(lmin(total, p.max_union));
+    if (p.union_tokens) p.union_tokens[b * p.Hkv + kvh] = static_cast<int32_t>(sh_tokens);
+  }
+}
+
+size_t quest_decode_select_smem(int64_t max_pages, int64_t G, int64_t topk, int64_t D, int elem_bytes) {
+  return static_cast<size_t>(NSTG) * CH * 2 * D * elem_bytes + static_cast<size_t>(G) * max_pages * 4 +
+         8 * 256 * 4 + static_cast<size_t>((max_pages + 31) / 32) * 4 + static_cast<size_t>(8) * 2 * topk * 4;
+}
+
+template <typename TM, int D, int G>
+static cudaError_t launch_ds(const DecodeSelectParams& p, size_t smem, cudaStream_t stream) {
+  static int configured[64] = {};
+  const int dev = device_index();
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (configured[dev] < static_cast<int>(smem)) {
+    cudaError_t e = cudaFuncSetAttribute(quest_decode_select_kernel<TM, D, G>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    configured[dev] = static_cast<int>(smem);
+  }
+  quest_decode_select_kernel<TM, D, G><<<static_cast<unsigned>(p.B * p.Hkv), 256, smem, stream>>>(p);
+  return cudaGetLastError();
+}
+
+template <typename TM, int D>
+static cudaError_t launch_ds_g(const DecodeSelectParams& p, int G, size_t smem, cudaStream_t stream) {
+  switch (G) {
+    case 1: return launch_ds<TM, D, 1>(p, smem, stream);
+    case 2: return launch_ds<TM, D, 2>(p, smem, stream);
+    case 4: return launch_ds<TM, D, 4>(p, smem, stream);
+    case 8: return launch_ds<TM, D, 8>(p, smem, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <typename TM>
+static cudaError_t launch_ds_d(const DecodeSelectParams& p, int D, int G, size_t smem, cudaStream_t stream) {
+  switch (D) {
+    case 64: return launch_ds_g<TM, 64>(p, G, smem, stream);
+    case 128: return launch_ds_g<TM, 128>(p, G, smem, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace linattn
+
+using namespace linattn;
+
+extern "C" int linattn_quest_decode_select(const void* q, int32_t q_dtype, int64_t B, int64_t Hq, int64_t D,
+                                           const int64_t* q_strides, const void* meta, int32_t meta_dtype,
+                                           int64_t n_kv_heads, int64_t max_pages, const int32_t* n_pages_b,
+                                           const int32_t* seq_lens, int64_t page_size, int64_t topk,
+                                           int32_t sink_pages, int32_t* ids, float* scores, int32_t* union_ids,
+                                           int32_t* union_count, int64_t max_union, int32_t* union_tokens,
+                                           int32_t* status, void* stream) {
+  if (!q || !q_strides || !meta || !n_pages_b || !seq_lens || !ids || !union_ids || !union_count)
+    return set_error(LINATTN_EINVAL, "quest_decode_select: NULL pointer");
+  if (q_dtype != LINATTN_F32 && q_dtype != LINATTN_F16 && q_dtype != LINATTN_BF16)
+    return set_error(LINATTN_EUNSUPPORTED, "quest_decode_select: q dtype");
+  if (meta_dtype != LINATTN_F16 && meta_dtype != LINATTN_BF16)
+    return set_error(LINATTN_EUNSUPPORTED, "quest_decode_select: metadata must be f16 or bf16");
+  if (D != 64 && D != 128) return set_error(LINATTN_EUNSUPPORTED, "quest_decode_select: head_dim must be 64 or 128");
+  if (n_kv_heads <= 0 || Hq % n_kv_heads) return set_error(LINATTN_EINVAL, "quest_decode_select: H_kv must divide H_q");
+  const int64_t G = Hq / n_kv_heads;
+  if (G != 1 && G != 2 && G != 4 && G != 8)
+    return set_error(LINATTN_EUNSUPPORTED, "quest_decode_select: group size must be 1, 2, 4 or 8");
+  if (topk < 1 || topk > 1024 || max_pages < 1 || page_size < 1 || max_union < 1)
+    return set_error(LINATTN_EINVAL, "quest_decode_select: bad topk / max_pages / page_size / max_union");
+  if (reinterpret_cast<uintptr_t>(meta) % 16) return set_error(LINATTN_EINVAL, "quest_decode_select: meta alignment");
+  const size_t smem = quest_decode_select_smem(max_pages, G, topk, D, 2);
+  if (smem > 220 * 1024)
+    return set_error(LINATTN_EUNSUPPORTED, "quest_decode_select: too many pages for the fused kernel");
+  if (B * n_kv_heads == 0) return LINATTN_OK;
+  DecodeSelectParams p;
+  p.q = q; p.q_dtype = q_dtype; p.B = B; p.Hq = Hq; p.Hkv = n_kv_heads;
+  for (int i = 0; i < 4; ++i) p.qs[i] = q_strides[i];
+  p.meta = meta; p.max_pages = max_pages; p.n_pages_b = n_pages_b; p.seq_lens = seq_lens; p.P = page_size;
+  p.topk = static_cast<int>(topk); p.sink_pages = sink_pages; p.ids = ids; p.scores = scores;
+  p.union_ids = union_ids; p.union_count = union_count; p.max_union = max_union; p.union_tokens = union_tokens;
+  p.status = status;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const cudaError_t e = meta_dtype == LINATTN_BF16 ? launch_ds_d<__nv_bfloat16>(p, static_cast<int>(D), static_cast<int>(G), smem, st)
+                                                   : launch_ds_d<__half>(p, static_cast<int>(D), static_cast<int>(G), smem, st);
+  if (e != cudaSuccess) {
+    char msg[256];
+    snprintf(msg, sizeof(msg), "quest_decode_select: %s", cudaGetErrorString(e));
+    return set_error(LINATTN_ECUDA, msg);
+  }
+  return LINATTN_OK;
+}

@@ -161,6 +161,11 @@ __global__ void __launch_bounds__(32 * MmaShape<D>::NW, 1)
   const bool small_pages = P <= TRW;
   const int64_t PPT = small_pages ? TRW / P : 1;
   const int64_t segs = small_pages ? 1 : (P + TRW - 1) / TRW;
+  // per-tile row -> (entry, row in page) in 32-bit arithmetic; shifts when P and the
+  // segment count are powers of two (the common case), division otherwise
+  const int P32 = static_cast<int>(P), PPT32 = static_cast<int>(PPT), segs32 = static_cast<int>(segs);
+  const bool pow2 = (P32 & (P32 - 1)) == 0 && (segs32 & (segs32 - 1)) == 0;
+  const int p_shift = __ffs(P32) - 1, seg_shift = __ffs(segs32) - 1;
 
   // ---- item resolution: grab items until one has tiles (writing empty ones)
   int res_count = 0;           // items resolved into slots so far
@@ -250,22 +255,16 @@ __global__ void __launch_bounds__(32 * MmaShape<D>::NW, 1)
     }
   };
 
-  // ---- production: item pi of the resolved sequence, tile ptile of it
+  // ---- production: item pi of the resolved sequence, tile ptile of it.  Returns
+  // false when the next tile needs an item that is not resolved yet (or none is left).
   int pi = 0, ptile = 0;
   int64_t produced = 0;
-  bool pending = false;  // a slot was freed: resolve the next item when the ring is full
   auto issue = [&]() -> bool {
-    while (true) {
-      if (pi >= res_count) {
-        if (exhausted) return false;
-        resolve();
-        continue;
-      }
-      if (ptile < items[w][pi & 1].n_tiles) break;
+    while (pi < res_count && ptile >= items[w][pi & 1].n_tiles) {
       ++pi;  // the slot of item pi-1 is free again
       ptile = 0;
-      if (!exhausted && res_count == pi + 1) pending = true;
     }
+    if (pi >= res_count) return false;
     const MmaItem& it = items[w][pi & 1];
     const int2* table = tables + (pi & 1) * S::ITEM_MAX;
     const int s = static_cast<int>(produced % STG);
@@ -273,20 +272,22 @@ __global__ void __launch_bounds__(32 * MmaShape<D>::NW, 1)
     uint8_t* vdst = kdst + S::TILE_BYTES;
     const int k = ptile;
     const int r = lane;
-    int64_t e, rp;
+    int e, rp, slot;
     if (small_pages) {
-      e = k * PPT + r / P;
-      rp = r % P;
+      slot = pow2 ? (r >> p_shift) : r / P32;
+      rp = pow2 ? (r & (P32 - 1)) : r - slot * P32;
+      e = k * PPT32 + slot;
     } else {
-      e = k / segs;
-      rp = (k % segs) * TRW + r;
+      slot = 0;
+      e = pow2 ? (k >> seg_shift) : k / segs32;
+      rp = (k - e * segs32) * TRW + r;
     }
     bool valid = false;
     int y = 0;
-    if (r < TRW && (small_pages ? r / P < PPT : true) && e < it.n && rp < P) {
+    if (r < TRW && slot < PPT32 && e < it.n && rp < P32) {
       const int2 ent = table[e];
       valid = ent.x >= 0 && ent.x + rp < it.limit;
-      y = ent.y + static_cast<int>(rp);
+      y = ent.y + rp;
     }
     const uint32_t mask = __ballot_sync(0xffffffffu, valid);
     const uint32_t box_mask = box_rows >= 32 ? 0xffffffffu : ((1u << box_rows) - 1u);
@@ -323,11 +324,6 @@ __global__ void __launch_bounds__(32 * MmaShape<D>::NW, 1)
     return true;
   };
 
-  resolve();
-  if (!exhausted) resolve();
-  for (int i = 0; i < STG; ++i)
-    if (!issue()) break;
-
   // ---- consumer state
   const int mi = lane >> 3, ri = lane & 7;
   const int hA = (lane & 3) * 2;   // this thread's two heads (accumulator columns)
@@ -341,7 +337,16 @@ __global__ void __launch_bounds__(32 * MmaShape<D>::NW, 1)
 
   int64_t consumed = 0;
   bool abort = false;
-  while (consumed < produced) {
+  while (true) {
+    // keep one item resolved ahead of production (the loads overlap the copies in
+    // flight), then top the ring up; both have exactly one call site
+    if (!exhausted && res_count <= pi + 1) resolve();
+    while (produced - consumed < STG && issue()) {
+    }
+    if (consumed == produced) {
+      if (exhausted && pi >= res_count) break;
+      continue;
+    }
     const int s = static_cast<int>(consumed % STG);
     if (!mbar_wait_bounded(&full_bar[w][s], static_cast<uint32_t>((consumed / STG) & 1))) {
       report(p.status, LINATTN_DEV_TIMEOUT);
@@ -388,18 +393,25 @@ __global__ void __launch_bounds__(32 * MmaShape<D>::NW, 1)
       __syncwarp();
     }
     // ---- S^T = K Q^T: tokens (16 per block) x heads (8)
-    float sc[S::MT][4];
+    float sc[S::MT][4], sc2[S::MT][4];  // two accumulation chains (even / odd channel blocks)
 #pragma unroll
-    for (int mt = 0; mt < S::MT; ++mt) sc[mt][0] = sc[mt][1] = sc[mt][2] = sc[mt][3] = 0.f;
+    for (int mt = 0; mt < S::MT; ++mt) {
+      sc[mt][0] = sc[mt][1] = sc[mt][2] = sc[mt][3] = 0.f;
+      sc2[mt][0] = sc2[mt][1] = sc2[mt][2] = sc2[mt][3] = 0.f;
+    }
 #pragma unroll
     for (int kk = 0; kk < S::KS; ++kk) {
 #pragma unroll
       for (int mt = 0; mt < S::MT; ++mt) {
         uint32_t a[4];
         ldsm_x4(kst + swz<D>(mt * 16 + (mi & 1) * 8 + ri, kk * 2 + (mi >> 1)), a[0], a[1], a[2], a[3]);
-        M::mma(sc[mt], a, qb[kk][0], qb[kk][1]);
+        M::mma((kk & 1) ? sc2[mt] : sc[mt], a, qb[kk][0], qb[kk][1]);
       }
     }
+#pragma unroll
+    for (int mt = 0; mt < S::MT; ++mt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) sc[mt][i] += sc2[mt][i];
     // ---- online softmax per head (column); unread rows -> -inf
     float tA = -INFINITY, tB = -INFINITY;
 #pragma unroll
@@ -498,11 +510,6 @@ __global__ void __launch_bounds__(32 * MmaShape<D>::NW, 1)
           if (tk == 0) p.ws_lse[static_cast<int64_t>(csplit) * rows_total + row] = j ? lseB : lseA;
         }
       }
-    }
-    issue();
-    if (pending) {
-      pending = false;
-      if (!exhausted) resolve();  // the ring is full: the loads overlap the copies in flight
     }
   }
   if (abort) {

@@ -9,7 +9,10 @@ B200-first:
 * ``k_pool, v_pool [N_phys, H_kv, P, D]`` - each (page, head) is one contiguous
   ``P*D`` chunk (16 KiB in bf16 at P=64, D=128), moved by one TMA bulk copy;
 * ``page_table int32 [B, max_pages]`` maps logical to physical pages;
-* ``meta_min/meta_max [N_phys, H_kv, D]`` - Quest's channel bounds per page;
+* ``meta [B, H_kv, max_pages, 2, D]`` - Quest's channel bounds (min row, max row) in
+  LOGICAL page order per sequence and kv head, so that scoring streams one
+  contiguous block per (sequence, kv head) with large TMA copies (``meta_min`` /
+  ``meta_max`` are views);
 * fp8 e4m3 pools add ``k_scale/v_scale fp32 [N_phys, H_kv]`` (``kv/quant.py:90-93``
   applied per (page, head)); the metadata then bounds the dequantised keys, rounded
   outward to the metadata dtype.
@@ -48,9 +51,9 @@ class PagedKVCache:
         self.k_pool = torch.zeros(shape, dtype=pool_dtype, device=self.device)
         self.v_pool = torch.zeros(shape, dtype=pool_dtype, device=self.device)
         self.meta_dtype = meta_dtype or (torch.bfloat16 if self.fp8 else dtype)
-        mshape = (self.num_phys_pages, n_kv_heads, head_dim)
-        self.meta_min = torch.zeros(mshape, dtype=self.meta_dtype, device=self.device)
-        self.meta_max = torch.zeros(mshape, dtype=self.meta_dtype, device=self.device)
+        self.meta = torch.zeros(batch, n_kv_heads, max_pages, 2, head_dim, dtype=self.meta_dtype, device=self.device)
+        self.meta_min = self.meta[..., 0, :]
+        self.meta_max = self.meta[..., 1, :]
         if self.fp8:
             self.k_scale = torch.ones(self.num_phys_pages, n_kv_heads, dtype=torch.float32, device=self.device)
             self.v_scale = torch.ones_like(self.k_scale)
@@ -73,9 +76,9 @@ class PagedKVCache:
                     self.num_phys_pages * hk * p)
 
     def meta_desc(self) -> L.Meta:
-        hk, d = self.n_kv_heads, self.head_dim
-        return L.Meta(self.meta_min.data_ptr(), self.meta_max.data_ptr(), 0, hk * d, d, self.page_table.data_ptr(),
-                      self.max_pages, self.num_phys_pages, L.dtype_code(self.meta_min), hk)
+        hk, d, n = self.n_kv_heads, self.head_dim, self.max_pages
+        return L.Meta(self.meta_min.data_ptr(), self.meta_max.data_ptr(), hk * n * 2 * d, 2 * d, n * 2 * d, None, 0,
+                      0, L.dtype_code(self.meta), hk)
 
     # -- page allocation (host) ----------------------------------------------------
     def _ensure_pages(self, b: int, n_pages: int) -> None:
@@ -162,7 +165,7 @@ class QuestDecoder:
 
     def __init__(self, cache: PagedKVCache, n_heads: int, topk: int, *, sink_pages: int = 0,
                  scale: Optional[float] = None, gqa_union: bool = True, n_splits: Optional[int] = None,
-                 q_dtype: torch.dtype = torch.bfloat16):
+                 q_dtype: torch.dtype = torch.bfloat16, keep_scores: bool = False):
         self.cache = cache
         self.n_heads = n_heads
         self.group = n_heads // cache.n_kv_heads if gqa_union else 1
@@ -171,7 +174,12 @@ class QuestDecoder:
         self.scale = scale if scale is not None else 1.0 / math.sqrt(cache.head_dim)
         dev = cache.device
         b, n = cache.batch, cache.max_pages
-        self.scores = torch.empty(b, n_heads, 1, n, dtype=torch.float32, device=dev)
+        group_size = n_heads // cache.n_kv_heads
+        # fused selection kernel (one CTA per sequence and kv head) when it applies
+        self.fused = (gqa_union and group_size in (1, 2, 4, 8) and cache.head_dim in (64, 128)
+                      and cache.meta_dtype in (torch.float16, torch.bfloat16) and self._fused_smem(n, group_size) <= 220 * 1024)
+        self.keep_scores = keep_scores or not self.fused
+        self.scores = torch.empty(b, n_heads, 1, n, dtype=torch.float32, device=dev) if self.keep_scores else None
         self.ids = torch.empty(b, n_heads, 1, self.topk, dtype=torch.int32, device=dev)
         self.max_union = min(self.group * self.topk, n)
         n_lists = n_heads // self.group
@@ -188,6 +196,10 @@ class QuestDecoder:
         self._lists = L.Lists(self.union_ids.data_ptr(), L.I32, n_lists, *self.union_ids.stride()[:3],
                               self.max_union, self.union_count.data_ptr(), *self.union_count.stride())
 
+    def _fused_smem(self, n: int, g: int) -> int:
+        d = self.cache.head_dim
+        return 8 * 32 * 2 * d * 2 + g * n * 4 + 8 * 256 * 4 + ((n + 31) // 32) * 4 + 8 * 2 * self.topk * 4
+
     def select(self, q: torch.Tensor) -> QuestSelection:
         c = self.cache
         dev = c.device
@@ -195,6 +207,13 @@ class QuestDecoder:
         stream = L.stream_of(q)
         b, hq, tq, d = q.shape
         lib = L.lib()
+        if self.fused:
+            L.check(lib.linattn_quest_decode_select(
+                q.data_ptr(), L.dtype_code(q), b, hq, d, L.strides4(q), c.meta.data_ptr(), L.dtype_code(c.meta),
+                c.n_kv_heads, c.max_pages, c.n_pages_b.data_ptr(), c.seq_lens.data_ptr(), c.page_size, self.topk,
+                self.sink_pages, self.ids.data_ptr(), L.ptr(self.scores), self.union_ids.data_ptr(),
+                self.union_count.data_ptr(), self.max_union, self.union_tokens.data_ptr(), status.data_ptr(), stream))
+            return QuestSelection(self.ids, self.scores, self.union_ids, self.union_count, self.union_tokens)
         L.check(lib.linattn_quest_scores(q.data_ptr(), L.dtype_code(q), b, hq, tq, d, L.strides4(q), c.meta_desc(),
                                          c.page_size, c.max_pages, DECODE_OFFSET, self.sink_pages,
                                          c.n_pages_b.data_ptr(), self.scores.data_ptr(), status.data_ptr(), stream))

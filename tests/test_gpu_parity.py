@@ -369,7 +369,7 @@ def _check_decode(cache, table, q, topk, sink, tol):
     from linattn_b200 import QuestDecoder
 
     hq = q.shape[1]
-    dec = QuestDecoder(cache, hq, topk, sink_pages=sink, q_dtype=q.dtype)
+    dec = QuestDecoder(cache, hq, topk, sink_pages=sink, q_dtype=q.dtype, keep_scores=True)
     out = dec.step(q)
     torch.cuda.synchronize()
     b, hkv, page, d = cache.batch, cache.n_kv_heads, cache.page_size, cache.head_dim
@@ -389,13 +389,13 @@ def _check_decode(cache, table, q, topk, sink, tol):
     vp = _np(cache.v_pool)
     if cache.fp8:
         vp = vp * cache.v_scale.cpu().numpy()[:, :, None, None]
-    mm, mx = _np(cache.meta_min), _np(cache.meta_max)
+    mm, mx = _np(cache.meta_min), _np(cache.meta_max)  # (B, H_kv, max_pages, D), logical pages
     for bi in range(b):
         for p in range(n_b[bi]):
             phys = int(table[bi, p])
             rows = min(page, lens[bi] - p * page)
-            assert np.all(mm[phys] <= kp[phys, :, :rows].min(axis=1))
-            assert np.all(mx[phys] >= kp[phys, :, :rows].max(axis=1))
+            assert np.all(mm[bi, :, p] <= kp[phys, :, :rows].min(axis=1))
+            assert np.all(mx[bi, :, p] >= kp[phys, :, :rows].max(axis=1))
     # union lists + attention over them vs the oracle
     group = hq // hkv
     cnt = dec.union_count.cpu().numpy()[:, :, 0]
