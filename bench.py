@@ -350,7 +350,7 @@ def run_ours(args, rank, world, local_rank):
     kv_bytes = tok * d * 2 * elt  # K and V rows actually read (union tokens)
     qo_bytes = 2 * b * hq * d * elt
     meta_bytes = 2 * b * hkv * (t // p) * d * elt
-    score_bytes = 2 * b * hq * (t // p) * 4  # written by scoring, read by top-k
+    score_bytes = 0 if dec.fused else 2 * b * hq * (t // p) * 4  # the fused selection keeps scores on chip
     step_bytes = kv_bytes + qo_bytes + meta_bytes + score_bytes
     hbm_peak, _, peak_kind = measured_peaks()
     att_bytes = kv_bytes + qo_bytes
