@@ -143,6 +143,40 @@ class PagedKVCache:
         self._sync_lens()
         self.refresh_meta(torch.tensor(first, dtype=torch.int32, device=self.device))
 
+    def fill(self, k: torch.Tensor, v: torch.Tensor, seq_lens, page_table: Optional[torch.Tensor] = None) -> None:
+        """Write whole sequences: ``k, v (B, H_kv, T, D)`` (any float dtype) with
+        ``seq_lens[b] <= T`` valid rows, through ``page_table (B, max_pages)`` (default:
+        sequence b owns physical pages ``[b*max_pages, (b+1)*max_pages)``).  fp8 pools are
+        quantised with one scale per (page, kv head): ``scale = max|x| / 448`` (clamped to
+        1e-8), ``codes = e4m3(x / scale)`` (``src/linattn/kv/quant.py:90-93``).  The page
+        metadata is rebuilt."""
+        L.require_cuda(k, v)
+        b_, hk, t, d = k.shape
+        p = self.page_size
+        if (b_, hk, d) != (self.batch, self.n_kv_heads, self.head_dim) or t > self.max_pages * p:
+            raise ValueError("fill shape mismatch")
+        if page_table is None:
+            page_table = torch.arange(self.batch * self.max_pages, dtype=torch.int32).view(self.batch, self.max_pages)
+        n = -(-t // p)
+        pad = n * p - t
+        kp = torch.nn.functional.pad(k.float(), (0, 0, 0, pad)).view(b_, hk, n, p, d).transpose(1, 2)
+        vp = torch.nn.functional.pad(v.float(), (0, 0, 0, pad)).view(b_, hk, n, p, d).transpose(1, 2)
+        phys = page_table[:, :n].to(self.device).long().reshape(-1)
+        kp = kp.reshape(-1, hk, p, d)
+        vp = vp.reshape(-1, hk, p, d)
+        if self.fp8:
+            for src, pool, sc in ((kp, self.k_pool, self.k_scale), (vp, self.v_pool, self.v_scale)):
+                amax = src.abs().amax(dim=(2, 3)).clamp_min(1e-8)
+                scale = amax / torch.full_like(amax, 448.0)  # true division, not * (1/448)
+                codes = (src / scale[:, :, None, None]).to(torch.float8_e4m3fn).view(torch.uint8)
+                pool[phys] = codes
+                sc[phys] = scale
+        else:
+            self.k_pool[phys] = kp.to(self.k_pool.dtype)
+            self.v_pool[phys] = vp.to(self.v_pool.dtype)
+        self.set_page_table(page_table, seq_lens)
+        self.refresh_meta()
+
     def refresh_meta(self, first_page: Optional[torch.Tensor] = None) -> None:
         """Recompute page bounds for pages ``[first_page[b], n_pages_b)`` (all if None)."""
         status = L.status_word(self.device)

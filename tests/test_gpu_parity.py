@@ -534,3 +534,59 @@ def test_rows_past_sequence_end_are_never_used(cuda, dtype):
                                         block_size=bs)
     assert torch.isfinite(out).all()
     assert_close_16(out, ref)
+
+
+def test_quest_decode_fp8_kv(cuda):
+    """Config-5 storage: fp8 e4m3 KV with one fp32 scale per (page, kv head), GQA 8.
+    Output within 1e-2 of the fp32 oracle on the dequantised KV with the kernel's own
+    selection; the quantisation error against the unquantised KV is only reported."""
+    from linattn_b200 import PagedKVCache, QuestDecoder
+    from oracle.quant import dequantize_fp8, quantize_fp8
+
+    gen = torch.Generator().manual_seed(55)
+    b, hq, hkv, d, page, t, topk = 2, 16, 2, 128, 64, 64 * 48, 12
+    k = torch.randn(b, hkv, t, d, generator=gen)
+    v = torch.randn(b, hkv, t, d, generator=gen)
+    q = torch.randn(b, hq, 1, d, generator=gen).to(torch.bfloat16)
+    cache = PagedKVCache(b, hkv, d, page, t // page, dtype=torch.float8_e4m3fn, device="cuda")
+    table = torch.randperm(b * (t // page), generator=gen).view(b, t // page).to(torch.int32)
+    lens = [t, t - 77]
+    cache.fill(k.to(cuda), v.to(cuda), lens, table)
+    dec = QuestDecoder(cache, hq, topk, sink_pages=1, keep_scores=True)
+    out = dec.step(q.to(cuda))
+    torch.cuda.synchronize()
+    # codec parity: the kernel-side pool equals the oracle codec (kv/quant.py) per page and head
+    kp = k.view(b, hkv, t // page, page, d).transpose(1, 2).numpy()
+    codes, scale = quantize_fp8(kp, reduce_axes=(3, 4))
+    got_codes = cache.k_pool[table.long().view(-1)].view(b, t // page, hkv, page, d).cpu().numpy()
+    assert np.array_equal(got_codes, codes)
+    got_scale = cache.k_scale[table.long().view(-1)].view(b, t // page, hkv).cpu().numpy()
+    assert np.array_equal(got_scale, scale.reshape(b, t // page, hkv))
+    kdq = dequantize_fp8(codes, scale)  # (b, n, hkv, P, D)
+    vcodes, vscale = quantize_fp8(v.view(b, hkv, t // page, page, d).transpose(1, 2).numpy(), reduce_axes=(3, 4))
+    vdq = dequantize_fp8(vcodes, vscale)
+    n_phys = b * (t // page)
+    kpool = np.zeros((n_phys, hkv, page, d), np.float32)
+    vpool = np.zeros_like(kpool)
+    for bi in range(b):
+        for pg in range(t // page):
+            kpool[table[bi, pg]] = kdq[bi, pg]
+            vpool[table[bi, pg]] = vdq[bi, pg]
+    cnt = dec.union_count.cpu().numpy()[:, :, 0]
+    uids = dec.union_ids.cpu().numpy()[:, :, 0]
+    ref = oracle.paged_sparse_decode(_np(q)[:, :, 0], kpool, vpool, table.numpy(), np.array(lens), uids, cnt,
+                                     page_size=page)
+    assert_close_16(out[:, :, 0], ref, tol=1e-2)
+    # metadata bounds the dequantised keys (rounded outward to bf16)
+    mm, mx = _np(cache.meta_min), _np(cache.meta_max)
+    for bi in range(b):
+        for pg in range(-(-lens[bi] // page)):
+            rows = min(page, lens[bi] - pg * page)
+            assert np.all(mm[bi, :, pg] <= kdq[bi, pg, :, :rows].min(axis=1))
+            assert np.all(mx[bi, :, pg] >= kdq[bi, pg, :, :rows].max(axis=1))
+    # selection bit-exact on the kernel's own scores
+    scores = dec.scores.cpu().numpy().astype(np.float64)
+    ids = dec.ids.cpu().numpy()
+    for bi in range(b):
+        nb = -(-lens[bi] // page)
+        assert np.array_equal(ids[bi, :, :, :topk], oracle.topk_lowest_index(scores[bi, :, :, :nb], topk))
