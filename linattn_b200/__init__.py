@@ -1,7 +1,8 @@
 """linattn_b200: the sparse-attention hot path of tongxin/linattn on NVIDIA B200 (sm_100a).
 
 Operators (same names and semantics as ``linattn.kernels.triton.*``):
-``page_bounds``, ``page_select``, ``block_sparse_attention``, ``lse_combine``.
+``page_bounds``, ``page_select``, ``block_sparse_attention``, ``indexer_topk``,
+``lse_combine``.
 Plugin: ``build("cuda_quest", cfg)`` returns an ``AttentionVariant`` like
 ``linattn.registry.build``.  Serving path: ``PagedKVCache`` + ``QuestDecoder``.
 
@@ -11,6 +12,7 @@ ABI of ``include/linattn_b200.h``; there is no CPU fallback.
 
 from linattn_b200.block_sparse import block_sparse_attention, sparse_attention  # noqa: F401
 from linattn_b200.core import AttnConfig, AttentionVariant  # noqa: F401
+from linattn_b200.indexer import indexer_scores, indexer_topk, quantize_keys_fp8  # noqa: F401
 from linattn_b200.merge import lse_combine  # noqa: F401
 from linattn_b200.paged import PagedKVCache, QuestDecoder  # noqa: F401
 from linattn_b200.quest_pages import page_bounds, page_select, quest_select  # noqa: F401
