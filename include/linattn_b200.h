@@ -248,8 +248,13 @@ int64_t linattn_sparse_attention_noalloc_limit(void);
  * scores[(b * (t_end - t_begin) + t - t_begin) * row_stride + s] for s < Tk.
  * q_idx (B, Tq, H_I, D), k_idx (B, Tk, H_I, D), head_weights (B, Tq, H_I), element
  * strides.  fp8 e4m3 keys carry one fp32 scale per `scale_group` tokens
- * (k_scale[b * scale_batch_stride + s / scale_group]).  With `causal`, keys after
- * offset + t score -inf.  H_I * D <= 512.
+ * (k_scale[b * scale_batch_stride + s / scale_group]).  causal = 1: keys after
+ * offset + t score -inf; causal = 2: the same inside each 64-key tile that holds a
+ * visible key, while tiles after every query of a 64-query block are left unwritten
+ * (for a causal top-k, which never reads them).  H_I * D <= 512.  16-bit queries
+ * with fp8 keys (or keys of the query's type), D in {32, 64, 128}, H_I * D <= 256 and
+ * contiguous (B, T_k, H_I, D) keys run on the tensor cores.  status: device
+ * status word (LINATTN_DEV_TIMEOUT if a tile copy never arrives), may be NULL.
  * Replaces indexer_scores_torch (src/linattn/kernels/triton/fused_indexer.py:52-60) and
  * the score pass of _indexer_block_max_kernel / _indexer_gather_kernel (:80-171).
  */
@@ -259,13 +264,13 @@ int linattn_indexer_scores(const void* q_idx, int32_t q_dtype, const int64_t* q_
                            const void* head_weights, int32_t w_dtype, const int64_t* w_strides /*[3]*/,
                            int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D, int32_t causal,
                            int64_t offset, int64_t t_begin, int64_t t_end, float* scores, int64_t row_stride,
-                           void* stream);
+                           int32_t* status, void* stream);
 
 /*
- * Top-k of each of `rows` fp32 rows of n scores (row r at scores + r * row_stride):
- * values descending and indices (int64 and/or int32) with the lowest index first among
- * equal values, k of each written at (r / period) * out_batch_stride + (r % period) *
- * out_stride.  With `causal`, row r only considers its first
+ * Top-k of each of `rows` fp32 rows of n scores (row r at scores + r * row_stride),
+ * ties at the k-th value going to the lowest indices, k of each written at
+ * (r / period) * out_batch_stride + (r % period) * out_stride: with `sorted`, values
+ * descending (lowest index first among equal values); else in ascending index order.  With `causal`, row r only considers its first
  * min(n, first_pos + r % period + 1) entries and pads the remaining slots with
  * (-inf, -1).  k <= 4096; rows of up to 32768 entries are staged in shared memory.
  * Replaces the torch.topk of indexer_topk_torch
@@ -273,8 +278,9 @@ int linattn_indexer_scores(const void* q_idx, int32_t q_dtype, const int64_t* q_
  * (src/linattn/variants/selection.py:744-749).
  */
 int linattn_row_topk(const float* scores, int64_t rows, int64_t n, int64_t row_stride, int64_t k,
-                     int32_t causal, int64_t first_pos, int64_t period, float* values, int64_t* idx_i64,
-                     int32_t* idx_i32, int64_t out_stride, int64_t out_batch_stride, void* stream);
+                     int32_t causal, int64_t first_pos, int64_t period, int32_t sorted, float* values,
+                     int64_t* idx_i64, int32_t* idx_i32, int64_t out_stride, int64_t out_batch_stride,
+                     void* stream);
 
 #ifdef __cplusplus
 }

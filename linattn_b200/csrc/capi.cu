@@ -111,62 +111,11 @@ int check_kv(const linattn_kv_t* kv) {
 }
 
 // ---- TMA tensor maps over the [rows, D] view of a 16-bit K or V pool --------------
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  });
-  return fn;
-}
-
-struct TmapEntry {
-  const void* base;
-  int64_t rows;
-  int d, dtype, box_rows;
-  bool used;
-  CUtensorMap map;
-};
-std::mutex g_tmap_mu;
-TmapEntry g_tmaps[32];
-int g_tmap_next = 0;
-
-// 2-D map {D, rows} with 64 x box_rows boxes and 128-byte swizzle; a map only encodes
-// these values, so a cached one is valid whenever they match.
+// 2-D map {D, rows} with 64 x box_rows boxes and 128-byte swizzle.
 bool kv_tensor_map(CUtensorMap* out, const void* base, int64_t rows, int d, int dtype, int box_rows) {
-  std::lock_guard<std::mutex> lock(g_tmap_mu);
-  for (const TmapEntry& e : g_tmaps)
-    if (e.used && e.base == base && e.rows == rows && e.d == d && e.dtype == dtype && e.box_rows == box_rows) {
-      *out = e.map;
-      return true;
-    }
-  PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
-  if (!fn) return false;
-  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(rows)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(d) * 2};
-  const cuuint32_t box[2] = {64u, static_cast<cuuint32_t>(box_rows)};
-  const cuuint32_t elem_strides[2] = {1u, 1u};
-  TmapEntry& e = g_tmaps[g_tmap_next];
-  const CUresult r = fn(&e.map, dtype == LINATTN_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                        2, const_cast<void*>(base), dims, strides, box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) {
-    e.used = false;
-    return false;
-  }
-  e.base = base;
-  e.rows = rows;
-  e.d = d;
-  e.dtype = dtype;
-  e.box_rows = box_rows;
-  e.used = true;
-  *out = e.map;
-  g_tmap_next = (g_tmap_next + 1) % 32;
-  return true;
+  return tensor_map_2d(out, base, dtype == LINATTN_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                        : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                       d, rows, static_cast<int64_t>(d) * 2, 64, box_rows);
 }
 
 }  // namespace

@@ -150,8 +150,279 @@ struct RowTopkParams {
   int64_t* idx64;
   int32_t* idx32;
   int64_t out_stride, out_bstride;
+  int sorted;  // 1: by (value desc, index asc); 0: ascending index
 };
 
+// Rows of up to NT * ITEMS entries: each thread keeps ITEMS order-preserving keys in
+// registers (entry i = it * NT + tid).  The first digit is one of 4096 bins linear in
+// the value over the row's finite range (monotone in the key, so it is a valid radix
+// digit, and it spreads the shared-memory atomics); 12-bit digits of the key relative
+// to the chosen bin's smallest key follow, for entries of that bin only.
+template <int NT, int ITEMS>
+__global__ void __launch_bounds__(NT, 1024 / NT) row_topk_reg_kernel(const RowTopkParams p) {
+  constexpr int BPT = 4096 / NT;  // first-pass bins per thread
+  extern __shared__ uint32_t rsm[];  // sorted: keys[kpow2] + idx[kpow2]; index order: bitmap
+  __shared__ uint32_t hist[4096];
+  __shared__ uint32_t scratch[NT / 32 + 1];
+  __shared__ uint32_t sh_min[NT / 32], sh_max[NT / 32];
+  __shared__ uint32_t sh_digit, sh_remaining, sh_bin_count, sh_count;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t r = blockIdx.x;
+  const int64_t seg = r / p.period, j = r % p.period;
+  const int nv = static_cast<int>(p.causal ? lmax(0, lmin(p.n, p.first_pos + j + 1)) : p.n);
+  const int64_t ob = seg * p.out_bstride + j * p.out_stride;
+  const int kb = static_cast<int>(lmin(p.k, nv));
+  const float* row = p.scores + r * p.row_stride;
+
+  uint32_t u[ITEMS];
+  // range of the finite entries, as order-preserving keys (for the first digit)
+  uint32_t fmin_k = 0xffffffffu, fmax_k = 0u;
+  const int my_n = nv > tid ? (nv - tid + NT - 1) / NT : 0;  // entries it < my_n are valid
+#pragma unroll
+  for (int it = 0; it < ITEMS; ++it) {
+    const float f = it < my_n ? __ldg(row + it * NT + tid) : 0.f;
+    u[it] = float_key(f);
+    if (it < my_n && isfinite(f)) {
+      fmin_k = min(fmin_k, u[it]);
+      fmax_k = max(fmax_k, u[it]);
+    }
+  }
+  // block-wide min / max of two keys (all threads get the result)
+  auto block_min_max = [&](uint32_t& mn, uint32_t& mx) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+      mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+    if (lane == 0) {
+      sh_min[warp] = mn;
+      sh_max[warp] = mx;
+    }
+    __syncthreads();
+    mn = sh_min[0];
+    mx = sh_max[0];
+#pragma unroll
+    for (int w = 1; w < NT / 32; ++w) {
+      mn = min(mn, sh_min[w]);
+      mx = max(mx, sh_max[w]);
+    }
+    __syncthreads();
+  };
+  // k-th largest digit over hist[0..4095] (descending): digit, count still needed in
+  // it, and its population
+  auto find_digit = [&](uint32_t remaining) {
+    uint32_t cnt[BPT], loc = 0u;
+#pragma unroll
+    for (int e = 0; e < BPT; ++e) {
+      cnt[e] = hist[4095 - BPT * tid - e];
+      loc += cnt[e];
+    }
+    uint32_t above = block_exclusive_scan<NT>(loc, scratch, nullptr);
+    if (above < remaining && above + loc >= remaining) {
+#pragma unroll
+      for (int e = 0; e < BPT; ++e) {
+        if (above < remaining && above + cnt[e] >= remaining) {
+          sh_digit = static_cast<uint32_t>(4095 - BPT * tid - e);
+          sh_remaining = remaining - above;
+          sh_bin_count = cnt[e];
+        }
+        above += cnt[e];
+      }
+    }
+    __syncthreads();
+  };
+  if (tid == 0) sh_count = 0u;
+  uint32_t kstar = 0u, need_eq = 0u, eq_total = 0u;
+  if (kb > 0 && kb < nv) {
+    block_min_max(fmin_k, fmax_k);
+    // first digit: 4096 bins linear in the value over the finite range (monotone in
+    // the key; non-finite entries go to the end bins)
+    const bool any_finite = fmin_k <= fmax_k;
+    const float lo = key_float(fmin_k), span = key_float(fmax_k) - lo;
+    const bool linear = any_finite && span > 0.f && isfinite(span);
+    const float bscale = linear ? 4096.f / span : 0.f;
+    auto bin_of = [&](uint32_t key) -> uint32_t {
+      if (!any_finite) return key >> 20;
+      if (key < fmin_k) return 0u;
+      if (key > fmax_k) return 4095u;
+      if (!linear) return 0u;
+      return static_cast<uint32_t>(min(static_cast<int>((key_float(key) - lo) * bscale), 4095));
+    };
+    for (int i = tid; i < 4096; i += NT) hist[i] = 0u;
+    __syncthreads();
+#pragma unroll
+    for (int it = 0; it < ITEMS; ++it)
+      if (it < my_n) atomicAdd(&hist[bin_of(u[it])], 1u);
+    __syncthreads();
+    find_digit(static_cast<uint32_t>(kb));
+    const uint32_t d1 = sh_digit;
+    uint32_t remaining = sh_remaining;
+    eq_total = sh_bin_count;
+    // entries in that bin, and their key range
+    uint32_t inb = 0u, blo = 0xffffffffu, bhi = 0u;
+#pragma unroll
+    for (int it = 0; it < ITEMS; ++it)
+      if (it < my_n && bin_of(u[it]) == d1) {
+        inb |= 1u << it;
+        blo = min(blo, u[it]);
+        bhi = max(bhi, u[it]);
+      }
+    block_min_max(blo, bhi);
+    // refine inside the bin: 12-bit digits of key - blo, entries with a matching prefix
+    const uint32_t rng = bhi - blo;
+    int bits_left = rng ? 32 - __clz(rng) : 0;
+    uint32_t prefix = 0u;
+    while (bits_left > 0) {
+      const int width = bits_left < 12 ? bits_left : 12;
+      const int shift = bits_left - width;
+      for (int i = tid; i < 4096; i += NT) hist[i] = 0u;
+      __syncthreads();
+#pragma unroll
+      for (int it = 0; it < ITEMS; ++it) {
+        const uint32_t uk = u[it] - blo;
+        if (((inb >> it) & 1u) && (static_cast<uint64_t>(uk) >> (shift + width)) == prefix)
+          atomicAdd(&hist[(uk >> shift) & ((1u << width) - 1u)], 1u);
+      }
+      __syncthreads();
+      find_digit(remaining);
+      prefix = (prefix << width) | sh_digit;
+      remaining = sh_remaining;
+      eq_total = sh_bin_count;
+      bits_left = shift;
+    }
+    kstar = blo + prefix;  // full key of the k-th largest entry
+    need_eq = remaining;
+  }
+  // ---- which entries are taken: key > kstar, or key == kstar among the first need_eq
+  uint64_t take = 0u;
+  if (kb >= nv) {
+#pragma unroll
+    for (int it = 0; it < ITEMS; ++it)
+      if (it < my_n) take |= 1ull << it;
+  } else if (kb > 0) {
+    const bool all_ties = need_eq == eq_total;
+#pragma unroll
+    for (int it = 0; it < ITEMS; ++it)
+      if (it < my_n && (u[it] > kstar || (all_ties && u[it] == kstar))) take |= 1ull << it;
+    if (!all_ties) {
+      // ties at the k-th value go to the lowest indices: select the need_eq-th smallest
+      // index among them by two radix passes over the index (high bits, then low bits)
+      const int lo_bits = nv > 256 ? 32 - __clz(static_cast<uint32_t>(nv - 1)) - 8 : 0;
+      uint32_t want = need_eq, hi = 0u;
+      for (int pass = 0; pass < 2; ++pass) {
+        if (tid < 256) hist[tid] = 0u;
+        __syncthreads();
+#pragma unroll
+        for (int it = 0; it < ITEMS; ++it) {
+          const uint32_t i = static_cast<uint32_t>(it * NT + tid);
+          if (it < my_n && u[it] == kstar) {
+            if (pass == 0) atomicAdd(&hist[i >> lo_bits], 1u);
+            else if ((i >> lo_bits) == hi) atomicAdd(&hist[i & ((1u << lo_bits) - 1u)], 1u);
+          }
+        }
+        __syncthreads();
+        const uint32_t cbin = tid < 256 ? hist[tid] : 0u;
+        const uint32_t before = block_exclusive_scan<NT>(cbin, scratch, nullptr);  // ascending bins
+        if (tid < 256 && before < want && before + cbin >= want) {
+          sh_digit = static_cast<uint32_t>(tid);
+          sh_remaining = want - before;
+        }
+        __syncthreads();
+        if (pass == 0) hi = sh_digit;
+        want = sh_remaining;
+        if (lo_bits == 0) break;
+      }
+      // the last tie taken has index (hi << lo_bits) | low digit
+      const uint32_t last = lo_bits ? ((hi << lo_bits) | sh_digit) : hi;
+#pragma unroll
+      for (int it = 0; it < ITEMS; ++it) {
+        if (it < my_n && u[it] == kstar && static_cast<uint32_t>(it * NT + tid) <= last) take |= 1ull << it;
+      }
+    }
+  }
+  if (p.sorted) {
+    uint32_t* sk = rsm;
+    uint32_t* si = rsm + p.kpow2;
+#pragma unroll
+    for (int it = 0; it < ITEMS; ++it)
+      if ((take >> it) & 1u) {
+        const uint32_t pos = atomicAdd(&sh_count, 1u);
+        if (pos < static_cast<uint32_t>(kb)) {
+          sk[pos] = u[it];
+          si[pos] = static_cast<uint32_t>(it * NT + tid);
+        }
+      }
+    __syncthreads();
+    for (int64_t i = kb + tid; i < p.kpow2; i += NT) {
+      sk[i] = 0u;
+      si[i] = 0xffffffffu;
+    }
+    __syncthreads();
+    for (int64_t size = 2; size <= p.kpow2; size <<= 1) {
+      for (int64_t stride = size >> 1; stride > 0; stride >>= 1) {
+        for (int64_t i = tid; i < p.kpow2; i += NT) {
+          const int64_t jj = i ^ stride;
+          if (jj > i) {
+            const bool desc = (i & size) == 0;
+            const uint32_t ka = sk[i], kb2 = sk[jj], ia = si[i], ib = si[jj];
+            const bool a_first = ka > kb2 || (ka == kb2 && ia < ib);
+            if (a_first != desc) {
+              sk[i] = kb2;
+              sk[jj] = ka;
+              si[i] = ib;
+              si[jj] = ia;
+            }
+          }
+        }
+        __syncthreads();
+      }
+    }
+    for (int64_t i = tid; i < p.k; i += NT) {
+      const bool ok = i < kb;
+      if (p.values) p.values[ob + i] = ok ? key_float(sk[i]) : -INFINITY;
+      if (p.idx64) p.idx64[ob + i] = ok ? static_cast<int64_t>(si[i]) : -1;
+      if (p.idx32) p.idx32[ob + i] = ok ? static_cast<int32_t>(si[i]) : -1;
+    }
+  } else {
+    // ascending index: bitmap, then a popcount scan over its words
+    uint32_t* bits = rsm;
+    const int nwords = (nv + 31) >> 5;
+    for (int i = tid; i < nwords; i += NT) bits[i] = 0u;
+    __syncthreads();
+#pragma unroll
+    for (int it = 0; it < ITEMS; ++it)
+      if ((take >> it) & 1u) {
+        const int i = it * NT + tid;
+        atomicOr(&bits[i >> 5], 1u << (i & 31));
+      }
+    __syncthreads();
+    const int per = (nwords + NT - 1) / NT;
+    const int w0 = tid * per, w1 = min(nwords, w0 + per);
+    uint32_t cnt = 0u;
+    for (int w = w0; w < w1; ++w) cnt += __popc(bits[w]);
+    uint32_t pos = block_exclusive_scan<NT>(cnt, scratch, nullptr);
+    for (int w = w0; w < w1; ++w) {
+      uint32_t m = bits[w];
+      while (m) {
+        const int bpos = __ffs(m) - 1;
+        m &= m - 1u;
+        const int i = (w << 5) | bpos;
+        if (p.values) p.values[ob + pos] = __ldg(row + i);
+        if (p.idx64) p.idx64[ob + pos] = i;
+        if (p.idx32) p.idx32[ob + pos] = i;
+        ++pos;
+      }
+    }
+    for (int64_t i = kb + tid; i < p.k; i += NT) {
+      if (p.values) p.values[ob + i] = -INFINITY;
+      if (p.idx64) p.idx64[ob + i] = -1;
+      if (p.idx32) p.idx32[ob + i] = -1;
+    }
+  }
+}
+
+// Rows of any length: keys staged in shared memory up to kSmemKeys entries, re-read
+// from global memory beyond.  Four 8-bit radix passes.
 __global__ void __launch_bounds__(512) row_topk_kernel(const RowTopkParams p) {
   extern __shared__ uint32_t tsm[];
   // rows of up to kSmemKeys entries are staged in shared memory as order-preserving
@@ -235,7 +506,8 @@ __global__ void __launch_bounds__(512) row_topk_kernel(const RowTopkParams p) {
         if (j > i) {
           const bool desc = (i & size) == 0;
           const uint32_t ka = sk[i], kb2 = sk[j], ia = si[i], ib = si[j];
-          const bool a_first = ka > kb2 || (ka == kb2 && ia < ib);  // a belongs before b
+          // a belongs before b: (key desc, index asc), or index asc for index order
+          const bool a_first = p.sorted ? (ka > kb2 || (ka == kb2 && ia < ib)) : ia < ib;
           if (a_first != desc) {
             sk[i] = kb2;
             sk[j] = ka;
@@ -265,7 +537,7 @@ extern "C" int linattn_indexer_scores(const void* q_idx, int32_t q_dtype, const 
                                       const void* head_weights, int32_t w_dtype, const int64_t* w_strides,
                                       int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D, int32_t causal,
                                       int64_t offset, int64_t t_begin, int64_t t_end, float* scores,
-                                      int64_t row_stride, void* stream) {
+                                      int64_t row_stride, int32_t* status, void* stream) {
   if (!q_idx || !k_idx || !head_weights || !scores || !q_strides || !k_strides || !w_strides)
     return set_error(LINATTN_EINVAL, "indexer_scores: NULL pointer");
   const bool qok = q_dtype == LINATTN_F32 || q_dtype == LINATTN_F16 || q_dtype == LINATTN_BF16;
@@ -274,6 +546,7 @@ extern "C" int linattn_indexer_scores(const void* q_idx, int32_t q_dtype, const 
   if (k_dtype == LINATTN_FP8E4M3 && (!k_scale || scale_group < 1))
     return set_error(LINATTN_EINVAL, "indexer_scores: fp8 keys need k_scale and scale_group");
   if (H < 1 || D < 1 || H * D > 512) return set_error(LINATTN_EUNSUPPORTED, "indexer_scores: H * D must be <= 512");
+  if (causal < 0 || causal > 2) return set_error(LINATTN_EINVAL, "indexer_scores: causal must be 0, 1 or 2");
   if (t_begin < 0 || t_end > Tq || t_begin > t_end || row_stride < Tk)
     return set_error(LINATTN_EINVAL, "indexer_scores: bad query range or row stride");
   if (B == 0 || t_end == t_begin || Tk == 0) return LINATTN_OK;
@@ -284,6 +557,19 @@ extern "C" int linattn_indexer_scores(const void* q_idx, int32_t q_dtype, const 
   for (int i = 0; i < 3; ++i) p.ws[i] = w_strides[i];
   p.ss = scale_batch_stride; p.causal = causal; p.offset = offset; p.t_begin = t_begin; p.scores = scores;
   p.row_stride = row_stride;
+  {
+    cudaError_t me = cudaSuccess;
+    if (indexer_scores_mma(q_idx, q_dtype, q_strides, k_idx, k_dtype, k_strides, k_scale, scale_group,
+                           scale_batch_stride, head_weights, w_dtype, w_strides, B, Tq, Tk, H, D, causal, offset,
+                           t_begin, t_end, scores, row_stride, status, static_cast<cudaStream_t>(stream), &me)) {
+      if (me != cudaSuccess) {
+        char msg[256];
+        snprintf(msg, sizeof(msg), "indexer_scores: %s", cudaGetErrorString(me));
+        return set_error(LINATTN_ECUDA, msg);
+      }
+      return LINATTN_OK;
+    }
+  }
   const size_t smem = (static_cast<size_t>(IQ) * H * D + static_cast<size_t>(IK) * (H * D + 1) +
                        static_cast<size_t>(IQ) * H) * sizeof(float);
   dim3 grid(static_cast<unsigned>((Tk + IK - 1) / IK), static_cast<unsigned>((t_end - t_begin + IQ - 1) / IQ),
@@ -312,7 +598,7 @@ extern "C" int linattn_indexer_scores(const void* q_idx, int32_t q_dtype, const 
 }
 
 extern "C" int linattn_row_topk(const float* scores, int64_t rows, int64_t n, int64_t row_stride, int64_t k,
-                                int32_t causal, int64_t first_pos, int64_t period, float* values,
+                                int32_t causal, int64_t first_pos, int64_t period, int32_t sorted, float* values,
                                 int64_t* idx_i64, int32_t* idx_i32, int64_t out_stride, int64_t out_batch_stride,
                                 void* stream) {
   if (!scores) return set_error(LINATTN_EINVAL, "row_topk: scores is NULL");
@@ -320,19 +606,35 @@ extern "C" int linattn_row_topk(const float* scores, int64_t rows, int64_t n, in
   if (k < 1 || k > 4096) return set_error(LINATTN_EUNSUPPORTED, "row_topk: k must be in [1, 4096]");
   if (row_stride < n || out_stride < k || period < 1) return set_error(LINATTN_EINVAL, "row_topk: bad strides");
   if (rows == 0) return LINATTN_OK;
+  if (rows > 0x7fffffff) return set_error(LINATTN_EUNSUPPORTED, "row_topk: too many rows");
   int64_t kp = 1;
   while (kp < k) kp <<= 1;
   RowTopkParams p;
   p.scores = scores; p.rows = rows; p.n = n; p.row_stride = row_stride; p.k = k; p.kpow2 = kp; p.causal = causal;
   p.first_pos = first_pos; p.period = period; p.values = values; p.idx64 = idx_i64; p.idx32 = idx_i32;
-  p.out_stride = out_stride; p.out_bstride = out_batch_stride;
-  const size_t smem = static_cast<size_t>((n <= kSmemKeys ? n : 0) + 2 * kp) * sizeof(uint32_t);
+  p.out_stride = out_stride; p.out_bstride = out_batch_stride; p.sorted = sorted ? 1 : 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaFuncSetAttribute(row_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
-  if (e == cudaSuccess) {
-    row_topk_kernel<<<static_cast<unsigned>(rows), 512, smem, st>>>(p);
-    e = cudaGetLastError();
+  const unsigned grid = static_cast<unsigned>(rows);
+  cudaError_t e = cudaSuccess;
+  if (n <= 32768) {
+    const size_t smem = sorted ? static_cast<size_t>(2 * kp) * sizeof(uint32_t)
+                               : static_cast<size_t>((n + 31) / 32) * sizeof(uint32_t);
+    auto go = [&](auto kernel, int nt) {
+      e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+      if (e == cudaSuccess) kernel<<<grid, nt, smem, st>>>(p);
+      if (e == cudaSuccess) e = cudaGetLastError();
+    };
+    if (n <= 4096) go(row_topk_reg_kernel<512, 8>, 512);
+    else if (n <= 8192) go(row_topk_reg_kernel<512, 16>, 512);
+    else if (n <= 16384) go(row_topk_reg_kernel<1024, 16>, 1024);
+    else go(row_topk_reg_kernel<1024, 32>, 1024);
+  } else {
+    const size_t smem = static_cast<size_t>(2 * kp) * sizeof(uint32_t);
+    e = cudaFuncSetAttribute(row_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e == cudaSuccess) {
+      row_topk_kernel<<<grid, 512, smem, st>>>(p);
+      e = cudaGetLastError();
+    }
   }
   if (e != cudaSuccess) {
     char msg[256];

@@ -51,6 +51,17 @@ cudaError_t launch_sparse_attention_mma_bf16(const AttnParams& p, const CUtensor
 cudaError_t launch_sparse_attention_mma_f16(const AttnParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv,
                                            int box_rows, int D, int* counter, int64_t n_items, cudaStream_t stream);
 int sm_count();
+// Tensor-core indexer scores (indexer_mma.cu); false when the call is not eligible
+// (nothing launched), else *err holds the launch status.
+bool indexer_scores_mma(const void* q, int q_dtype, const int64_t* qs, const void* k, int k_dtype, const int64_t* ks,
+                        const float* k_scale, int64_t group, int64_t ss, const void* w, int w_dtype, const int64_t* ws,
+                        int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D, int causal, int64_t offset,
+                        int64_t t_begin, int64_t t_end, float* scores, int64_t row_stride, int32_t* status,
+                        cudaStream_t st, cudaError_t* err);
+// 2-D TMA tensor map {inner, rows} (row stride in bytes) with box {box_inner, box_rows}
+// and 128-byte swizzle, from a process-wide cache.  False if encoding fails.
+bool tensor_map_2d(CUtensorMap* out, const void* base, CUtensorMapDataType cu_dtype, int64_t inner, int64_t rows,
+                   int64_t stride_bytes, int box_inner, int box_rows);
 int tile_rows_f32(int D);
 int tile_rows_f16(int D);
 int tile_rows_bf16(int D);

@@ -23,7 +23,7 @@ import torch
 
 from linattn_b200 import _lib as L
 
-__all__ = ["indexer_scores", "indexer_topk", "quantize_keys_fp8"]
+__all__ = ["indexer_scores", "indexer_topk", "row_topk", "quantize_keys_fp8"]
 
 _MAX_SCRATCH = 1 << 29  # 512 MiB of fp32 scores per chunk
 
@@ -58,7 +58,7 @@ def _launch_scores(q_idx, k_idx, head_weights, k_scale, scale_group, causal, off
         q_idx.data_ptr(), L.dtype_code(q_idx), L.strides4(q_idx), k_idx.data_ptr(), L.dtype_code(k_idx),
         L.strides4(k_idx), L.ptr(k_scale), scale_group, s, head_weights.data_ptr(), L.dtype_code(head_weights),
         (L.c_i64 * 3)(*head_weights.stride()), b, tq, tk, h, d, int(causal), offset, t0, t1, out.data_ptr(),
-        row_stride, L.stream_of(q_idx)))
+        row_stride, L.status_word(q_idx.device).data_ptr(), L.stream_of(q_idx)))
 
 
 def indexer_scores(q_idx: torch.Tensor, k_idx: torch.Tensor, head_weights: torch.Tensor, *,
@@ -76,10 +76,11 @@ def indexer_scores(q_idx: torch.Tensor, k_idx: torch.Tensor, head_weights: torch
 def indexer_topk(q_idx: torch.Tensor, k_idx: torch.Tensor, head_weights: torch.Tensor, k: int, *,
                  backend: str = "auto", causal: bool = False, offset: int = 0,
                  k_scale: Optional[torch.Tensor] = None, scale_group: int = 64,
-                 index_dtype: torch.dtype = torch.int64,
+                 index_dtype: torch.dtype = torch.int64, sorted: bool = True,
                  max_scratch_bytes: int = _MAX_SCRATCH) -> Tuple[torch.Tensor, torch.Tensor]:
     """Top-``k`` indexer scores per query: ``(values fp32 (B,T_q,k'), indices (B,T_q,k'))``
-    with ``k' = min(k, T_k)`` (``fused_indexer.py:197-206``)."""
+    with ``k' = min(k, T_k)`` (``fused_indexer.py:197-206``).  ``sorted=False`` returns
+    the same set in ascending index order (the order the sparse attention reads it in)."""
     if backend not in ("auto", "cuda"):
         raise ValueError(f"linattn_b200 has one backend ('cuda'); got backend={backend!r}")
     if index_dtype not in (torch.int32, torch.int64):
@@ -98,12 +99,40 @@ def indexer_topk(q_idx: torch.Tensor, k_idx: torch.Tensor, head_weights: torch.T
     i64 = index_dtype == torch.int64
     for t0 in range(0, tq, rows):
         t1 = min(tq, t0 + rows)
-        _launch_scores(q_idx, k_idx, head_weights, k_scale, scale_group, causal, offset, t0, t1, scratch, tk)
+        # causal mode 2: score tiles after every query of a block are never read
+        _launch_scores(q_idx, k_idx, head_weights, k_scale, scale_group, 2 if causal else 0, offset, t0, t1,
+                       scratch, tk)
         v = values[:, t0]
         ix = indices[:, t0]
         L.check(L.lib().linattn_row_topk(
-            scratch.data_ptr(), b * (t1 - t0), tk, tk, kk, int(causal), offset + t0, t1 - t0, v.data_ptr(),
-            ix.data_ptr() if i64 else None, None if i64 else ix.data_ptr(), kk, tq * kk, L.stream_of(q_idx)))
+            scratch.data_ptr(), b * (t1 - t0), tk, tk, kk, int(causal), offset + t0, t1 - t0, int(sorted),
+            v.data_ptr(), ix.data_ptr() if i64 else None, None if i64 else ix.data_ptr(), kk, tq * kk,
+            L.stream_of(q_idx)))
+    if L.strict():
+        L.check_status(dev)
+    return values, indices
+
+
+def row_topk(scores: torch.Tensor, k: int, *, sorted: bool = True, causal: bool = False, first_pos: int = 0,
+             index_dtype: torch.dtype = torch.int64) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Top-``k`` of each row of a 2-D fp32 ``scores`` (``torch.topk(scores, k, dim=-1)`` with
+    the lowest index first among equal values).  ``sorted=False`` gives the same set in
+    ascending index order.  ``causal``: row ``r`` only considers its first
+    ``first_pos + r + 1`` entries; slots past that count hold (-inf, -1)."""
+    L.require_cuda(scores)
+    if scores.dim() != 2 or scores.dtype != torch.float32 or scores.stride(1) != 1:
+        raise ValueError("scores must be a 2-D fp32 tensor with unit stride on the last axis")
+    rows, n = scores.shape
+    kk = min(int(k), n)
+    values = torch.empty(rows, kk, dtype=torch.float32, device=scores.device)
+    indices = torch.empty(rows, kk, dtype=index_dtype, device=scores.device)
+    if values.numel() == 0:
+        return values, indices
+    i64 = index_dtype == torch.int64
+    L.check(L.lib().linattn_row_topk(
+        scores.data_ptr(), rows, n, scores.stride(0), kk, int(causal), first_pos, max(rows, 1), int(sorted),
+        values.data_ptr(), indices.data_ptr() if i64 else None, None if i64 else indices.data_ptr(), kk, 0,
+        L.stream_of(scores)))
     return values, indices
 
 

@@ -173,3 +173,92 @@ def test_indexer_rejects_bad_arguments(cuda):
         indexer_topk(q.to(cuda), kk_.to(cuda).to(torch.float8_e4m3fn), w.to(cuda), 4)  # no scales
     with pytest.raises(NotImplementedError):
         indexer_topk(q.to(cuda), kk_.to(cuda), w.to(cuda), 4097)  # k above 4096
+
+
+@pytest.mark.parametrize("n", [300, 4096, 5000, 16384, 20000, 32768, 40000])
+@pytest.mark.parametrize("k", [1, 17, 2048])
+def test_row_topk_ties_and_orders(cuda, n, k):
+    """Rows with heavy ties (values from a small set): the k-th value's ties go to the
+    lowest indices, in value order and in index order, against the oracle."""
+    from linattn_b200 import row_topk
+
+    g = torch.Generator().manual_seed(n + k)
+    rows = 6
+    s = torch.randint(0, 7, (rows, n), generator=g).float() * 0.25 - 0.5
+    s[1] = 0.0                                   # one value everywhere
+    s[2] = torch.randn(n, generator=g)           # no ties
+    s[3, : n // 2] = float("-inf")               # -inf entries
+    sd = s.to(cuda)
+    kk = min(k, n)
+    ref_idx = topk_lowest_index(s.numpy().astype(np.float64), kk)
+    ref_val = np.take_along_axis(s.numpy(), ref_idx, -1)
+    v, i = row_topk(sd, k)
+    assert np.array_equal(i.cpu().numpy(), ref_idx)
+    assert np.array_equal(v.cpu().numpy(), ref_val)
+    v2, i2 = row_topk(sd, k, sorted=False, index_dtype=torch.int32)
+    srt = np.sort(ref_idx, -1)
+    assert np.array_equal(i2.cpu().numpy(), srt)
+    assert np.array_equal(v2.cpu().numpy(), np.take_along_axis(s.numpy(), srt, -1))
+
+
+def test_row_topk_causal_index_order(cuda):
+    from linattn_b200 import row_topk
+
+    g = torch.Generator().manual_seed(4)
+    rows, n, k = 40, 3000, 64
+    s = torch.randint(0, 3, (rows, n), generator=g).float()
+    v, i = row_topk(s.to(cuda), k, sorted=False, causal=True, first_pos=20)
+    for r in range(rows):
+        nv = min(n, 20 + r + 1)
+        sel = topk_lowest_index(s[r:r + 1, :nv].numpy().astype(np.float64), min(k, nv))[0]
+        exp = np.full(k, -1)
+        exp[: len(sel)] = np.sort(sel)
+        assert np.array_equal(i[r].cpu().numpy(), exp)
+        assert torch.all(torch.isneginf(v[r, len(sel):]))
+
+
+def test_indexer_zero_weights_all_ties(cuda):
+    """All scores exactly 0: the first k keys, in both orders (and causal padding)."""
+    from linattn_b200 import indexer_topk
+
+    q, kk_, w = _inputs(1, 100, 5000, 4, 64, seed=8, dtype=torch.bfloat16)
+    w = torch.zeros_like(w)
+    v, i = indexer_topk(q.to(cuda), kk_.to(cuda), w.to(cuda), 300)
+    assert torch.equal(i[0].cpu(), torch.arange(300).expand(100, 300))
+    v2, i2 = indexer_topk(q.to(cuda), kk_.to(cuda), w.to(cuda), 300, sorted=False, causal=True, offset=250)
+    for t in (0, 10, 99):
+        nv = min(300, 250 + t + 1)
+        assert torch.equal(i2[0, t, :nv].cpu(), torch.arange(nv))
+        assert torch.all(i2[0, t, nv:] == -1)
+
+
+@pytest.mark.parametrize("h,d,kdt", [(2, 128, torch.bfloat16), (8, 32, "fp8"), (1, 64, torch.float16),
+                                     (4, 32, torch.bfloat16), (2, 64, "fp8")])
+@pytest.mark.parametrize("tk", [333, 1024])
+def test_indexer_tensor_core_shapes(cuda, h, d, kdt, tk):
+    """Every tensor-core instantiation class, ragged T_k (odd row stride), B = 2, causal."""
+    from linattn_b200 import indexer_scores, indexer_topk, quantize_keys_fp8
+
+    b, tq, k = 2, 70, 40
+    qdt = torch.float16 if kdt == torch.float16 else torch.bfloat16
+    q, kk_, w = _inputs(b, tq, tk, h, d, seed=h * d + tk, dtype=qdt)
+    qd, wd = q.to(cuda), w.to(cuda)
+    if kdt == "fp8":
+        kd, sc = quantize_keys_fp8(kk_.to(cuda), 64)
+        kref = oracle.e4m3_decode(kd.view(torch.uint8).cpu().numpy()).astype(np.float64)
+        scn = sc.cpu().numpy()
+    else:
+        kd, sc = kk_.to(kdt).to(cuda), None
+        kref, scn = _np(kd), None
+    off = tk - tq
+    s = indexer_scores(qd, kd, wd, k_scale=sc, causal=True, offset=off)
+    ref = oracle.indexer_scores(_np(q), kref, _np(w), k_scale=scn, group=64)
+    allow = np.arange(tk)[None, :] <= (np.arange(tq)[:, None] + off)
+    got = _np(s)
+    assert np.all(np.isneginf(got[:, ~allow]))
+    assert np.abs(got[:, allow] - ref[:, allow]).max() <= 2e-6 * (np.abs(ref).max() + 1e-6) * max(1, h * d / 64)
+    vals, idx = indexer_topk(qd, kd, wd, k, k_scale=sc, causal=True, offset=off)
+    _check_selection_on_own_scores(s, vals, idx, k, causal=True, offset=off)
+    _, idx_u = indexer_topk(qd, kd, wd, k, k_scale=sc, causal=True, offset=off, sorted=False)
+    srt = np.sort(np.where(idx.cpu().numpy() < 0, 1 << 40, idx.cpu().numpy()), -1)
+    assert np.array_equal(np.where(srt == 1 << 40, -1, srt), idx_u.cpu().numpy())
