@@ -248,8 +248,10 @@ int64_t linattn_sparse_attention_noalloc_limit(void);
  * scores[(b * (t_end - t_begin) + t - t_begin) * row_stride + s] for s < Tk.
  * q_idx (B, Tq, H_I, D), k_idx (B, Tk, H_I, D), head_weights (B, Tq, H_I), element
  * strides.  fp8 e4m3 keys carry one fp32 scale per `scale_group` tokens
- * (k_scale[b * scale_batch_stride + s / scale_group]).  causal = 1: keys after
- * offset + t score -inf; causal = 2: the same inside each 64-key tile that holds a
+ * (k_scale[b * scale_batch_stride + s / scale_group]).  Key s covers positions
+ * [s * key_block, (s + 1) * key_block) (1 for tokens; the pooling ratio for pooled
+ * groups) and is visible from query t iff s * key_block <= offset + t.  causal = 1:
+ * invisible keys score -inf; causal = 2: the same inside each 64-key tile that holds a
  * visible key, while tiles after every query of a 64-query block are left unwritten
  * (for a causal top-k, which never reads them).  H_I * D <= 512.  16-bit queries
  * with fp8 keys (or keys of the query's type), D in {32, 64, 128}, H_I * D <= 256 and
@@ -263,24 +265,52 @@ int linattn_indexer_scores(const void* q_idx, int32_t q_dtype, const int64_t* q_
                            const float* k_scale, int64_t scale_group, int64_t scale_batch_stride,
                            const void* head_weights, int32_t w_dtype, const int64_t* w_strides /*[3]*/,
                            int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D, int32_t causal,
-                           int64_t offset, int64_t t_begin, int64_t t_end, float* scores, int64_t row_stride,
+                           int64_t offset, int64_t key_block, int64_t t_begin, int64_t t_end, float* scores,
+                           int64_t row_stride,
                            int32_t* status, void* stream);
 
 /*
  * Top-k of each of `rows` fp32 rows of n scores (row r at scores + r * row_stride),
  * ties at the k-th value going to the lowest indices, k of each written at
  * (r / period) * out_batch_stride + (r % period) * out_stride: with `sorted`, values
- * descending (lowest index first among equal values); else in ascending index order.  With `causal`, row r only considers its first
- * min(n, first_pos + r % period + 1) entries and pads the remaining slots with
- * (-inf, -1).  k <= 4096; rows of up to 32768 entries are staged in shared memory.
+ * descending (lowest index first among equal values); else in ascending index order.
+ * With `causal`, row r only considers its first
+ * min(n, (first_pos + r % period) / key_block + 1) entries and pads the remaining
+ * slots with (-inf, -1).  k <= 4096; rows of up to 32768 entries stay in registers,
+ * longer ones are re-read from global memory.
  * Replaces the torch.topk of indexer_topk_torch
  * (src/linattn/kernels/triton/fused_indexer.py:63-73) and of DSAAttention.select
  * (src/linattn/variants/selection.py:744-749).
  */
 int linattn_row_topk(const float* scores, int64_t rows, int64_t n, int64_t row_stride, int64_t k,
-                     int32_t causal, int64_t first_pos, int64_t period, int32_t sorted, float* values,
+                     int32_t causal, int64_t first_pos, int64_t key_block, int64_t period, int32_t sorted,
+                     float* values,
                      int64_t* idx_i64, int32_t* idx_i32, int64_t out_stride, int64_t out_batch_stride,
                      void* stream);
+
+/*
+ * Token-sparse attention (DSA / CSA prefill and decode).  Each query (b, h, t) attends
+ * to the union of: the tokens of its list (list head h / (H_q / lists->n_heads); each
+ * entry id stands for tokens [id * block, id * block + block); negative ids are
+ * padding), the first `sink` tokens, and the `window` tokens ending at position
+ * offset + t; restricted to positions < Tk, and <= offset + t when `causal`.  A token
+ * in several of these counts once.  q, out (B, H_q, T_q, D); K, V (B, H_kv, Tk, D)
+ * with element strides kv_strides = {batch, head, token} (rows contiguous, 16-byte
+ * aligned); q / K / V bf16 or f16 (one type), D in {64, 128}.  lse_out (B, H_q, T_q)
+ * and reads_out (B, H_q, T_q, tokens read) optional.  A query with nothing to read
+ * reads token min(offset + t, Tk - 1) with `diag_fallback` (the reference's empty-row
+ * rule, selection.py:100-107), else gets o = 0, lse = -inf.
+ * Replaces the masked attention of BlockSelectionAttention.attend
+ * (src/linattn/variants/selection.py:86-116) for the DSA selection
+ * (DSAAttention.select, :738-763), and block_sparse_attention_torch with block_size 1
+ * (src/linattn/kernels/triton/block_sparse.py:40-75).
+ */
+int linattn_token_attention(const void* q, int32_t dtype, int64_t B, int64_t Hq, int64_t Tq,
+                            const int64_t* q_strides /*[4]*/, const void* k, const void* v, int64_t Hkv, int64_t Tk,
+                            int64_t D, const int64_t* kv_strides /*[3]*/, const linattn_lists_t* lists, int64_t block,
+                            int64_t sink, int64_t window, int32_t causal, int64_t offset, float scale,
+                            int32_t diag_fallback, void* out, const int64_t* out_strides /*[4]*/, float* lse_out,
+                            int32_t* reads_out, int32_t* status, void* stream);
 
 #ifdef __cplusplus
 }

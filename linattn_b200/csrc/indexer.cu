@@ -46,6 +46,7 @@ struct IndexerParams {
   int64_t qs[4], ks[4], ws[3], ss;  // element strides; ss = batch stride of k_scale
   int causal;
   int64_t offset;
+  int64_t kb;       // key s covers positions [s * kb, (s + 1) * kb): visible iff s * kb <= offset + t
   int64_t t_begin;  // first query of this launch; rows of `scores` are t - t_begin
   float* scores;
   int64_t row_stride;
@@ -66,7 +67,7 @@ __global__ void __launch_bounds__(256) indexer_scores_kernel(const IndexerParams
   const int64_t t0 = p.t_begin + static_cast<int64_t>(blockIdx.y) * IQ;
   const int64_t s0 = static_cast<int64_t>(blockIdx.x) * IK;
   const int64_t t_last = lmin(p.Tq, t0 + IQ) - 1;
-  if (p.causal && s0 > p.offset + t_last) {
+  if (p.causal && s0 * p.kb > p.offset + t_last) {
     // whole tile after every query of the block: -inf
     for (int i = tid; i < IQ * IK; i += 256) {
       const int64_t t = t0 + i / IK, s = s0 + i % IK;
@@ -127,7 +128,7 @@ __global__ void __launch_bounds__(256) indexer_scores_kernel(const IndexerParams
       if (s >= p.Tk) continue;
       float v = acc[i][j];
       if (p.k_scale) v *= p.k_scale[b * p.ss + s / p.group];
-      if (p.causal && s > p.offset + t) v = -INFINITY;
+      if (p.causal && s * p.kb > p.offset + t) v = -INFINITY;
       p.scores[(b * (p.Tq - p.t_begin) + t - p.t_begin) * p.row_stride + s] = v;
     }
   }
@@ -138,13 +139,19 @@ __global__ void __launch_bounds__(256) indexer_scores_kernel(const IndexerParams
 // ---------------------------------------------------------------------------------
 constexpr int64_t kSmemKeys = 32768;
 
+// Keys visible from position pos when key s covers [s * kb, (s + 1) * kb): s * kb <= pos.
+__device__ __forceinline__ int64_t visible_keys(int64_t n, int64_t pos, int64_t kb) {
+  return pos < 0 ? 0 : lmin(n, pos / kb + 1);
+}
+
 struct RowTopkParams {
   const float* scores;
   int64_t rows, n, row_stride;
   int64_t k;
   int64_t kpow2;
   int causal;
-  int64_t first_pos;  // causal: row r keeps n_valid = min(n, first_pos + r % period + 1)
+  int64_t first_pos;  // causal: row r keeps n_valid = min(n, (first_pos + r % period) / kb + 1)
+  int64_t kb;
   int64_t period;     // rows per sequence
   float* values;      // row r -> (r / period) * out_bstride + (r % period) * out_stride
   int64_t* idx64;
@@ -169,7 +176,7 @@ __global__ void __launch_bounds__(NT, 1024 / NT) row_topk_reg_kernel(const RowTo
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t r = blockIdx.x;
   const int64_t seg = r / p.period, j = r % p.period;
-  const int nv = static_cast<int>(p.causal ? lmax(0, lmin(p.n, p.first_pos + j + 1)) : p.n);
+  const int nv = static_cast<int>(p.causal ? visible_keys(p.n, p.first_pos + j, p.kb) : p.n);
   const int64_t ob = seg * p.out_bstride + j * p.out_stride;
   const int kb = static_cast<int>(lmin(p.k, nv));
   const float* row = p.scores + r * p.row_stride;
@@ -437,7 +444,7 @@ __global__ void __launch_bounds__(512) row_topk_kernel(const RowTopkParams p) {
   const int tid = threadIdx.x;
   const int64_t r = blockIdx.x;
   const int64_t seg = r / p.period, j = r % p.period;
-  const int64_t nv = p.causal ? lmax(0, lmin(p.n, p.first_pos + j + 1)) : p.n;
+  const int64_t nv = p.causal ? visible_keys(p.n, p.first_pos + j, p.kb) : p.n;
   const int64_t ob = seg * p.out_bstride + j * p.out_stride;
   const int64_t kb = lmin(p.k, nv);
   const float* row = p.scores + r * p.row_stride;
@@ -536,7 +543,7 @@ extern "C" int linattn_indexer_scores(const void* q_idx, int32_t q_dtype, const 
                                       const float* k_scale, int64_t scale_group, int64_t scale_batch_stride,
                                       const void* head_weights, int32_t w_dtype, const int64_t* w_strides,
                                       int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D, int32_t causal,
-                                      int64_t offset, int64_t t_begin, int64_t t_end, float* scores,
+                                      int64_t offset, int64_t key_block, int64_t t_begin, int64_t t_end, float* scores,
                                       int64_t row_stride, int32_t* status, void* stream) {
   if (!q_idx || !k_idx || !head_weights || !scores || !q_strides || !k_strides || !w_strides)
     return set_error(LINATTN_EINVAL, "indexer_scores: NULL pointer");
@@ -547,6 +554,7 @@ extern "C" int linattn_indexer_scores(const void* q_idx, int32_t q_dtype, const 
     return set_error(LINATTN_EINVAL, "indexer_scores: fp8 keys need k_scale and scale_group");
   if (H < 1 || D < 1 || H * D > 512) return set_error(LINATTN_EUNSUPPORTED, "indexer_scores: H * D must be <= 512");
   if (causal < 0 || causal > 2) return set_error(LINATTN_EINVAL, "indexer_scores: causal must be 0, 1 or 2");
+  if (key_block < 1) return set_error(LINATTN_EINVAL, "indexer_scores: key_block must be >= 1");
   if (t_begin < 0 || t_end > Tq || t_begin > t_end || row_stride < Tk)
     return set_error(LINATTN_EINVAL, "indexer_scores: bad query range or row stride");
   if (B == 0 || t_end == t_begin || Tk == 0) return LINATTN_OK;
@@ -555,12 +563,14 @@ extern "C" int linattn_indexer_scores(const void* q_idx, int32_t q_dtype, const 
   p.w = head_weights; p.w_dtype = w_dtype; p.B = B; p.Tq = t_end; p.Tk = Tk; p.H = H; p.D = D;
   for (int i = 0; i < 4; ++i) { p.qs[i] = q_strides[i]; p.ks[i] = k_strides[i]; }
   for (int i = 0; i < 3; ++i) p.ws[i] = w_strides[i];
-  p.ss = scale_batch_stride; p.causal = causal; p.offset = offset; p.t_begin = t_begin; p.scores = scores;
+  p.ss = scale_batch_stride; p.causal = causal; p.offset = offset; p.kb = key_block; p.t_begin = t_begin;
+  p.scores = scores;
   p.row_stride = row_stride;
   {
     cudaError_t me = cudaSuccess;
     if (indexer_scores_mma(q_idx, q_dtype, q_strides, k_idx, k_dtype, k_strides, k_scale, scale_group,
                            scale_batch_stride, head_weights, w_dtype, w_strides, B, Tq, Tk, H, D, causal, offset,
+                           key_block,
                            t_begin, t_end, scores, row_stride, status, static_cast<cudaStream_t>(stream), &me)) {
       if (me != cudaSuccess) {
         char msg[256];
@@ -598,20 +608,22 @@ extern "C" int linattn_indexer_scores(const void* q_idx, int32_t q_dtype, const 
 }
 
 extern "C" int linattn_row_topk(const float* scores, int64_t rows, int64_t n, int64_t row_stride, int64_t k,
-                                int32_t causal, int64_t first_pos, int64_t period, int32_t sorted, float* values,
+                                int32_t causal, int64_t first_pos, int64_t key_block, int64_t period, int32_t sorted,
+                                float* values,
                                 int64_t* idx_i64, int32_t* idx_i32, int64_t out_stride, int64_t out_batch_stride,
                                 void* stream) {
   if (!scores) return set_error(LINATTN_EINVAL, "row_topk: scores is NULL");
   if (n < 1 || n >= (int64_t(1) << 31)) return set_error(LINATTN_EUNSUPPORTED, "row_topk: row length must be in [1, 2^31)");
   if (k < 1 || k > 4096) return set_error(LINATTN_EUNSUPPORTED, "row_topk: k must be in [1, 4096]");
-  if (row_stride < n || out_stride < k || period < 1) return set_error(LINATTN_EINVAL, "row_topk: bad strides");
+  if (row_stride < n || out_stride < k || period < 1 || key_block < 1)
+    return set_error(LINATTN_EINVAL, "row_topk: bad strides or key_block");
   if (rows == 0) return LINATTN_OK;
   if (rows > 0x7fffffff) return set_error(LINATTN_EUNSUPPORTED, "row_topk: too many rows");
   int64_t kp = 1;
   while (kp < k) kp <<= 1;
   RowTopkParams p;
   p.scores = scores; p.rows = rows; p.n = n; p.row_stride = row_stride; p.k = k; p.kpow2 = kp; p.causal = causal;
-  p.first_pos = first_pos; p.period = period; p.values = values; p.idx64 = idx_i64; p.idx32 = idx_i32;
+  p.first_pos = first_pos; p.kb = key_block; p.period = period; p.values = values; p.idx64 = idx_i64; p.idx32 = idx_i32;
   p.out_stride = out_stride; p.out_bstride = out_batch_stride; p.sorted = sorted ? 1 : 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const unsigned grid = static_cast<unsigned>(rows);

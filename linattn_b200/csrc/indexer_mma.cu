@@ -46,7 +46,7 @@ struct IndexerMmaParams {
   int64_t ws[3];
   int64_t Tq, Tk;  // Tq = t_end
   int causal;      // 0: none, 1: mask and write -inf, 2: mask, skip tiles past every query
-  int64_t offset, t_begin;
+  int64_t offset, kb, t_begin;  // key s is visible from t iff s * kb <= offset + t
   float* scores;
   int64_t row_stride;
   int32_t* status;
@@ -104,7 +104,11 @@ __global__ void __launch_bounds__(256, 2)
   const int64_t kt0 = static_cast<int64_t>(blockIdx.x) * XKCT;
   const int64_t kt_chunk_end = lmin(n_tiles_all, kt0 + XKCT);
   int64_t kt_end = kt_chunk_end;
-  if (p.causal) kt_end = lmin(kt_end, (p.offset + t_last) / XK + 1);  // tiles with a visible key
+  if (p.causal) {
+    // tiles with a key visible from the block's last query
+    const int64_t pos = p.offset + t_last;
+    kt_end = pos < 0 ? kt0 : lmin(kt_end, (pos / p.kb) / XK + 1);
+  }
   const int64_t n = lmax(0, kt_end - kt0);
   const int64_t rows_per_b = p.Tq - p.t_begin;
 
@@ -230,7 +234,7 @@ __global__ void __launch_bounds__(256, 2)
     __syncthreads();
     if (tid == 0 && i + XSTG < n) issue(stage, kt0 + i + XSTG);
     // ---- epilogue: key scales, causal mask, store
-    const bool diag = p.causal && s0 + XK - 1 > p.offset + q0;
+    const bool diag = p.causal && (s0 + XK - 1) * p.kb > p.offset + q0;
     float* out0 = p.scores + (b * rows_per_b + r0 - p.t_begin) * p.row_stride;
     float* out1 = out0 + 8 * p.row_stride;
 #pragma unroll
@@ -244,10 +248,10 @@ __global__ void __launch_bounds__(256, 2)
       }
       float o[4] = {tot[nt][0] * sc0, tot[nt][1] * sc1, tot[nt][2] * sc0, tot[nt][3] * sc1};
       if (diag) {
-        if (col > p.offset + r0) o[0] = -INFINITY;
-        if (col + 1 > p.offset + r0) o[1] = -INFINITY;
-        if (col > p.offset + r1) o[2] = -INFINITY;
-        if (col + 1 > p.offset + r1) o[3] = -INFINITY;
+        if (col * p.kb > p.offset + r0) o[0] = -INFINITY;
+        if ((col + 1) * p.kb > p.offset + r0) o[1] = -INFINITY;
+        if (col * p.kb > p.offset + r1) o[2] = -INFINITY;
+        if ((col + 1) * p.kb > p.offset + r1) o[3] = -INFINITY;
       }
       if (col + 1 < p.Tk && (p.row_stride & 1) == 0) {
         if (v0) *reinterpret_cast<float2*>(out0 + col) = make_float2(o[0], o[1]);
@@ -316,7 +320,7 @@ cudaError_t launch_hd(int H, int D, const IndexerMmaParams& p, const CUtensorMap
 bool indexer_scores_mma(const void* q, int q_dtype, const int64_t* qs, const void* k, int k_dtype, const int64_t* ks,
                         const float* k_scale, int64_t group, int64_t ss, const void* w, int w_dtype, const int64_t* ws,
                         int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D, int causal, int64_t offset,
-                        int64_t t_begin, int64_t t_end, float* scores, int64_t row_stride, int32_t* status,
+                        int64_t key_block, int64_t t_begin, int64_t t_end, float* scores, int64_t row_stride, int32_t* status,
                         cudaStream_t st, cudaError_t* err) {
   *err = cudaSuccess;
   if (q_dtype != LINATTN_F16 && q_dtype != LINATTN_BF16) return false;
@@ -340,7 +344,7 @@ bool indexer_scores_mma(const void* q, int q_dtype, const int64_t* qs, const voi
   p.k_scale = fp8 ? k_scale : nullptr; p.group = group > 0 ? group : 1; p.ss = ss;
   p.w = w; p.w_dtype = w_dtype;
   for (int i = 0; i < 3; ++i) p.ws[i] = ws[i];
-  p.Tq = t_end; p.Tk = Tk; p.causal = causal; p.offset = offset; p.t_begin = t_begin;
+  p.Tq = t_end; p.Tk = Tk; p.causal = causal; p.offset = offset; p.kb = key_block; p.t_begin = t_begin;
   p.scores = scores; p.row_stride = row_stride; p.status = status;
   const int64_t n_tiles = (Tk + XK - 1) / XK;
   dim3 grid(static_cast<unsigned>((n_tiles + XKCT - 1) / XKCT), static_cast<unsigned>((t_end - t_begin + XQ - 1) / XQ),

@@ -56,7 +56,7 @@ int sm_count();
 bool indexer_scores_mma(const void* q, int q_dtype, const int64_t* qs, const void* k, int k_dtype, const int64_t* ks,
                         const float* k_scale, int64_t group, int64_t ss, const void* w, int w_dtype, const int64_t* ws,
                         int64_t B, int64_t Tq, int64_t Tk, int64_t H, int64_t D, int causal, int64_t offset,
-                        int64_t t_begin, int64_t t_end, float* scores, int64_t row_stride, int32_t* status,
+                        int64_t key_block, int64_t t_begin, int64_t t_end, float* scores, int64_t row_stride, int32_t* status,
                         cudaStream_t st, cudaError_t* err);
 // 2-D TMA tensor map {inner, rows} (row stride in bytes) with box {box_inner, box_rows}
 // and 128-byte swizzle, from a process-wide cache.  False if encoding fails.

@@ -50,33 +50,36 @@ def _checked(q_idx, k_idx, head_weights, k_scale, scale_group):
     return b, tq, k_idx.shape[1], h, d, fp8
 
 
-def _launch_scores(q_idx, k_idx, head_weights, k_scale, scale_group, causal, offset, t0, t1, out, row_stride):
+def _launch_scores(q_idx, k_idx, head_weights, k_scale, scale_group, causal, offset, t0, t1, out, row_stride,
+                   key_block=1):
     b, tq, h, d = q_idx.shape
     tk = k_idx.shape[1]
     s = k_scale.stride(0) if k_scale is not None else 0
     L.check(L.lib().linattn_indexer_scores(
         q_idx.data_ptr(), L.dtype_code(q_idx), L.strides4(q_idx), k_idx.data_ptr(), L.dtype_code(k_idx),
         L.strides4(k_idx), L.ptr(k_scale), scale_group, s, head_weights.data_ptr(), L.dtype_code(head_weights),
-        (L.c_i64 * 3)(*head_weights.stride()), b, tq, tk, h, d, int(causal), offset, t0, t1, out.data_ptr(),
+        (L.c_i64 * 3)(*head_weights.stride()), b, tq, tk, h, d, int(causal), offset, key_block, t0, t1,
+        out.data_ptr(),
         row_stride, L.status_word(q_idx.device).data_ptr(), L.stream_of(q_idx)))
 
 
 def indexer_scores(q_idx: torch.Tensor, k_idx: torch.Tensor, head_weights: torch.Tensor, *,
                    k_scale: Optional[torch.Tensor] = None, scale_group: int = 64, causal: bool = False,
-                   offset: int = 0) -> torch.Tensor:
-    """``(B,T_q,T_k)`` fp32 indexer scores (``fused_indexer.py:52-60``); -inf at keys
-    after ``offset + t`` when ``causal``."""
+                   offset: int = 0, key_block: int = 1) -> torch.Tensor:
+    """``(B,T_q,T_k)`` fp32 indexer scores (``fused_indexer.py:52-60``); with ``causal``,
+    -inf at keys ``s`` with ``s * key_block > offset + t`` (``key_block`` > 1: keys are
+    pooled groups of that many tokens)."""
     b, tq, tk, _, _, _ = _checked(q_idx, k_idx, head_weights, k_scale, scale_group)
     out = torch.empty(b, tq, tk, dtype=torch.float32, device=q_idx.device)
     if out.numel():
-        _launch_scores(q_idx, k_idx, head_weights, k_scale, scale_group, causal, offset, 0, tq, out, tk)
+        _launch_scores(q_idx, k_idx, head_weights, k_scale, scale_group, causal, offset, 0, tq, out, tk, key_block)
     return out
 
 
 def indexer_topk(q_idx: torch.Tensor, k_idx: torch.Tensor, head_weights: torch.Tensor, k: int, *,
                  backend: str = "auto", causal: bool = False, offset: int = 0,
                  k_scale: Optional[torch.Tensor] = None, scale_group: int = 64,
-                 index_dtype: torch.dtype = torch.int64, sorted: bool = True,
+                 index_dtype: torch.dtype = torch.int64, sorted: bool = True, key_block: int = 1,
                  max_scratch_bytes: int = _MAX_SCRATCH) -> Tuple[torch.Tensor, torch.Tensor]:
     """Top-``k`` indexer scores per query: ``(values fp32 (B,T_q,k'), indices (B,T_q,k'))``
     with ``k' = min(k, T_k)`` (``fused_indexer.py:197-206``).  ``sorted=False`` returns
@@ -101,11 +104,11 @@ def indexer_topk(q_idx: torch.Tensor, k_idx: torch.Tensor, head_weights: torch.T
         t1 = min(tq, t0 + rows)
         # causal mode 2: score tiles after every query of a block are never read
         _launch_scores(q_idx, k_idx, head_weights, k_scale, scale_group, 2 if causal else 0, offset, t0, t1,
-                       scratch, tk)
+                       scratch, tk, key_block)
         v = values[:, t0]
         ix = indices[:, t0]
         L.check(L.lib().linattn_row_topk(
-            scratch.data_ptr(), b * (t1 - t0), tk, tk, kk, int(causal), offset + t0, t1 - t0, int(sorted),
+            scratch.data_ptr(), b * (t1 - t0), tk, tk, kk, int(causal), offset + t0, key_block, t1 - t0, int(sorted),
             v.data_ptr(), ix.data_ptr() if i64 else None, None if i64 else ix.data_ptr(), kk, tq * kk,
             L.stream_of(q_idx)))
     if L.strict():
@@ -130,7 +133,7 @@ def row_topk(scores: torch.Tensor, k: int, *, sorted: bool = True, causal: bool 
         return values, indices
     i64 = index_dtype == torch.int64
     L.check(L.lib().linattn_row_topk(
-        scores.data_ptr(), rows, n, scores.stride(0), kk, int(causal), first_pos, max(rows, 1), int(sorted),
+        scores.data_ptr(), rows, n, scores.stride(0), kk, int(causal), first_pos, 1, max(rows, 1), int(sorted),
         values.data_ptr(), indices.data_ptr() if i64 else None, None if i64 else indices.data_ptr(), kk, 0,
         L.stream_of(scores)))
     return values, indices

@@ -12,11 +12,11 @@ from __future__ import annotations
 from typing import Any, Dict, List
 
 from linattn_b200.core import AttentionVariant
-from linattn_b200.variants import CUDA_SUPPORTED, CudaQuestAttention
+from linattn_b200.variants import CUDA_SUPPORTED, CudaDSAAttention, CudaQuestAttention
 
 __all__ = ["KERNEL_VARIANTS", "build", "build_cuda", "list_kernel_variants", "describe_kernel"]
 
-_CLASSES = {"quest": CudaQuestAttention}
+_CLASSES = {"quest": CudaQuestAttention, "dsa": CudaDSAAttention}
 
 KERNEL_VARIANTS: Dict[str, str] = {f"cuda_{name}": name for name in CUDA_SUPPORTED}
 

@@ -130,6 +130,39 @@ def make_quest_variant(out):
     np.savez_compressed(out / "quest_variant.npz", **rec)
 
 
+def make_dsa_variant(out):
+    import torch
+    from linattn.core import AttnConfig
+    from linattn.harness import structured_inputs
+    from linattn.registry import build
+
+    q, k, v = structured_inputs(1, 4, 192, 32, kv_heads=2, seed=3)
+    rec = {"fn": "DSAAttention", "q": _np(q.float()), "k": _np(k.float()), "v": _np(v.float())}
+    # token-level (compress_ratio 1) and compressed (CSA, ratio 4) selections
+    for label, ratio in (("tok", 1), ("csa", 4)):
+        cfg = AttnConfig(n_heads=4, n_kv_heads=2, head_dim=32, block_size=16, window_size=24, topk_tokens=40,
+                         compress_ratio=ratio, sink_size=2, seed=5)
+        var = build("dsa", cfg)
+        state = var.prepare_state(1, q.device, q.dtype)
+        state = var.push_kv(state, k, v)
+        with torch.no_grad():
+            rec[f"mask_{label}"] = _np(var.effective_mask(q, state, 0))
+            rec[f"scores_{label}"] = _np(var.indexer_scores(q, k if ratio == 1 else _pool(k, ratio)))
+            o64, _ = build("dsa", cfg).forward(q, k, v, chunk=64)
+            o192, _ = build("dsa", cfg).forward(q, k, v, chunk=192)
+            var2 = build("dsa", cfg)
+            var2.forward(q, k, v, chunk=192)
+        rec[f"out64_{label}"] = _np(o64)
+        rec[f"out192_{label}"] = _np(o192)
+        rec[f"reads_{label}"] = var2.stats()["reads_per_query"]
+    np.savez_compressed(out / "dsa_variant.npz", **rec)
+
+
+def _pool(k, m):
+    from linattn.core import block_reduce
+    return block_reduce(k, m, -2)
+
+
 def make_block_sparse(out):
     import torch
     from linattn.kernels.triton.block_sparse import block_sparse_attention_torch
@@ -247,7 +280,7 @@ def main() -> int:
     args = ap.parse_args()
     _import_reference(Path(args.ref))
     for fn in (make_page_bounds, make_page_select, make_topk_ties, make_quest_variant, make_block_sparse,
-               make_indexer, make_dense, make_block_selectors, make_quant, make_paged_decode):
+               make_indexer, make_dense, make_block_selectors, make_quant, make_paged_decode, make_dsa_variant):
         fn(HERE)
         print("wrote", fn.__name__)
     return 0
