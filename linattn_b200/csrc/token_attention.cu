@@ -12,7 +12,8 @@
 // One warp per item = (batch, query, chunk of up to 8 query heads that share a kv
 // head and a list); items are ordered chunk-major so that the warps in flight read
 // one kv head's K / V (L2-resident) at a time.  Per 16-row tile (D = 128; 32 rows for
-// D = 64) the warp resolves the tile's tokens (list ids read two tiles ahead, then
+// D = 64) the warp resolves the tile's tokens (list ids copied three tiles ahead into a
+// per-warp ring, then
 // the sink and window ranges as virtual entries; list ids inside those ranges are
 // dropped) and gathers the K and V rows with zero-filling 16-byte cp.async into a
 // 128-byte-swizzled 3-stage ring, each stage completing on an mbarrier through
@@ -53,10 +54,18 @@ namespace {
 
 constexpr int TNW = 8;   // warps per CTA
 constexpr int TSTG = 3;  // ring stages per warp (8 warps x 3 x 8 KiB = 192 KiB)
+constexpr int TIDR = TSTG + 1;  // list-id ring slots per warp (tiles)
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
   const int sz = valid ? 16 : 0;  // 0: write 16 zero bytes, read nothing
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(sz) : "memory");
+}
+__device__ __forceinline__ void cp_async_small(uint32_t dst, const void* src, int bytes, bool valid) {
+  const int sz = valid ? bytes : 0;
+  if (bytes == 8)
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(dst), "l"(src), "r"(sz) : "memory");
+  else
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(sz) : "memory");
 }
 __device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
@@ -69,13 +78,14 @@ __global__ void __launch_bounds__(32 * TNW, 1) token_attention_kernel(const Toke
   using S = MmaShape<D>;
   using M = MmaOp<T>;
   constexpr int TRW = S::TRW;
-  constexpr int CPR = D / 8;                 // 16-byte chunks per row
-  constexpr int LPR = 32 / TRW;              // lanes per row (2 for D = 128, 1 for D = 64)
-  constexpr int CPL = CPR / LPR;             // chunks per lane per row, for each of K and V
+  constexpr int CPR = D / 8;                 // 16-byte chunks per row = lanes per row in a copy
+  constexpr int RPI = 32 / CPR;              // rows per copy instruction (2 for D = 128, 4 for D = 64)
+  constexpr int NCI = TRW / RPI;             // copy instructions per tile, for each of K and V
   extern __shared__ __align__(128) uint8_t tsmem_raw[];
   uint8_t* smem = tsmem_raw + ((1024 - (smem_u32(tsmem_raw) & 1023)) & 1023);
   __shared__ __align__(8) uint64_t full_bar[TNW][TSTG];
   __shared__ uint32_t stage_rows[TNW][TSTG];
+  __shared__ __align__(8) int64_t id_ring[TNW][TIDR][MmaShape<D>::TRW];  // raw list ids (int32 in the low word)
 
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int64_t item = static_cast<int64_t>(blockIdx.x) * TNW + w;
@@ -112,13 +122,6 @@ __global__ void __launch_bounds__(32 * TNW, 1) token_attention_kernel(const Toke
   const T* kbase = static_cast<const T*>(p.k) + b * p.kv_sb + kvh * p.kv_sh;
   const T* vbase = static_cast<const T*>(p.v) + b * p.kv_sb + kvh * p.kv_sh;
   const int row = lane % TRW, part = lane / TRW;  // this lane's tile row and chunk range
-  // list id behind virtual token e (e < n_lt)
-  auto list_id = [&](int64_t e) -> int64_t {
-    if (e >= n_lt) return -1;
-    const int64_t j = p.block == 1 ? e : e / p.block;
-    return p.lists.ids_dtype == LINATTN_I64 ? static_cast<const int64_t*>(p.lists.ids)[lbase + j]
-                                            : static_cast<int64_t>(static_cast<const int32_t*>(p.lists.ids)[lbase + j]);
-  };
   // token of virtual token e (-1: not read): list tokens, then the sink and window
   // ranges; list tokens inside those ranges are dropped (the union counts them once)
   auto token_of = [&](int64_t e, int64_t id) -> int64_t {
@@ -131,30 +134,60 @@ __global__ void __launch_bounds__(32 * TNW, 1) token_attention_kernel(const Toke
     if (e < ne) return w_lo + (e - n_lt - n_sink);
     return -1;
   };
-  // list ids of this lane's row, two tiles ahead of the next issue
-  int64_t pf0 = list_id(row), pf1 = list_id(TRW + row);
+  const bool ids64 = p.lists.ids_dtype == LINATTN_I64;
+  const int id_bytes = ids64 ? 8 : 4;
+  const char* id_src = static_cast<const char*>(p.lists.ids) + lbase * id_bytes;
+  // list ids of tile k's rows (lane r < TRW: row r) -> id-ring slot k % TIDR.  With
+  // `async`, a cp.async completing with the stage copies of the issuing tile.
+  auto fetch_ids = [&](int64_t k, bool async) {
+    if (lane >= TRW) return;
+    const int64_t e = k * TRW + lane;
+    const bool ok = e < n_lt;
+    const int64_t j = !ok ? 0 : (p.block == 1 ? e : e / p.block);
+    int64_t* slot = &id_ring[w][k % TIDR][lane];
+    if (async) {
+      cp_async_small(smem_u32(slot), id_src + j * id_bytes, id_bytes, ok);
+    } else {
+      *slot = !ok ? 0 : (ids64 ? reinterpret_cast<const int64_t*>(id_src)[j]
+                               : static_cast<int64_t>(reinterpret_cast<const int32_t*>(id_src)[j]));
+    }
+  };
+  for (int64_t k = 0; k < TSTG; ++k) fetch_ids(k, false);
+  __syncwarp();
 
   int64_t produced = 0;
   auto issue = [&]() {
     const int s = static_cast<int>(produced % TSTG);
-    const int64_t e = produced * TRW + row;
-    int64_t tok = token_of(e, pf0);
-    if (produced == n_tiles)  // the fallback tile: the diagonal token alone
-      tok = (row == 0 && pos >= 0 && p.Tk > 0) ? lmin(pos, p.Tk - 1) : -1;
-    pf0 = pf1;
-    pf1 = list_id(e + 2 * TRW);
-    const bool valid = tok >= 0;
+    // this lane's row token (lanes < TRW); the tile's ids arrived TSTG tiles ago
+    int32_t tok = -1;
+    if (lane < TRW) {
+      const int64_t e = produced * TRW + lane;
+      int64_t id = -1;
+      if (e < n_lt) {
+        const int64_t raw = id_ring[w][produced % TIDR][lane];
+        id = ids64 ? raw : static_cast<int64_t>(static_cast<int32_t>(raw & 0xffffffffll));
+      }
+      int64_t t64 = token_of(e, id);
+      if (produced == n_tiles)  // the fallback tile: the diagonal token alone
+        t64 = (lane == 0 && pos >= 0 && p.Tk > 0) ? lmin(pos, p.Tk - 1) : -1;
+      tok = static_cast<int32_t>(t64);
+    }
+    __syncwarp();
+    // ids of tile produced + TSTG, into the slot freed by tile produced - 1
+    fetch_ids(produced + TSTG, true);
     const uint32_t kdst = smem_u32(ring + static_cast<size_t>(s) * S::STAGE_BYTES);
     const uint32_t vdst = kdst + S::TILE_BYTES;
-    const T* ks = kbase + (valid ? tok : 0) * p.kv_st;
-    const T* vs = vbase + (valid ? tok : 0) * p.kv_st;
+    // whole rows per instruction: lanes c of row (i RPI + lane / CPR) copy chunk c
+    const int c = lane % CPR;
 #pragma unroll
-    for (int c = 0; c < CPL; ++c) {
-      const int chunk = part * CPL + c;
-      cp_async16(kdst + swz<D>(row, chunk), ks + chunk * 8, valid);
-      cp_async16(vdst + swz<D>(row, chunk), vs + chunk * 8, valid);
+    for (int i = 0; i < NCI; ++i) {
+      const int r = i * RPI + lane / CPR;
+      const int32_t tr = __shfl_sync(0xffffffffu, tok, r);
+      const int64_t ro = static_cast<int64_t>(tr < 0 ? 0 : tr) * p.kv_st + c * 8;
+      cp_async16(kdst + swz<D>(r, c), kbase + ro, tr >= 0);
+      cp_async16(vdst + swz<D>(r, c), vbase + ro, tr >= 0);
     }
-    const uint32_t mask = __ballot_sync(0xffffffffu, valid && part == 0);
+    const uint32_t mask = __ballot_sync(0xffffffffu, lane < TRW && tok >= 0);
     if (lane == 0) stage_rows[w][s] = mask;
     cp_async_arrive(&full_bar[w][s]);
     ++produced;
