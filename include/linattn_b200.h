@@ -276,15 +276,16 @@ int linattn_indexer_scores(const void* q_idx, int32_t q_dtype, const int64_t* q_
  * descending (lowest index first among equal values); else in ascending index order.
  * With `causal`, row r only considers its first
  * min(n, (first_pos + r % period) / key_block + 1) entries and pads the remaining
- * slots with (-inf, -1).  k <= 4096; rows of up to 32768 entries stay in registers,
+ * slots with (-inf, -1).  The first `skip` entries of every row are never candidates
+ * (indices stay those of the full row).  k <= 4096; rows of up to 32768 entries stay in registers,
  * longer ones are re-read from global memory.
  * Replaces the torch.topk of indexer_topk_torch
  * (src/linattn/kernels/triton/fused_indexer.py:63-73) and of DSAAttention.select
  * (src/linattn/variants/selection.py:744-749).
  */
 int linattn_row_topk(const float* scores, int64_t rows, int64_t n, int64_t row_stride, int64_t k,
-                     int32_t causal, int64_t first_pos, int64_t key_block, int64_t period, int32_t sorted,
-                     float* values,
+                     int32_t causal, int64_t first_pos, int64_t key_block, int64_t period, int64_t skip,
+                     int32_t sorted, float* values,
                      int64_t* idx_i64, int32_t* idx_i32, int64_t out_stride, int64_t out_batch_stride,
                      void* stream);
 
@@ -311,6 +312,50 @@ int linattn_token_attention(const void* q, int32_t dtype, int64_t B, int64_t Hq,
                             int64_t sink, int64_t window, int32_t causal, int64_t offset, float scale,
                             int32_t diag_fallback, void* out, const int64_t* out_strides /*[4]*/, float* lse_out,
                             int32_t* reads_out, int32_t* status, void* stream);
+
+/*
+ * Mean of each `block` consecutive tokens of x (B, H, T, D) (element strides), the
+ * tail block padded by repeating the last token: out (B, H, ceil(T / block), D) fp32,
+ * contiguous.  Replaces block_reduce (src/linattn/core.py:103-120) for the pooled
+ * queries / keys of MInferenceAttention._block_sparse and MoBAAttention.select
+ * (src/linattn/variants/selection.py:339-353, 635-649).
+ */
+int linattn_block_mean(const void* x, int32_t dtype, int64_t B, int64_t H, int64_t T, int64_t D,
+                       const int64_t* strides /*[4]*/, int64_t block, float* out, void* stream);
+
+/*
+ * Block lists from a top-k selection: for each of `rows` rows, the ascending union
+ * (duplicates removed) of its top-k ids (int32, -1 padded, rows of k) with the forced
+ * blocks [0, sink) and [own - window + 1, own], plus `own` itself with force_own, all
+ * clipped to [0, own], where own = min((first_pos + r % period) / own_div, n_blocks - 1).
+ * out (rows, n_max) -1 padded; counts (rows) optional.  Replaces the boolean unions of
+ * MInferenceAttention._block_sparse (own block, selection.py:350-351) and
+ * MoBAAttention.select (own block, :645-646), and builds the sink + window + top-k lists
+ * of the block-sparse prefill.
+ */
+int linattn_merge_block_lists(const int32_t* topk, int64_t rows, int64_t k, int64_t period, int64_t first_pos,
+                              int64_t own_div, int64_t n_blocks, int64_t sink, int64_t window, int32_t force_own,
+                              int32_t* out, int64_t n_max, int32_t* counts, void* stream);
+
+/*
+ * Block-sparse causal prefill on the tcgen05 tensor cores.  Query t of head h reads the
+ * 64-token key blocks of list ids[b, h, t / rows_per_list, :] (ascending, -1 padded,
+ * counts optional; id_strides / count_strides = {batch, head, list row} in elements),
+ * plus the tokens below `sink`, restricted to keys < Tk and, with `causal`, to keys
+ * <= offset + t.  q (B, H_q, T_q, 128), K / V (B, H_kv, Tk, 128): contiguous rows,
+ * bf16 or f16 (one type); out with element strides, lse_out (B, H_q, T_q) optional.
+ * Lists of at most 64 blocks, Tk <= 2^18.  A row that reads nothing gets o = 0,
+ * lse = -inf.  Replaces the token mask + masked dense attention of
+ * MInferenceAttention._block_sparse and MoBAAttention.select
+ * (src/linattn/variants/selection.py:339-353, 635-649, 86-116) and
+ * block_sparse_attention_torch for prefill (src/linattn/kernels/triton/block_sparse.py:40-75).
+ */
+int linattn_block_sparse_prefill(const void* q, int32_t dtype, int64_t B, int64_t Hq, int64_t Tq, const void* k,
+                                 const void* v, int64_t Hkv, int64_t Tk, int64_t D, const int32_t* ids,
+                                 const int32_t* counts, const int64_t* id_strides /*[3]*/, int64_t n_max,
+                                 int64_t rows_per_list, const int64_t* count_strides /*[3]*/, int64_t sink,
+                                 int32_t causal, int64_t offset, float scale, void* out,
+                                 const int64_t* out_strides /*[4]*/, float* lse_out, int32_t* status, void* stream);
 
 #ifdef __cplusplus
 }

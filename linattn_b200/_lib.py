@@ -104,12 +104,18 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.linattn_indexer_scores.argtypes = [c_vp, c_i32, P(c_i64), c_vp, c_i32, P(c_i64), c_vp, c_i64, c_i64, c_vp,
                                            c_i32, P(c_i64), c_i64, c_i64, c_i64, c_i64, c_i64, c_i32, c_i64, c_i64,
                                            c_i64, c_i64, c_vp, c_i64, c_vp, c_vp]
-    lib.linattn_row_topk.argtypes = [c_vp, c_i64, c_i64, c_i64, c_i64, c_i32, c_i64, c_i64, c_i64, c_i32, c_vp, c_vp,
-                                     c_vp, c_i64, c_i64, c_vp]
+    lib.linattn_row_topk.argtypes = [c_vp, c_i64, c_i64, c_i64, c_i64, c_i32, c_i64, c_i64, c_i64, c_i64, c_i32, c_vp,
+                                     c_vp, c_vp, c_i64, c_i64, c_vp]
     lib.linattn_token_attention.argtypes = [c_vp, c_i32, c_i64, c_i64, c_i64, P(c_i64), c_vp, c_vp, c_i64, c_i64,
                                             c_i64, P(c_i64), P(Lists), c_i64, c_i64, c_i64, c_i32, c_i64,
                                             ctypes.c_float, c_i32, c_vp, P(c_i64), c_vp, c_vp, c_vp, c_vp]
-    for name in ("linattn_token_attention", "linattn_indexer_scores", "linattn_row_topk", "linattn_page_bounds", "linattn_paged_page_bounds", "linattn_quest_scores", "linattn_page_topk",
+    lib.linattn_block_mean.argtypes = [c_vp, c_i32, c_i64, c_i64, c_i64, c_i64, P(c_i64), c_i64, c_vp, c_vp]
+    lib.linattn_merge_block_lists.argtypes = [c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i32,
+                                              c_vp, c_i64, c_vp, c_vp]
+    lib.linattn_block_sparse_prefill.argtypes = [c_vp, c_i32, c_i64, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64,
+                                                 c_vp, c_vp, P(c_i64), c_i64, c_i64, P(c_i64), c_i64, c_i32, c_i64,
+                                                 ctypes.c_float, c_vp, P(c_i64), c_vp, c_vp, c_vp]
+    for name in ("linattn_block_sparse_prefill", "linattn_block_mean", "linattn_merge_block_lists", "linattn_token_attention", "linattn_indexer_scores", "linattn_row_topk", "linattn_page_bounds", "linattn_paged_page_bounds", "linattn_quest_scores", "linattn_page_topk",
                  "linattn_sparse_attention", "linattn_lse_combine"):
         getattr(lib, name).restype = ctypes.c_int
 

@@ -1,0 +1,141 @@
+"""Block selection for block-sparse attention on the B200.
+
+* ``block_mean``: mean-pooled blocks of queries / keys (``block_reduce``,
+  ``src/linattn/core.py:103-120``), a CUDA kernel.
+* ``pooled_block_scores``: ``mean(q_blk) . mean(k_blk) / sqrt(D)`` per (b, q-head,
+  q-block, k-block) (``MInferenceAttention._block_sparse``,
+  ``src/linattn/variants/selection.py:339-347``): the pooling kernel, then a plain
+  batched GEMM (cuBLAS through ``torch.matmul``).
+* ``block_select``: per q-block lists = the top-k causal candidate blocks (radix-select
+  kernel, lowest-index ties) united with forced blocks: the own block (MInference,
+  ``selection.py:350-351``) and/or sink blocks and a window of blocks (the block-sparse
+  prefill's sink + window + top-k).
+* ``moba_select``: per-token lists of ``MoBAAttention.select`` (``selection.py:635-649``):
+  gate ``q . mean(k_blk) / sqrt(D)``, top-k over blocks that start at or before the
+  query, plus the own block.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional, Tuple
+
+import torch
+
+from linattn_b200 import _lib as L
+from linattn_b200.indexer import row_topk
+
+__all__ = ["block_mean", "pooled_block_scores", "block_select", "moba_select", "merge_block_lists",
+           "block_sparse_prefill"]
+
+
+def block_mean(x: torch.Tensor, block: int) -> torch.Tensor:
+    """``(B,H,T,D)`` -> ``(B,H,ceil(T/block),D)`` fp32 block means (tail repeats the last row)."""
+    L.require_cuda(x)
+    b, h, t, d = x.shape
+    nb = -(-t // block)
+    out = torch.empty(b, h, nb, d, dtype=torch.float32, device=x.device)
+    L.check(L.lib().linattn_block_mean(x.data_ptr(), L.dtype_code(x), b, h, t, d, L.strides4(x), block,
+                                       out.data_ptr(), L.stream_of(x)))
+    return out
+
+
+def pooled_block_scores(q: torch.Tensor, k: torch.Tensor, block: int) -> torch.Tensor:
+    """``(B,H_q,n_qb,n_kb)`` fp32 pooled block scores with the GQA repeat of ``k``."""
+    b, hq, _, d = q.shape
+    hkv = k.shape[1]
+    qp = block_mean(q, block)
+    kp = block_mean(k, block)
+    g = hq // hkv
+    s = torch.matmul(qp.view(b, hkv, g, qp.shape[2], d), kp.view(b, hkv, 1, kp.shape[2], d).transpose(-1, -2))
+    return s.view(b, hq, qp.shape[2], kp.shape[2]).mul_(1.0 / math.sqrt(d))
+
+
+def merge_block_lists(topk_ids: torch.Tensor, *, period: int, first_pos: int, own_div: int, n_blocks: int,
+                      sink: int = 0, window: int = 0, force_own: bool = True,
+                      n_max: int = 0) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Ascending union of ``topk_ids (..., k)`` with the forced blocks (see
+    ``linattn_merge_block_lists``); returns ``(ids (..., n_max) int32, counts (...) int32)``."""
+    k = topk_ids.shape[-1]
+    rows = topk_ids.numel() // max(k, 1)
+    n_max = n_max or (k + sink + max(window, 1))
+    out = torch.empty(*topk_ids.shape[:-1], n_max, dtype=torch.int32, device=topk_ids.device)
+    counts = torch.empty(topk_ids.shape[:-1], dtype=torch.int32, device=topk_ids.device)
+    tk = topk_ids.to(torch.int32).contiguous()
+    L.check(L.lib().linattn_merge_block_lists(tk.data_ptr(), rows, k, period, first_pos, own_div, n_blocks, sink,
+                                              window, int(force_own), out.data_ptr(), n_max, counts.data_ptr(),
+                                              L.stream_of(tk)))
+    return out, counts
+
+
+def block_select(q: torch.Tensor, k: torch.Tensor, block: int, topk: int, *, offset: int = 0, sink_blocks: int = 0,
+                 window_blocks: int = 0, force_own: bool = True) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Per (b, q-head, q-block) block lists, ascending, -1 padded, with counts.
+
+    Candidates of q-block ``i`` (absolute block ``qb = offset // block + i``): blocks
+    ``[sink_blocks, qb - window_blocks]`` (``kb <= qb`` when ``window_blocks == 0``); the
+    top ``topk`` of their pooled scores are united with ``[0, sink_blocks)``, the window
+    ``[qb - window_blocks + 1, qb]`` and, with ``force_own``, ``qb``.
+    ``window_blocks = sink_blocks = 0, force_own`` is MInference's block-sparse pattern."""
+    scores = pooled_block_scores(q, k, block)
+    b, hq, nqb, nkb = scores.shape
+    qb0 = offset // block
+    kk = max(1, min(topk, nkb))
+    # causal candidates: the first (qb - window_blocks + 1) entries of each row, minus the sink
+    _, ids = row_topk(scores.view(-1, nkb), kk, sorted=False, causal=True, first_pos=qb0 - window_blocks,
+                      period=nqb, skip=sink_blocks, index_dtype=torch.int32)
+    return merge_block_lists(ids.view(b, hq, nqb, kk), period=nqb, first_pos=qb0, own_div=1, n_blocks=nkb,
+                             sink=sink_blocks, window=window_blocks, force_own=force_own,
+                             n_max=kk + sink_blocks + max(window_blocks, 1))
+
+
+def moba_select(q: torch.Tensor, k: torch.Tensor, block: int, topk: int, *,
+                offset: int = 0) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Per (b, q-head, query) block lists of MoBA (``selection.py:635-649``)."""
+    b, hq, tq, d = q.shape
+    hkv = k.shape[1]
+    kp = block_mean(k, block)
+    nkb = kp.shape[2]
+    g = hq // hkv
+    gates = torch.matmul(q.float().view(b, hkv, g * tq, d), kp.transpose(-1, -2)).view(b, hq, tq, nkb)
+    gates.mul_(1.0 / math.sqrt(d))
+    kk = max(1, min(topk, nkb))
+    # a query never routes to a block that starts after it: block j visible iff j * block <= pos
+    _, ids = row_topk(gates.view(-1, nkb), kk, sorted=False, causal=True, first_pos=offset, key_block=block,
+                      period=tq, index_dtype=torch.int32)
+    return merge_block_lists(ids.view(b, hq, tq, kk), period=tq, first_pos=offset, own_div=block, n_blocks=nkb,
+                             force_own=True, n_max=kk + 1)
+
+
+def block_sparse_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ids: torch.Tensor, *,
+                         counts: Optional[torch.Tensor] = None, rows_per_list: int = 64, sink: int = 0,
+                         causal: bool = True, offset: int = 0, scale: Optional[float] = None,
+                         lse_out: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Block-sparse causal prefill on the tcgen05 tensor cores: query ``t`` reads the
+    64-token key blocks of ``ids[b, h, t // rows_per_list]`` (ascending, -1 padded) plus
+    the tokens below ``sink``.  ``q (B,H_q,T_q,128)``, ``k, v (B,H_kv,T_k,128)``, bf16 or f16."""
+    dev = L.require_cuda(q, k, v, ids, counts, lse_out)
+    if q.dtype != k.dtype or k.dtype != v.dtype:
+        raise ValueError("q, k and v must have one dtype (bf16 or f16)")
+    b, hq, tq, d = q.shape
+    hkv, tk = k.shape[1], k.shape[2]
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    if ids.dtype != torch.int32 or ids.stride(-1) != 1:
+        ids = ids.to(torch.int32).contiguous()
+    if ids.dim() != 4:
+        raise ValueError("ids must be (B, H_q, list rows, n)")
+    cs = None
+    if counts is not None:
+        counts = counts.to(torch.int32)
+        cs = (L.c_i64 * 3)(*counts.stride())
+    if out is None:
+        out = torch.empty_like(q)
+    scale = (1.0 / math.sqrt(d)) if scale is None else float(scale)
+    status = L.status_word(dev)
+    L.check(L.lib().linattn_block_sparse_prefill(
+        q.data_ptr(), L.dtype_code(q), b, hq, tq, k.data_ptr(), v.data_ptr(), hkv, tk, d, ids.data_ptr(),
+        L.ptr(counts), (L.c_i64 * 3)(*ids.stride()[:3]), ids.shape[-1], rows_per_list, cs, sink, int(causal), offset,
+        scale, out.data_ptr(), L.strides4(out), L.ptr(lse_out), status.data_ptr(), L.stream_of(q)))
+    if L.strict():
+        L.check_status(dev)
+    return out

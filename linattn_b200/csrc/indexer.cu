@@ -158,6 +158,7 @@ struct RowTopkParams {
   int32_t* idx32;
   int64_t out_stride, out_bstride;
   int sorted;  // 1: by (value desc, index asc); 0: ascending index
+  int64_t skip;  // entries [0, skip) of every row are not candidates
 };
 
 // Rows of up to NT * ITEMS entries: each thread keeps ITEMS order-preserving keys in
@@ -176,10 +177,12 @@ __global__ void __launch_bounds__(NT, 1024 / NT) row_topk_reg_kernel(const RowTo
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t r = blockIdx.x;
   const int64_t seg = r / p.period, j = r % p.period;
-  const int nv = static_cast<int>(p.causal ? visible_keys(p.n, p.first_pos + j, p.kb) : p.n);
+  const int nv_all = static_cast<int>(p.causal ? visible_keys(p.n, p.first_pos + j, p.kb) : p.n);
+  const int skip = static_cast<int>(lmin(p.skip, nv_all));
+  const int nv = nv_all - skip;  // candidates: entries skip .. nv_all - 1, indexed from 0 here
   const int64_t ob = seg * p.out_bstride + j * p.out_stride;
   const int kb = static_cast<int>(lmin(p.k, nv));
-  const float* row = p.scores + r * p.row_stride;
+  const float* row = p.scores + r * p.row_stride + skip;
 
   uint32_t u[ITEMS];
   // range of the finite entries, as order-preserving keys (for the first digit)
@@ -387,8 +390,8 @@ __global__ void __launch_bounds__(NT, 1024 / NT) row_topk_reg_kernel(const RowTo
     for (int64_t i = tid; i < p.k; i += NT) {
       const bool ok = i < kb;
       if (p.values) p.values[ob + i] = ok ? key_float(sk[i]) : -INFINITY;
-      if (p.idx64) p.idx64[ob + i] = ok ? static_cast<int64_t>(si[i]) : -1;
-      if (p.idx32) p.idx32[ob + i] = ok ? static_cast<int32_t>(si[i]) : -1;
+      if (p.idx64) p.idx64[ob + i] = ok ? static_cast<int64_t>(si[i]) + skip : -1;
+      if (p.idx32) p.idx32[ob + i] = ok ? static_cast<int32_t>(si[i]) + skip : -1;
     }
   } else {
     // ascending index: bitmap, then a popcount scan over its words
@@ -415,8 +418,8 @@ __global__ void __launch_bounds__(NT, 1024 / NT) row_topk_reg_kernel(const RowTo
         m &= m - 1u;
         const int i = (w << 5) | bpos;
         if (p.values) p.values[ob + pos] = __ldg(row + i);
-        if (p.idx64) p.idx64[ob + pos] = i;
-        if (p.idx32) p.idx32[ob + pos] = i;
+        if (p.idx64) p.idx64[ob + pos] = i + skip;
+        if (p.idx32) p.idx32[ob + pos] = i + skip;
         ++pos;
       }
     }
@@ -444,10 +447,12 @@ __global__ void __launch_bounds__(512) row_topk_kernel(const RowTopkParams p) {
   const int tid = threadIdx.x;
   const int64_t r = blockIdx.x;
   const int64_t seg = r / p.period, j = r % p.period;
-  const int64_t nv = p.causal ? visible_keys(p.n, p.first_pos + j, p.kb) : p.n;
+  const int64_t nv_all = p.causal ? visible_keys(p.n, p.first_pos + j, p.kb) : p.n;
+  const int64_t skip = lmin(p.skip, nv_all);
+  const int64_t nv = nv_all - skip;
   const int64_t ob = seg * p.out_bstride + j * p.out_stride;
   const int64_t kb = lmin(p.k, nv);
-  const float* row = p.scores + r * p.row_stride;
+  const float* row = p.scores + r * p.row_stride + skip;
   if (staged)
     for (int64_t i = tid; i < nv; i += 512) keys[i] = float_key(row[i]);
   auto key_at = [&](int64_t i) { return staged ? keys[i] : float_key(row[i]); };
@@ -529,8 +534,8 @@ __global__ void __launch_bounds__(512) row_topk_kernel(const RowTopkParams p) {
   for (int64_t i = tid; i < p.k; i += 512) {
     const bool ok = i < kb;
     if (p.values) p.values[ob + i] = ok ? key_float(sk[i]) : -INFINITY;
-    if (p.idx64) p.idx64[ob + i] = ok ? static_cast<int64_t>(si[i]) : -1;
-    if (p.idx32) p.idx32[ob + i] = ok ? static_cast<int32_t>(si[i]) : -1;
+    if (p.idx64) p.idx64[ob + i] = ok ? static_cast<int64_t>(si[i]) + skip : -1;
+    if (p.idx32) p.idx32[ob + i] = ok ? static_cast<int32_t>(si[i]) + skip : -1;
   }
 }
 
@@ -608,8 +613,8 @@ extern "C" int linattn_indexer_scores(const void* q_idx, int32_t q_dtype, const 
 }
 
 extern "C" int linattn_row_topk(const float* scores, int64_t rows, int64_t n, int64_t row_stride, int64_t k,
-                                int32_t causal, int64_t first_pos, int64_t key_block, int64_t period, int32_t sorted,
-                                float* values,
+                                int32_t causal, int64_t first_pos, int64_t key_block, int64_t period, int64_t skip,
+                                int32_t sorted, float* values,
                                 int64_t* idx_i64, int32_t* idx_i32, int64_t out_stride, int64_t out_batch_stride,
                                 void* stream) {
   if (!scores) return set_error(LINATTN_EINVAL, "row_topk: scores is NULL");
@@ -624,7 +629,7 @@ extern "C" int linattn_row_topk(const float* scores, int64_t rows, int64_t n, in
   RowTopkParams p;
   p.scores = scores; p.rows = rows; p.n = n; p.row_stride = row_stride; p.k = k; p.kpow2 = kp; p.causal = causal;
   p.first_pos = first_pos; p.kb = key_block; p.period = period; p.values = values; p.idx64 = idx_i64; p.idx32 = idx_i32;
-  p.out_stride = out_stride; p.out_bstride = out_batch_stride; p.sorted = sorted ? 1 : 0;
+  p.out_stride = out_stride; p.out_bstride = out_batch_stride; p.sorted = sorted ? 1 : 0; p.skip = skip < 0 ? 0 : skip;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const unsigned grid = static_cast<unsigned>(rows);
   cudaError_t e = cudaSuccess;

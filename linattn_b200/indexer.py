@@ -108,7 +108,7 @@ def indexer_topk(q_idx: torch.Tensor, k_idx: torch.Tensor, head_weights: torch.T
         v = values[:, t0]
         ix = indices[:, t0]
         L.check(L.lib().linattn_row_topk(
-            scratch.data_ptr(), b * (t1 - t0), tk, tk, kk, int(causal), offset + t0, key_block, t1 - t0, int(sorted),
+            scratch.data_ptr(), b * (t1 - t0), tk, tk, kk, int(causal), offset + t0, key_block, t1 - t0, 0, int(sorted),
             v.data_ptr(), ix.data_ptr() if i64 else None, None if i64 else ix.data_ptr(), kk, tq * kk,
             L.stream_of(q_idx)))
     if L.strict():
@@ -117,11 +117,13 @@ def indexer_topk(q_idx: torch.Tensor, k_idx: torch.Tensor, head_weights: torch.T
 
 
 def row_topk(scores: torch.Tensor, k: int, *, sorted: bool = True, causal: bool = False, first_pos: int = 0,
+             key_block: int = 1, period: Optional[int] = None, skip: int = 0,
              index_dtype: torch.dtype = torch.int64) -> Tuple[torch.Tensor, torch.Tensor]:
     """Top-``k`` of each row of a 2-D fp32 ``scores`` (``torch.topk(scores, k, dim=-1)`` with
     the lowest index first among equal values).  ``sorted=False`` gives the same set in
     ascending index order.  ``causal``: row ``r`` only considers its first
-    ``first_pos + r + 1`` entries; slots past that count hold (-inf, -1)."""
+    ``(first_pos + r % period) // key_block + 1`` entries; ``skip``: entries before it
+    are never candidates; slots past the candidate count hold (-inf, -1)."""
     L.require_cuda(scores)
     if scores.dim() != 2 or scores.dtype != torch.float32 or scores.stride(1) != 1:
         raise ValueError("scores must be a 2-D fp32 tensor with unit stride on the last axis")
@@ -132,9 +134,10 @@ def row_topk(scores: torch.Tensor, k: int, *, sorted: bool = True, causal: bool 
     if values.numel() == 0:
         return values, indices
     i64 = index_dtype == torch.int64
+    per = max(rows, 1) if period is None else period
     L.check(L.lib().linattn_row_topk(
-        scores.data_ptr(), rows, n, scores.stride(0), kk, int(causal), first_pos, 1, max(rows, 1), int(sorted),
-        values.data_ptr(), indices.data_ptr() if i64 else None, None if i64 else indices.data_ptr(), kk, 0,
+        scores.data_ptr(), rows, n, scores.stride(0), kk, int(causal), first_pos, key_block, per, skip, int(sorted),
+        values.data_ptr(), indices.data_ptr() if i64 else None, None if i64 else indices.data_ptr(), kk, per * kk,
         L.stream_of(scores)))
     return values, indices
 
