@@ -9,23 +9,29 @@
 // 635-649.)
 //
 // One CTA = 128 query rows of one (batch, head); it walks the ascending union of its
-// rows' lists, 64 keys at a time, and a row ignores (-inf) the blocks not in its list.
-// Warp roles (192 threads, one CTA per SM):
-//   warp 0     TMEM allocation (256 columns) and the TMA producer: Q (two 128x64 boxes)
-//              once, then K and V blocks (two 64x64 boxes each, 128-byte swizzle) into
-//              a 3-stage ring;
+// rows' lists two blocks (128 keys) per step, and a row ignores (-inf) the blocks not
+// in its list.  Warp roles (320 threads, one CTA per SM):
+//   warp 0     TMEM allocation (512 columns) and the TMA producer: Q (two 128 x 64
+//              boxes) once, then per step the K and V rows of two blocks (four 64 x 64
+//              boxes each, 128-byte swizzle) into a 2-stage ring, with the blocks of the
+//              next steps prefetched into L2;
 //   warp 1     one thread issues tcgen05.mma (kind::f16, M = 128, fp32 accumulators in
-//              TMEM): S_j = Q K_j^T (N = 64) into one of two S buffers, then
-//              O += P_{j-1} V_{j-1} (N = 128, V read MN-major), and commits each to the
-//              mbarriers the other roles wait on;
-//   warps 2-5  softmax, one thread per row (TMEM lane): tcgen05.ld of its S row, masks,
-//              online softmax in the log2 domain, P written into swizzled shared
-//              tiles (the A operand of the PV product): for bf16 as hi + lo parts
-//              (two products, P to ~2^-17), for f16 one tile with the row sum of the
-//              rounded P (O / l an exact weighted mean of V rows).  O is rescaled in TMEM
-//              only when a row's running maximum grows by more than 8 (a factor 256),
-//              so P stays below 2^8 and the rare rescale waits for the PV in flight.
-//              The epilogue reads O from TMEM, divides by the row sum and stores.
+//              TMEM): S_j = Q K_j^T (N = 128 keys) into one of two S buffers, then
+//              O += P_{j-1} V_{j-1} (N = 128 channels) with P read from TMEM (A operand)
+//              and V from shared memory (MN-major), and commits to the mbarriers the
+//              other roles wait on.  MMAs of one thread execute in issue order, so S_{j+2}
+//              may be issued into the buffer whose P the earlier PV_j reads;
+//   warps 2-9  softmax, two threads per row (TMEM lane): warps 2-5 take the step's
+//              first block (64 keys), warps 6-9 the second; the pair exchanges its row
+//              maximum each step through shared memory.  tcgen05.ld of the scores,
+//              masks, online softmax in the log2 domain, then P written back over its
+//              scores (tcgen05.st): bf16 as hi + lo parts (two products, P to ~2^-17),
+//              f16 as one part with the row sum of the rounded P (O / l an exact
+//              weighted mean of V rows).  O is rescaled in TMEM only when a row's
+//              running maximum grows by more than 8, so P stays below 2^8; the rare
+//              rescale waits for the PV in flight.  The epilogue reads O from TMEM,
+//              divides by the row sum and stores (full tiles: staged in the Q tile and
+//              written by two TMA stores).
 // Every mbarrier wait is bounded (LINATTN_DEV_TIMEOUT on give-up); TMEM is released on
 // every path.
 #include <cudaTypedefs.h>
@@ -53,22 +59,24 @@ struct PrefillParams {
   float* lse;             // (B, Hq, Tq) or NULL
   int64_t n_tiles;        // query tiles of 128 per (b, head)
   int64_t n_kb;           // key blocks
+  int tma_out;            // out is contiguous (B, H_q, T_q, 128): full tiles leave through TMA stores
   int32_t* status;
 };
 
 namespace {
 
 constexpr int PQ = 128;          // query rows per CTA
-constexpr int PK = 64;           // keys per block
-constexpr int PKST = 3;          // K / V ring stages
+constexpr int PK = 64;           // keys per list block
+constexpr int PSTEP = 128;       // keys per step (two list blocks)
+constexpr int PKST = 2;          // K / V ring stages (steps)
+constexpr int PPF = 3;           // steps prefetched into L2 ahead of the ring
 constexpr int PLMAX = 64;        // longest list a row may have
 constexpr int PMAXKB = 4096;     // key blocks (T_k <= 2^18)
 constexpr int BOXB = 64 * 128;   // one 64-row x 128-byte box
 constexpr int QBYTES = 2 * PQ * 128;           // Q: two 128 x 64 boxes
-constexpr int STAGE = 4 * BOXB;                // K (2 boxes) + V (2 boxes)
-constexpr int PBYTES = PQ * 128;               // P: 128 rows x 64 keys (16-bit)
-// bf16: P = hi + lo (two tiles per buffer, 2^-17 relative); f16: one tile (2^-11)
-constexpr int SMEM_DYN = 1024 + QBYTES + PKST * STAGE + 2 * 2 * PBYTES;
+constexpr int HALFB = PSTEP * 128;             // 128 key rows x 64 channels
+constexpr int STAGE = 4 * HALFB;               // K (two channel halves) + V (two halves)
+constexpr int SMEM_DYN = 1024 + QBYTES + PKST * STAGE;
 
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
   uint64_t d = static_cast<uint64_t>((saddr >> 4) & 0x3fffu);
@@ -90,6 +98,16 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+// A operand from TMEM (K-major: lane = row, two 16-bit values per 32-bit column)
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                            uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
 }
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -123,45 +141,66 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32
       : "memory");
 }
 #undef LINATTN_W8
+__device__ __forceinline__ void tma_prefetch_2d(const void* tmap, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(tmap)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_kv(const void* tk, const void* tv, int y) {
+  tma_prefetch_2d(tk, 0, y);
+  tma_prefetch_2d(tk, 64, y);
+  tma_prefetch_2d(tv, 0, y);
+  tma_prefetch_2d(tv, 64, y);
+}
+// 2^x with the hardware approximation (ex2.approx.ftz: relative error ~2^-22; 2^-inf = 0)
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 }  // namespace
 
 template <typename T>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     prefill_umma_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tmq,
-                        const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv) {
+                        const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                        const __grid_constant__ CUtensorMap tmo) {
   using M = MmaOp<T>;
   constexpr int AB = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
-  constexpr uint32_t IDESC_S = umma_idesc(AB, PQ, PK, 0);
+  constexpr bool SPLIT = AB == 1;  // bf16 P as hi + lo
+  constexpr uint32_t IDESC_S = umma_idesc(AB, PQ, PSTEP, 0);
   constexpr uint32_t IDESC_O = umma_idesc(AB, PQ, 128, 1);
   extern __shared__ __align__(128) uint8_t psmem_raw[];
   uint8_t* smem = psmem_raw + ((1024 - (smem_u32(psmem_raw) & 1023)) & 1023);
-  uint8_t* sq = smem;                          // Q boxes
-  uint8_t* skv = sq + QBYTES;                  // ring: [K box0, K box1, V box0, V box1] per stage
-  uint8_t* sp = skv + PKST * STAGE;            // P buffers: [hi, lo] x 2
-  constexpr bool SPLIT = AB == 1;              // bf16 P as hi + lo
-  __shared__ __align__(8) uint64_t q_full, o_done, kv_full[PKST], kv_empty[PKST], s_full[2], s_free[2],
-      p_full[2], p_free[2];
+  uint8_t* sq = smem;          // Q boxes
+  uint8_t* skv = sq + QBYTES;  // ring: [K half0, K half1, V half0, V half1] per stage
+  __shared__ __align__(8) uint64_t q_full, o_done, kv_full[PKST], kv_empty[PKST], s_full[2], p_full[2], pv_done[2],
+      xch[2];
   __shared__ uint32_t tmem_base_sh;
   __shared__ uint32_t bitmap[PMAXKB / 32];
-  __shared__ uint16_t ulist[PMAXKB];
+  __shared__ uint16_t ulist[PMAXKB + 1];
   __shared__ uint16_t rlist[PQ][PLMAX + 2];  // odd word stride: rows in distinct banks
   __shared__ int n_union, dead;
+  __shared__ int rlen[PQ];              // list length of each row
+  __shared__ float xchg[2][2][PQ];      // [step parity][block half][row]: row maxima, then sums
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // ---- tile: (b, head, query tile), longest tiles first
+  // heads fastest: the CTAs in flight share a query tile, so the heads of a GQA group
+  // and neighbouring tiles (overlapping windows) read the same K / V blocks from L2
   const int64_t tile = blockIdx.x;
-  const int64_t qt = p.n_tiles - 1 - tile % p.n_tiles;
-  const int64_t bh = tile / p.n_tiles;
-  const int64_t h = bh % p.Hq, b = bh / p.Hq;
+  const int64_t h = tile % p.Hq;
+  const int64_t rest = tile / p.Hq;
+  const int64_t qt = p.n_tiles - 1 - rest % p.n_tiles;
+  const int64_t b = rest / p.n_tiles;
   const int64_t kvh = h / (p.Hq / p.Hkv);
   const int64_t t0 = qt * PQ;
 
   // ---- set-up: barriers, TMEM, the union of the rows' block lists
   const int nwords = static_cast<int>((p.n_kb + 31) / 32);
-  for (int i = tid; i < nwords; i += 192) bitmap[i] = 0u;
+  for (int i = tid; i < nwords; i += 320) bitmap[i] = 0u;
   if (tid == 0) {
     mbar_init(&q_full, 1);
     mbar_init(&o_done, 1);
@@ -171,45 +210,57 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
-      mbar_init(&s_free[s], PQ);
-      mbar_init(&p_full[s], PQ);
-      mbar_init(&p_free[s], 1);
+      mbar_init(&p_full[s], 2 * PQ);
+      mbar_init(&pv_done[s], 1);
+      mbar_init(&xch[s], 2 * PQ);
     }
     dead = 0;
     mbar_fence_init();
   }
   if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_u32(&tmem_base_sh))
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(&tmem_base_sh))
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   __syncthreads();
-  // softmax threads: row r = TMEM lane (32 x (warp % 4) + lane)
+  // softmax threads: row r = TMEM lane (32 x (warp % 4) + lane), block half hb
   const bool is_sm = warp >= 2;
   const int r = is_sm ? 32 * (warp & 3) + lane : 0;
+  const int hb = warp >= 6 ? 1 : 0;
   const int64_t t = t0 + r;
   const bool row_ok = is_sm && t < p.Tq;
   const int64_t pos = p.offset + t;
   int my_n = 0;
-  if (row_ok) {
+  // the union only needs, per list, its last row in this tile (the widest causal view)
+  const int64_t t_last_row = lmin(p.Tq, t0 + PQ) - 1;
+  const bool owner = row_ok && (t == t_last_row || (t + 1) / p.rows_per_list != t / p.rows_per_list);
+  if (row_ok && hb == 0) {
     const int64_t lr = t / p.rows_per_list;
     const int32_t* ids = p.ids + b * p.ls_b + h * p.ls_h + lr * p.ls_r;
     int64_t cnt = p.n_max;
     if (p.counts) cnt = lmin(cnt, static_cast<int64_t>(p.counts[b * p.cs_b + h * p.cs_h + lr * p.cs_r]));
     const int64_t vis = p.causal ? (pos < 0 ? -1 : pos / PK) : p.n_kb - 1;  // last visible block
-    for (int64_t i = 0; i < cnt && my_n < PLMAX; ++i) {
-      const int32_t blk = ids[i];
-      if (blk < 0 || blk >= p.n_kb || blk > vis) continue;
-      if (my_n > 0 && blk <= rlist[r][my_n - 1]) continue;  // ascending lists only
-      rlist[r][my_n++] = static_cast<uint16_t>(blk);
-      atomicOr(&bitmap[blk >> 5], 1u << (blk & 31));
+    for (int64_t i0 = 0; i0 < cnt && my_n < PLMAX; i0 += 8) {
+      int32_t blk8[8];  // eight independent loads in flight
+#pragma unroll
+      for (int e = 0; e < 8; ++e) blk8[e] = i0 + e < cnt ? __ldg(ids + i0 + e) : -1;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int32_t blk = blk8[e];
+        if (blk < 0 || blk >= p.n_kb || blk > vis || my_n >= PLMAX) continue;
+        if (my_n > 0 && blk <= rlist[r][my_n - 1]) continue;  // ascending lists only
+        rlist[r][my_n++] = static_cast<uint16_t>(blk);
+        if (owner) atomicOr(&bitmap[blk >> 5], 1u << (blk & 31));
+      }
     }
-    if (p.sink > 0) {
+    if (p.sink > 0 && t == t_last_row) {
       const int64_t sb = lmin((p.sink - 1) / PK, vis);
       for (int64_t blk = 0; blk <= sb; ++blk) atomicOr(&bitmap[blk >> 5], 1u << (blk & 31));
     }
   }
+  if (is_sm && hb == 0) rlen[r] = my_n;
   __syncthreads();
+  if (is_sm) my_n = rlen[r];
   if (warp == 1) {
     // ascending union: popcount scan over the bitmap words
     int base = 0;
@@ -231,13 +282,18 @@ __global__ void __launch_bounds__(192, 1)
       }
       base += __shfl_sync(0xffffffffu, incl, 31);
     }
-    if (lane == 0) n_union = base;
+    if (lane == 0) {
+      n_union = base;
+      // an odd union: the last step repeats its first block (masked for every row)
+      if (base & 1) ulist[base] = ulist[base - 1];
+    }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const int n = n_union;
-  const uint32_t tmem = tmem_base_sh;  // columns [0, 64): S0, [64, 128): S1, [128, 256): O
+  const int n_steps = (n + 1) >> 1;
+  const uint32_t tmem = tmem_base_sh;  // columns [0, 128): S / P 0, [128, 256): S / P 1, [256, 384): O
 
   if (warp == 0) {
     // ================= TMA producer
@@ -247,8 +303,13 @@ __global__ void __launch_bounds__(192, 1)
       tma_load_2d(sq, &tmq, 0, qrow, &q_full);
       tma_load_2d(sq + PQ * 128, &tmq, 64, qrow, &q_full);
       const int64_t kv0 = (b * p.Hkv + kvh) * p.Tk;
+      auto row_of = [&](int e) { return static_cast<int>(kv0 + static_cast<int64_t>(ulist[e]) * PK); };
+      auto prefetch_step = [&](int j) {
+        tma_prefetch_kv(&tmk, &tmv, row_of(2 * j));
+        tma_prefetch_kv(&tmk, &tmv, row_of(2 * j + 1));
+      };
       int issued = 0;
-      for (int j = 0; j < n; ++j) {
+      for (int j = 0; j < n_steps; ++j) {
         const int st = j % PKST;
         if (j >= PKST && !mbar_wait_bounded(&kv_empty[st], static_cast<uint32_t>(((j / PKST) - 1) & 1))) {
           report(p.status, LINATTN_DEV_TIMEOUT);
@@ -257,13 +318,22 @@ __global__ void __launch_bounds__(192, 1)
         }
         if (dead) break;
         uint8_t* dst = skv + st * STAGE;
-        const int y = static_cast<int>(kv0 + static_cast<int64_t>(ulist[j]) * PK);
+        const int ya = row_of(2 * j), yb = row_of(2 * j + 1);
         mbar_arrive_expect_tx(&kv_full[st], STAGE);
-        tma_load_2d(dst, &tmk, 0, y, &kv_full[st]);
-        tma_load_2d(dst + BOXB, &tmk, 64, y, &kv_full[st]);
-        tma_load_2d(dst + 2 * BOXB, &tmv, 0, y, &kv_full[st]);
-        tma_load_2d(dst + 3 * BOXB, &tmv, 64, y, &kv_full[st]);
+        // 128 key rows per channel half: block a rows 0-63, block b rows 64-127
+        tma_load_2d(dst, &tmk, 0, ya, &kv_full[st]);
+        tma_load_2d(dst + BOXB, &tmk, 0, yb, &kv_full[st]);
+        tma_load_2d(dst + HALFB, &tmk, 64, ya, &kv_full[st]);
+        tma_load_2d(dst + HALFB + BOXB, &tmk, 64, yb, &kv_full[st]);
+        tma_load_2d(dst + 2 * HALFB, &tmv, 0, ya, &kv_full[st]);
+        tma_load_2d(dst + 2 * HALFB + BOXB, &tmv, 0, yb, &kv_full[st]);
+        tma_load_2d(dst + 3 * HALFB, &tmv, 64, ya, &kv_full[st]);
+        tma_load_2d(dst + 3 * HALFB + BOXB, &tmv, 64, yb, &kv_full[st]);
         issued = j + 1;
+        // warm L2 with the steps PPF further on (no shared memory involved)
+        if (j == 0)
+          for (int f = 1; f <= PPF && f < n_steps; ++f) prefetch_step(f);
+        if (j + PPF + 1 < n_steps) prefetch_step(j + PPF + 1);
       }
       if (dead) {
         // let the copies in flight land (bounded) before the CTA gives up its smem
@@ -275,54 +345,54 @@ __global__ void __launch_bounds__(192, 1)
     // ================= MMA issuer
     if (lane == 0 && n > 0) {
       bool ok = mbar_wait_bounded(&q_full, 0);
-      const uint32_t sq_a = smem_u32(sq), skv_a = smem_u32(skv), sp_a = smem_u32(sp);
+      const uint32_t sq_a = smem_u32(sq), skv_a = smem_u32(skv);
       auto pv = [&](int j) -> bool {
         const int pb = j & 1;
         if (!mbar_wait_bounded(&p_full[pb], static_cast<uint32_t>((j >> 1) & 1))) return false;
         tc_fence_after();
-        const uint32_t vb = skv_a + (j % PKST) * STAGE + 2 * BOXB;
+        const uint32_t vb = skv_a + (j % PKST) * STAGE + 2 * HALFB;
+        const uint32_t pt = tmem + pb * 128;  // P of step j, over its scores
 #pragma unroll
-        for (int kk = 0; kk < PK / 16; ++kk) {
-          const uint64_t bd = umma_desc(vb + kk * 2048, BOXB, 1024);
-          const uint64_t a = umma_desc(sp_a + (2 * pb) * PBYTES + kk * 32, 16, 1024);
-          umma_f16(tmem + 128, a, bd, IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
-          if (SPLIT) umma_f16(tmem + 128, umma_desc(sp_a + (2 * pb + 1) * PBYTES + kk * 32, 16, 1024), bd, IDESC_O, 1u);
+        for (int kk = 0; kk < PSTEP / 16; ++kk) {
+          const uint64_t bd = umma_desc(vb + kk * 2048, HALFB, 1024);
+          umma_f16_ts(tmem + 256, pt + kk * 8, bd, IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+          if (SPLIT) umma_f16_ts(tmem + 256, pt + 64 + kk * 8, bd, IDESC_O, 1u);
         }
-        umma_commit(&o_done);
-        umma_commit(&p_free[pb]);
+        umma_commit(&pv_done[pb]);
         umma_commit(&kv_empty[j % PKST]);
         return true;
       };
-      for (int j = 0; ok && j < n; ++j) {
+      for (int j = 0; ok && j < n_steps; ++j) {
         const int st = j % PKST, sb = j & 1;
         ok = mbar_wait_bounded(&kv_full[st], static_cast<uint32_t>((j / PKST) & 1));
-        if (ok && j >= 2) ok = mbar_wait_bounded(&s_free[sb], static_cast<uint32_t>(((j >> 1) - 1) & 1));
         if (!ok) break;
         tc_fence_after();
+        // S_j into buffer sb: its previous P (step j - 2) is read by PV_{j-2}, issued
+        // before this point; MMAs run in issue order
         const uint32_t kb = skv_a + st * STAGE;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint64_t a = umma_desc(sq_a + (kk >> 2) * (PQ * 128) + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = umma_desc(kb + (kk >> 2) * BOXB + (kk & 3) * 32, 16, 1024);
-          umma_f16(tmem + sb * 64, a, bd, IDESC_S, kk > 0 ? 1u : 0u);
+          const uint64_t bd = umma_desc(kb + (kk >> 2) * HALFB + (kk & 3) * 32, 16, 1024);
+          umma_f16(tmem + sb * 128, a, bd, IDESC_S, kk > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[sb]);
         if (j >= 1) ok = pv(j - 1);
       }
-      if (ok) ok = pv(n - 1);
+      if (ok) ok = pv(n_steps - 1);
       if (!ok) {
         report(p.status, LINATTN_DEV_TIMEOUT);
         dead = 1;
       }
     }
   } else {
-    // ================= softmax (one thread per query row)
+    // ================= softmax (two threads per query row: block half hb)
     // tcgen05.ld / st are warp-collective: every branch around them is warp-uniform
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16);
     float m_used = -INFINITY, l = 0.f;
     int ptr = 0;
     bool ok = true;
-    for (int j = 0; j < n; ++j) {
+    for (int j = 0; j < n_steps; ++j) {
       const int sb = j & 1;
       if (!__all_sync(0xffffffffu, mbar_wait_bounded(&s_full[sb], static_cast<uint32_t>((j >> 1) & 1)))) {
         ok = false;
@@ -330,116 +400,175 @@ __global__ void __launch_bounds__(192, 1)
       }
       tc_fence_after();
       uint32_t sv[2][32];
-      tmem_ld32(lane_addr + sb * 64, sv[0]);
-      tmem_ld32(lane_addr + sb * 64 + 32, sv[1]);
+      tmem_ld32(lane_addr + sb * 128 + hb * 64, sv[0]);
+      tmem_ld32(lane_addr + sb * 128 + hb * 64 + 32, sv[1]);
       tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&s_free[sb]);
-      // which keys of block ulist[j] this row reads
-      const int blk = ulist[j];
-      while (ptr < my_n && rlist[r][ptr] < blk) ++ptr;
-      const bool member = row_ok && ptr < my_n && rlist[r][ptr] == blk;
-      const int64_t key0 = static_cast<int64_t>(blk) * PK;
-      int64_t kend = member ? PK : lmin(PK, p.sink - key0);   // keys [key0, key0 + kend) are read
-      if (!row_ok) kend = 0;
-      kend = lmin(kend, p.Tk - key0);
-      if (p.causal) kend = lmin(kend, pos - key0 + 1);
-      float x[64];
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        x[c] = c < kend ? __uint_as_float(sv[c >> 5][c & 31]) * p.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, x[c]);
+      // which keys of this thread's block the row reads
+      int ke = 0;
+      {
+        const int e = 2 * j + hb;
+        const int blk = ulist[e];
+        bool member = false;
+        if (e < n) {
+          while (ptr < my_n && rlist[r][ptr] < blk) ++ptr;
+          member = row_ok && ptr < my_n && rlist[r][ptr] == blk;
+        }
+        const int64_t key0 = static_cast<int64_t>(blk) * PK;
+        int64_t kend = member ? PK : (e < n ? lmin(PK, p.sink - key0) : 0);
+        if (!row_ok) kend = 0;
+        kend = lmin(kend, p.Tk - key0);
+        if (p.causal) kend = lmin(kend, pos - key0 + 1);
+        ke = static_cast<int>(lmax(0, kend));
       }
-      // running maximum: moved (and O rescaled) only when it grows by more than 8
+      // raw scores; masks only where needed (scale > 0: max of raw = max / scale)
+      float mx8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx8[i] = -INFINITY;
+      if (ke >= PK) {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], __uint_as_float(sv[c >> 5][c & 31]));
+      } else {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          const float v = c < ke ? __uint_as_float(sv[c >> 5][c & 31]) : -INFINITY;
+          sv[c >> 5][c & 31] = __float_as_uint(v);
+          mx8[c & 7] = fmaxf(mx8[c & 7], v);
+        }
+      }
+      const float mloc = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      // the pair's row maximum, through an mbarrier of the eight softmax warps (bounded
+      // wait; double-buffered by step parity: the partner has read this slot before
+      // either writes it again two steps later)
+      xchg[sb][hb][r] = mloc;
+      mbar_arrive(&xch[sb]);
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&xch[sb], static_cast<uint32_t>((j >> 1) & 1)))) {
+        ok = false;
+        break;
+      }
+      const float mx = fmaxf(mloc, xchg[sb][hb ^ 1][r]) * p.scale_log2;
+      // running maximum: moved (and O rescaled) only when it grows by more than 8; both
+      // threads of a row take the same decision from the same values
       const bool first = mx > -INFINITY && m_used == -INFINITY;
       const bool grow = mx > -INFINITY && m_used != -INFINITY && mx > m_used + 8.f;
       if (__any_sync(0xffffffffu, grow)) {
-        const float alpha = grow ? exp2f(m_used - mx) : 1.f;
-        // O holds blocks < j once PV(j-1) is done: the completion of use (j-1)/2 of P
-        // buffer (j-1)%2 (this thread waited for that buffer's previous use, so the
-        // parity names exactly this phase)
-        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&p_free[(j - 1) & 1],
+        const float alpha = grow ? ex2_approx(m_used - mx) : 1.f;
+        // O holds steps < j once PV_{j-1} is done (the completion of use (j-1)/2 of
+        // buffer (j-1)%2; its previous use finished before S_{j-1}, which this thread saw)
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&pv_done[(j - 1) & 1],
                                                        static_cast<uint32_t>(((j - 1) >> 1) & 1)))) {
           ok = false;
           break;
         }
         tc_fence_after();
 #pragma unroll 1
-        for (int cc = 0; cc < 4; ++cc) {
+        for (int cc = 0; cc < 2; ++cc) {  // this thread's 64 channels of O
           uint32_t ov[32];
-          tmem_ld32(lane_addr + 128 + cc * 32, ov);
+          const uint32_t oa = lane_addr + 256 + hb * 64 + cc * 32;
+          tmem_ld32(oa, ov);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
-          tmem_st32(lane_addr + 128 + cc * 32, ov);
+          tmem_st32(oa, ov);
         }
         tmem_wait_st();
         l *= alpha;
       }
       if (first || grow) m_used = mx;
-      // P = exp2(x - m_used) into the swizzled P tile (row r, 8 chunks of 8 keys)
-      const int pb = j & 1;
-      if (j >= 2 &&
-          !__all_sync(0xffffffffu, mbar_wait_bounded(&p_free[pb], static_cast<uint32_t>(((j >> 1) - 1) & 1)))) {
-        ok = false;
-        break;
-      }
-      uint8_t* prow = sp + (2 * pb) * PBYTES + r * 128;
-      float sum = 0.f;
+      // P = 2^(s * scale - m) over the scores: hi columns [32 hb, 32 hb + 32), lo 64 further;
+      // masked scores are -inf (P = 0); a row with nothing read yet has m = -inf: P = 0
+      const float sl = p.scale_log2;
+      const float neg = m_used == -INFINITY ? -INFINITY : -m_used;
+      float sum8[8];
 #pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
-        uint32_t wv[4], wl[4];
+      for (int i = 0; i < 8; ++i) sum8[i] = 0.f;
+      uint32_t hi[32], lo[32];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float a = m_used == -INFINITY ? 0.f : exp2f(x[ch * 8 + 2 * e] - m_used);
-          const float c2 = m_used == -INFINITY ? 0.f : exp2f(x[ch * 8 + 2 * e + 1] - m_used);
-          wv[e] = M::pack(a, c2);
-          const float2 rp = M::unpack(wv[e]);
-          if (SPLIT) {
-            wl[e] = M::pack(a - rp.x, c2 - rp.y);  // hi + lo carries P to ~2^-17
-            sum += a + c2;
-          } else {
-            sum += rp.x + rp.y;  // the rounded P the product uses: O / l an exact weighted mean
-          }
+      for (int e = 0; e < 32; ++e) {
+        const int c = 2 * e;
+        const float a = ex2_approx(fmaf(__uint_as_float(sv[c >> 5][c & 31]), sl, neg));
+        const float c2 = ex2_approx(fmaf(__uint_as_float(sv[(c + 1) >> 5][(c + 1) & 31]), sl, neg));
+        hi[e] = M::pack(a, c2);
+        const float2 rp = M::unpack(hi[e]);
+        if (SPLIT) {
+          lo[e] = M::pack(a - rp.x, c2 - rp.y);
+          sum8[e & 7] += a + c2;
+        } else {
+          lo[e] = 0u;
+          sum8[e & 7] += rp.x + rp.y;
         }
-        const int off = (ch ^ (r & 7)) << 4;
-        *reinterpret_cast<uint4*>(prow + off) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-        if (SPLIT) *reinterpret_cast<uint4*>(prow + PBYTES + off) = make_uint4(wl[0], wl[1], wl[2], wl[3]);
       }
-      l += sum;
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tmem_st32(lane_addr + sb * 128 + hb * 32, hi);
+      if (SPLIT) tmem_st32(lane_addr + sb * 128 + 64 + hb * 32, lo);
+      l += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
+      tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&p_full[pb]);
+      mbar_arrive(&p_full[sb]);
     }
-    // ---- epilogue: O / l
-    if (ok && n > 0 &&
-        !__all_sync(0xffffffffu, mbar_wait_bounded(&p_free[(n - 1) & 1], static_cast<uint32_t>(((n - 1) >> 1) & 1))))
+    // ---- epilogue: O / l once the last PV is done (exact phase, as above)
+    if (ok && n_steps > 0 &&
+        !__all_sync(0xffffffffu, mbar_wait_bounded(&pv_done[(n_steps - 1) & 1],
+                                                   static_cast<uint32_t>(((n_steps - 1) >> 1) & 1))))
       ok = false;
     if (!ok) {
       report(p.status, LINATTN_DEV_TIMEOUT);
       dead = 1;
     }
+    // the row sum of the pair (both halves use the same running maximum); slot
+    // n_steps & 1 was last written at step n_steps - 2, read before that step's barrier
+    const int slot = n_steps & 1;
+    xchg[slot][hb][r] = l;
+    asm volatile("bar.sync 2, 256;" ::: "memory");
+    l += xchg[slot][hb ^ 1][r];
     tc_fence_after();
     const float inv = l > 0.f ? 1.f / l : 0.f;
     const int64_t ob = b * p.os[0] + h * p.os[1] + t * p.os[2];
+    // full tiles with contiguous output: rows staged (swizzled, as TMA boxes) in the Q
+    // tile, which every MMA has finished reading, then two TMA stores
+    const bool via_tma = p.tma_out && t0 + PQ <= p.Tq;
 #pragma unroll 1
-    for (int cc = 0; cc < 4; ++cc) {
+    for (int cc = 0; cc < 2; ++cc) {  // this thread's 64 channels
       uint32_t ov[32];
-      if (ok && n > 0) {  // warp-uniform
-        tmem_ld32(lane_addr + 128 + cc * 32, ov);
+      if (ok && n_steps > 0) {  // warp-uniform
+        tmem_ld32(lane_addr + 256 + hb * 64 + cc * 32, ov);
         tmem_wait_ld();
       } else {
 #pragma unroll
         for (int i = 0; i < 32; ++i) ov[i] = 0u;
       }
-      if (row_ok) {
+      if (via_tma) {
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const int c = cc * 4 + q4;  // 16-byte chunk (8 channels) within the channel half hb
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            w[e] = M::pack(__uint_as_float(ov[q4 * 8 + 2 * e]) * inv, __uint_as_float(ov[q4 * 8 + 2 * e + 1]) * inv);
+          *reinterpret_cast<uint4*>(sq + hb * (PQ * 128) + r * 128 + ((c ^ (r & 7)) << 4)) =
+              make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      } else if (row_ok) {
 #pragma unroll
         for (int i = 0; i < 32; ++i)
-          store_any(p.out, ob + (cc * 32 + i) * p.os[3], p.out_dtype, __uint_as_float(ov[i]) * inv);
+          store_any(p.out, ob + (hb * 64 + cc * 32 + i) * p.os[3], p.out_dtype, __uint_as_float(ov[i]) * inv);
       }
     }
-    if (row_ok && p.lse)
+    if (via_tma) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      asm volatile("bar.sync 1, 256;" ::: "memory");  // the eight softmax warps
+      if (r == 0 && hb == 0) {
+        const int y = static_cast<int>((b * p.Hq + h) * p.Tq + t0);
+        asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                         reinterpret_cast<uint64_t>(&tmo)), "r"(0), "r"(y), "r"(smem_u32(sq))
+                     : "memory");
+        asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                         reinterpret_cast<uint64_t>(&tmo)), "r"(64), "r"(y), "r"(smem_u32(sq + PQ * 128))
+                     : "memory");
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // smem read before the CTA exits
+      }
+    }
+    if (row_ok && hb == 0 && p.lse)
       p.lse[(b * p.Hq + h) * p.Tq + t] = l > 0.f ? (m_used + log2f(l)) * 0.69314718055994531f : -INFINITY;
   }
   // ---- tear-down: every tcgen05 op of this CTA is complete (the epilogue waited for
@@ -449,24 +578,23 @@ __global__ void __launch_bounds__(192, 1)
   if (dead && tid == 32 && n > 0) {
     umma_commit(&o_done);
     (void)mbar_wait_bounded(&o_done, 0, 200000000ull);
-    (void)mbar_wait_bounded(&o_done, 1, 200000000ull);
   }
   __syncthreads();
   tc_fence_after();
   if (warp == 0)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
 }
 
 namespace {
 
 template <typename T>
 cudaError_t launch_prefill(const PrefillParams& p, const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
-                           cudaStream_t st) {
+                           const CUtensorMap& o, cudaStream_t st) {
   auto kern = prefill_umma_kernel<T>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_DYN);
   if (e != cudaSuccess) return e;
   const int64_t grid = p.B * p.Hq * p.n_tiles;
-  kern<<<static_cast<unsigned>(grid), 192, SMEM_DYN, st>>>(p, q, k, v);
+  kern<<<static_cast<unsigned>(grid), 320, SMEM_DYN, st>>>(p, q, k, v, o);
   return cudaGetLastError();
 }
 
@@ -517,9 +645,14 @@ extern "C" int linattn_block_sparse_prefill(const void* q, int32_t dtype, int64_
   for (int i = 0; i < 4; ++i) p.os[i] = out_strides[i];
   p.n_tiles = (Tq + PQ - 1) / PQ;
   p.n_kb = n_kb;
+  // output through TMA stores when it is contiguous (B, H_q, T_q, 128) and 16-byte aligned
+  CUtensorMap to = tq;
+  const bool contiguous_out = out_strides[3] == 1 && out_strides[2] == 128 && out_strides[1] == Tq * 128 &&
+                              (B == 1 || out_strides[0] == Hq * Tq * 128) && reinterpret_cast<uintptr_t>(out) % 16 == 0;
+  p.tma_out = contiguous_out && tensor_map_2d(&to, out, cu, 128, B * Hq * Tq, 256, 64, PQ) ? 1 : 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const cudaError_t e = dtype == LINATTN_BF16 ? launch_prefill<__nv_bfloat16>(p, tq, tk, tv, st)
-                                              : launch_prefill<__half>(p, tq, tk, tv, st);
+  const cudaError_t e = dtype == LINATTN_BF16 ? launch_prefill<__nv_bfloat16>(p, tq, tk, tv, to, st)
+                                              : launch_prefill<__half>(p, tq, tk, tv, to, st);
   if (e != cudaSuccess) {
     char msg[256];
     snprintf(msg, sizeof(msg), "block_sparse_prefill: %s", cudaGetErrorString(e));
