@@ -11,19 +11,21 @@
 // One CTA = 128 query rows of one (batch, head); it walks the ascending union of its
 // rows' lists two blocks (128 keys) per step, and a row ignores (-inf) the blocks not
 // in its list.  Warp roles (320 threads, one CTA per SM):
-//   warp 0     TMEM allocation (512 columns) and the TMA producer: Q (two 128 x 64
-//              boxes) once, then per step the K and V rows of two blocks (four 64 x 64
-//              boxes each, 128-byte swizzle) into a 2-stage ring, with the blocks of the
-//              next steps prefetched into L2;
+//   warp 0     TMEM allocation (512 columns) and two TMA producer lanes: lane 0 Q (two
+//              128 x 64 boxes) once, then per step the K rows of two blocks (four 64 x 64
+//              boxes, 128-byte swizzle) into a 3-stage K ring freed as soon as S_j is
+//              done; lane 1 the V rows into a 2-stage V ring freed by PV_j; both prefetch
+//              the blocks of the next steps into L2;
 //   warp 1     one thread issues tcgen05.mma (kind::f16, M = 128, fp32 accumulators in
 //              TMEM): S_j = Q K_j^T (N = 128 keys) into one of two S buffers, then
 //              O += P_{j-1} V_{j-1} (N = 128 channels) with P read from TMEM (A operand)
 //              and V from shared memory (MN-major), and commits to the mbarriers the
 //              other roles wait on.  MMAs of one thread execute in issue order, so S_{j+2}
 //              may be issued into the buffer whose P the earlier PV_j reads;
-//   warps 2-9  softmax, two threads per row (TMEM lane): warps 2-5 take the step's
-//              first block (64 keys), warps 6-9 the second; the pair exchanges its row
-//              maximum each step through shared memory.  tcgen05.ld of the scores,
+//   warps 2-9  softmax, two threads per row (TMEM lane): warps 2-5 take every step's
+//              first block (64 keys), warps 6-9 its second; each half keeps its own
+//              running (O, m, l), the two O accumulators merged in the epilogue.
+//              tcgen05.ld of the scores,
 //              masks, online softmax in the log2 domain, then P written back over its
 //              scores (tcgen05.st): bf16 as hi + lo parts (two products, P to ~2^-17),
 //              f16 as one part with the row sum of the rounded P (O / l an exact
@@ -68,15 +70,16 @@ namespace {
 constexpr int PQ = 128;          // query rows per CTA
 constexpr int PK = 64;           // keys per list block
 constexpr int PSTEP = 128;       // keys per step (two list blocks)
-constexpr int PKST = 2;          // K / V ring stages (steps)
+constexpr int PKS = 3;           // K ring stages (steps): freed when S_j is done
+constexpr int PVS = 2;           // V ring stages (steps): freed when PV_j is done
 constexpr int PPF = 3;           // steps prefetched into L2 ahead of the ring
 constexpr int PLMAX = 64;        // longest list a row may have
 constexpr int PMAXKB = 4096;     // key blocks (T_k <= 2^18)
 constexpr int BOXB = 64 * 128;   // one 64-row x 128-byte box
 constexpr int QBYTES = 2 * PQ * 128;           // Q: two 128 x 64 boxes
 constexpr int HALFB = PSTEP * 128;             // 128 key rows x 64 channels
-constexpr int STAGE = 4 * HALFB;               // K (two channel halves) + V (two halves)
-constexpr int SMEM_DYN = 1024 + QBYTES + PKST * STAGE;
+constexpr int TILE = 2 * HALFB;                // K or V of one step (two channel halves)
+constexpr int SMEM_DYN = 1024 + QBYTES + (PKS + PVS) * TILE;
 
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
   uint64_t d = static_cast<uint64_t>((saddr >> 4) & 0x3fffu);
@@ -176,16 +179,17 @@ __global__ void __launch_bounds__(320, 1)
   extern __shared__ __align__(128) uint8_t psmem_raw[];
   uint8_t* smem = psmem_raw + ((1024 - (smem_u32(psmem_raw) & 1023)) & 1023);
   uint8_t* sq = smem;          // Q boxes
-  uint8_t* skv = sq + QBYTES;  // ring: [K half0, K half1, V half0, V half1] per stage
-  __shared__ __align__(8) uint64_t q_full, o_done, kv_full[PKST], kv_empty[PKST], s_full[2], p_full[2], pv_done[2],
-      xch[2];
+  uint8_t* sk = sq + QBYTES;        // K ring: [channel half 0, half 1] of 128 key rows per stage
+  uint8_t* sv_ring = sk + PKS * TILE;  // V ring, same layout
+  __shared__ __align__(8) uint64_t q_full, o_done, k_full[PKS], k_empty[PKS], v_full[PVS], v_empty[PVS], s_full[2],
+      p_full[2], pv_done[2];
   __shared__ uint32_t tmem_base_sh;
   __shared__ uint32_t bitmap[PMAXKB / 32];
   __shared__ uint16_t ulist[PMAXKB + 1];
   __shared__ uint16_t rlist[PQ][PLMAX + 2];  // odd word stride: rows in distinct banks
   __shared__ int n_union, dead;
   __shared__ int rlen[PQ];              // list length of each row
-  __shared__ float xchg[2][2][PQ];      // [step parity][block half][row]: row maxima, then sums
+  __shared__ float xchg[2][2][PQ];      // epilogue: [m | l][block half][row]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // heads fastest: the CTAs in flight share a query tile, so the heads of a GQA group
@@ -204,15 +208,18 @@ __global__ void __launch_bounds__(320, 1)
   if (tid == 0) {
     mbar_init(&q_full, 1);
     mbar_init(&o_done, 1);
-    for (int s = 0; s < PKST; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+    for (int s = 0; s < PKS; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < PVS; ++s) {
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
       mbar_init(&p_full[s], 2 * PQ);
       mbar_init(&pv_done[s], 1);
-      mbar_init(&xch[s], 2 * PQ);
     }
     dead = 0;
     mbar_fence_init();
@@ -293,83 +300,93 @@ __global__ void __launch_bounds__(320, 1)
   tc_fence_after();
   const int n = n_union;
   const int n_steps = (n + 1) >> 1;
-  const uint32_t tmem = tmem_base_sh;  // columns [0, 128): S / P 0, [128, 256): S / P 1, [256, 384): O
+  // columns [0, 128): S / P 0, [128, 256): S / P 1, [256, 384): O of each step's first
+  // block, [384, 512): O of its second block (merged in the epilogue)
+  const uint32_t tmem = tmem_base_sh;
 
   if (warp == 0) {
-    // ================= TMA producer
-    if (lane == 0 && n > 0) {
-      const int qrow = static_cast<int>((b * p.Hq + h) * p.Tq + t0);
-      mbar_arrive_expect_tx(&q_full, QBYTES);
-      tma_load_2d(sq, &tmq, 0, qrow, &q_full);
-      tma_load_2d(sq + PQ * 128, &tmq, 64, qrow, &q_full);
+    // ================= TMA producers: lane 0 Q and K (ahead by PKS steps), lane 1 V
+    if (lane < 2 && n > 0) {
+      const bool is_k = lane == 0;
+      const CUtensorMap* tm = is_k ? &tmk : &tmv;
+      uint8_t* ring = is_k ? sk : sv_ring;
+      uint64_t* full = is_k ? k_full : v_full;
+      uint64_t* empty = is_k ? k_empty : v_empty;
+      const int nst = is_k ? PKS : PVS;
+      if (is_k) {
+        const int qrow = static_cast<int>((b * p.Hq + h) * p.Tq + t0);
+        mbar_arrive_expect_tx(&q_full, QBYTES);
+        tma_load_2d(sq, &tmq, 0, qrow, &q_full);
+        tma_load_2d(sq + PQ * 128, &tmq, 64, qrow, &q_full);
+      }
       const int64_t kv0 = (b * p.Hkv + kvh) * p.Tk;
       auto row_of = [&](int e) { return static_cast<int>(kv0 + static_cast<int64_t>(ulist[e]) * PK); };
-      auto prefetch_step = [&](int j) {
-        tma_prefetch_kv(&tmk, &tmv, row_of(2 * j));
-        tma_prefetch_kv(&tmk, &tmv, row_of(2 * j + 1));
+      auto prefetch_step = [&](int j) {  // warm L2 (no shared memory involved)
+        tma_prefetch_2d(tm, 0, row_of(2 * j));
+        tma_prefetch_2d(tm, 64, row_of(2 * j));
+        tma_prefetch_2d(tm, 0, row_of(2 * j + 1));
+        tma_prefetch_2d(tm, 64, row_of(2 * j + 1));
       };
       int issued = 0;
       for (int j = 0; j < n_steps; ++j) {
-        const int st = j % PKST;
-        if (j >= PKST && !mbar_wait_bounded(&kv_empty[st], static_cast<uint32_t>(((j / PKST) - 1) & 1))) {
+        const int st = j % nst;
+        if (j >= nst && !mbar_wait_bounded(&empty[st], static_cast<uint32_t>(((j / nst) - 1) & 1))) {
           report(p.status, LINATTN_DEV_TIMEOUT);
           dead = 1;
           break;
         }
         if (dead) break;
-        uint8_t* dst = skv + st * STAGE;
+        uint8_t* dst = ring + st * TILE;
         const int ya = row_of(2 * j), yb = row_of(2 * j + 1);
-        mbar_arrive_expect_tx(&kv_full[st], STAGE);
+        mbar_arrive_expect_tx(&full[st], TILE);
         // 128 key rows per channel half: block a rows 0-63, block b rows 64-127
-        tma_load_2d(dst, &tmk, 0, ya, &kv_full[st]);
-        tma_load_2d(dst + BOXB, &tmk, 0, yb, &kv_full[st]);
-        tma_load_2d(dst + HALFB, &tmk, 64, ya, &kv_full[st]);
-        tma_load_2d(dst + HALFB + BOXB, &tmk, 64, yb, &kv_full[st]);
-        tma_load_2d(dst + 2 * HALFB, &tmv, 0, ya, &kv_full[st]);
-        tma_load_2d(dst + 2 * HALFB + BOXB, &tmv, 0, yb, &kv_full[st]);
-        tma_load_2d(dst + 3 * HALFB, &tmv, 64, ya, &kv_full[st]);
-        tma_load_2d(dst + 3 * HALFB + BOXB, &tmv, 64, yb, &kv_full[st]);
+        tma_load_2d(dst, tm, 0, ya, &full[st]);
+        tma_load_2d(dst + BOXB, tm, 0, yb, &full[st]);
+        tma_load_2d(dst + HALFB, tm, 64, ya, &full[st]);
+        tma_load_2d(dst + HALFB + BOXB, tm, 64, yb, &full[st]);
         issued = j + 1;
-        // warm L2 with the steps PPF further on (no shared memory involved)
         if (j == 0)
           for (int f = 1; f <= PPF && f < n_steps; ++f) prefetch_step(f);
         if (j + PPF + 1 < n_steps) prefetch_step(j + PPF + 1);
       }
       if (dead) {
         // let the copies in flight land (bounded) before the CTA gives up its smem
-        for (int j = issued > PKST ? issued - PKST : 0; j < issued; ++j)
-          (void)mbar_wait_bounded(&kv_full[j % PKST], static_cast<uint32_t>((j / PKST) & 1), 200000000ull);
+        for (int j = issued > nst ? issued - nst : 0; j < issued; ++j)
+          (void)mbar_wait_bounded(&full[j % nst], static_cast<uint32_t>((j / nst) & 1), 200000000ull);
       }
     }
   } else if (warp == 1) {
     // ================= MMA issuer
     if (lane == 0 && n > 0) {
       bool ok = mbar_wait_bounded(&q_full, 0);
-      const uint32_t sq_a = smem_u32(sq), skv_a = smem_u32(skv);
+      const uint32_t sq_a = smem_u32(sq), sk_a = smem_u32(sk), sv_a = smem_u32(sv_ring);
       auto pv = [&](int j) -> bool {
         const int pb = j & 1;
         if (!mbar_wait_bounded(&p_full[pb], static_cast<uint32_t>((j >> 1) & 1))) return false;
+        if (!mbar_wait_bounded(&v_full[j % PVS], static_cast<uint32_t>((j / PVS) & 1))) return false;
         tc_fence_after();
-        const uint32_t vb = skv_a + (j % PKST) * STAGE + 2 * HALFB;
+        const uint32_t vb = sv_a + (j % PVS) * TILE;
         const uint32_t pt = tmem + pb * 128;  // P of step j, over its scores
+        // block half hb of the step (64 keys, P columns [32 hb, 32 hb + 32)) into O_hb
 #pragma unroll
         for (int kk = 0; kk < PSTEP / 16; ++kk) {
+          const uint32_t od = tmem + 256 + (kk >> 2) * 128;
           const uint64_t bd = umma_desc(vb + kk * 2048, HALFB, 1024);
-          umma_f16_ts(tmem + 256, pt + kk * 8, bd, IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
-          if (SPLIT) umma_f16_ts(tmem + 256, pt + 64 + kk * 8, bd, IDESC_O, 1u);
+          umma_f16_ts(od, pt + kk * 8, bd, IDESC_O, (j > 0 || (kk & 3) > 0) ? 1u : 0u);
+          if (SPLIT) umma_f16_ts(od, pt + 64 + kk * 8, bd, IDESC_O, 1u);
         }
         umma_commit(&pv_done[pb]);
-        umma_commit(&kv_empty[j % PKST]);
+        umma_commit(&v_empty[j % PVS]);
         return true;
       };
       for (int j = 0; ok && j < n_steps; ++j) {
-        const int st = j % PKST, sb = j & 1;
-        ok = mbar_wait_bounded(&kv_full[st], static_cast<uint32_t>((j / PKST) & 1));
+        const int st = j % PKS, sb = j & 1;
+        ok = mbar_wait_bounded(&k_full[st], static_cast<uint32_t>((j / PKS) & 1));
         if (!ok) break;
         tc_fence_after();
         // S_j into buffer sb: its previous P (step j - 2) is read by PV_{j-2}, issued
         // before this point; MMAs run in issue order
-        const uint32_t kb = skv_a + st * STAGE;
+        const uint32_t kb = sk_a + st * TILE;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint64_t a = umma_desc(sq_a + (kk >> 2) * (PQ * 128) + (kk & 3) * 32, 16, 1024);
@@ -377,6 +394,7 @@ __global__ void __launch_bounds__(320, 1)
           umma_f16(tmem + sb * 128, a, bd, IDESC_S, kk > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[sb]);
+        umma_commit(&k_empty[st]);
         if (j >= 1) ok = pv(j - 1);
       }
       if (ok) ok = pv(n_steps - 1);
@@ -392,6 +410,8 @@ __global__ void __launch_bounds__(320, 1)
     float m_used = -INFINITY, l = 0.f;
     int ptr = 0;
     bool ok = true;
+    const int sink32 = static_cast<int>(lmin(p.sink, int64_t(1) << 30)), tk32 = static_cast<int>(p.Tk);
+    const int pos32 = static_cast<int>(lmax(lmin(pos, int64_t(1) << 30), -(int64_t(1) << 30)));
     for (int j = 0; j < n_steps; ++j) {
       const int sb = j & 1;
       if (!__all_sync(0xffffffffu, mbar_wait_bounded(&s_full[sb], static_cast<uint32_t>((j >> 1) & 1)))) {
@@ -413,12 +433,13 @@ __global__ void __launch_bounds__(320, 1)
           while (ptr < my_n && rlist[r][ptr] < blk) ++ptr;
           member = row_ok && ptr < my_n && rlist[r][ptr] == blk;
         }
-        const int64_t key0 = static_cast<int64_t>(blk) * PK;
-        int64_t kend = member ? PK : (e < n ? lmin(PK, p.sink - key0) : 0);
+        // 32-bit: T_k <= 2^18 and |offset + t| < 2^31 (checked on the host)
+        const int key0 = blk * PK;
+        int kend = member ? PK : (e < n ? min(PK, sink32 - key0) : 0);
         if (!row_ok) kend = 0;
-        kend = lmin(kend, p.Tk - key0);
-        if (p.causal) kend = lmin(kend, pos - key0 + 1);
-        ke = static_cast<int>(lmax(0, kend));
+        kend = min(kend, tk32 - key0);
+        if (p.causal) kend = min(kend, pos32 - key0 + 1);
+        ke = max(0, kend);
       }
       // raw scores; masks only where needed (scale > 0: max of raw = max / scale)
       float mx8[8];
@@ -437,18 +458,9 @@ __global__ void __launch_bounds__(320, 1)
       }
       const float mloc = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-      // the pair's row maximum, through an mbarrier of the eight softmax warps (bounded
-      // wait; double-buffered by step parity: the partner has read this slot before
-      // either writes it again two steps later)
-      xchg[sb][hb][r] = mloc;
-      mbar_arrive(&xch[sb]);
-      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&xch[sb], static_cast<uint32_t>((j >> 1) & 1)))) {
-        ok = false;
-        break;
-      }
-      const float mx = fmaxf(mloc, xchg[sb][hb ^ 1][r]) * p.scale_log2;
-      // running maximum: moved (and O rescaled) only when it grows by more than 8; both
-      // threads of a row take the same decision from the same values
+      // this half's running maximum: moved (and O_hb rescaled) only when it grows by
+      // more than 8; the two halves keep their own (O, m, l), merged in the epilogue
+      const float mx = mloc * p.scale_log2;
       const bool first = mx > -INFINITY && m_used == -INFINITY;
       const bool grow = mx > -INFINITY && m_used != -INFINITY && mx > m_used + 8.f;
       if (__any_sync(0xffffffffu, grow)) {
@@ -462,9 +474,9 @@ __global__ void __launch_bounds__(320, 1)
         }
         tc_fence_after();
 #pragma unroll 1
-        for (int cc = 0; cc < 2; ++cc) {  // this thread's 64 channels of O
+        for (int cc = 0; cc < 4; ++cc) {  // O_hb of this row
           uint32_t ov[32];
-          const uint32_t oa = lane_addr + 256 + hb * 64 + cc * 32;
+          const uint32_t oa = lane_addr + 256 + hb * 128 + cc * 32;
           tmem_ld32(oa, ov);
           tmem_wait_ld();
 #pragma unroll
@@ -514,12 +526,18 @@ __global__ void __launch_bounds__(320, 1)
       report(p.status, LINATTN_DEV_TIMEOUT);
       dead = 1;
     }
-    // the row sum of the pair (both halves use the same running maximum); slot
-    // n_steps & 1 was last written at step n_steps - 2, read before that step's barrier
-    const int slot = n_steps & 1;
-    xchg[slot][hb][r] = l;
-    asm volatile("bar.sync 2, 256;" ::: "memory");
-    l += xchg[slot][hb ^ 1][r];
+    // merge the halves: O = (O_0 2^(m_0 - M) + O_1 2^(m_1 - M)) / (l_0 2^(m_0 - M) + l_1 2^(m_1 - M)),
+    // thread hb producing channels [64 hb, 64 hb + 64) from both accumulators
+    xchg[0][hb][r] = m_used;
+    xchg[1][hb][r] = l;
+    asm volatile("bar.sync 2, 256;" ::: "memory");  // every softmax thread reaches this point
+    const float m_o = xchg[0][hb ^ 1][r], l_o = xchg[1][hb ^ 1][r];
+    const float m_all = fmaxf(m_used, m_o);
+    const float f_me = m_used == -INFINITY ? 0.f : ex2_approx(m_used - m_all);
+    const float f_o = m_o == -INFINITY ? 0.f : ex2_approx(m_o - m_all);
+    const float f0 = hb == 0 ? f_me : f_o, f1 = hb == 0 ? f_o : f_me;
+    l = l * f_me + l_o * f_o;
+    m_used = m_all;
     tc_fence_after();
     const float inv = l > 0.f ? 1.f / l : 0.f;
     const int64_t ob = b * p.os[0] + h * p.os[1] + t * p.os[2];
@@ -530,8 +548,13 @@ __global__ void __launch_bounds__(320, 1)
     for (int cc = 0; cc < 2; ++cc) {  // this thread's 64 channels
       uint32_t ov[32];
       if (ok && n_steps > 0) {  // warp-uniform
+        uint32_t o1[32];
         tmem_ld32(lane_addr + 256 + hb * 64 + cc * 32, ov);
+        tmem_ld32(lane_addr + 384 + hb * 64 + cc * 32, o1);
         tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          ov[i] = __float_as_uint(__uint_as_float(ov[i]) * f0 + __uint_as_float(o1[i]) * f1);
       } else {
 #pragma unroll
         for (int i = 0; i < 32; ++i) ov[i] = 0u;
@@ -626,6 +649,8 @@ extern "C" int linattn_block_sparse_prefill(const void* q, int32_t dtype, int64_
     return set_error(LINATTN_EINVAL, "block_sparse_prefill: q / K / V must be 16-byte aligned");
   if (B * Hq * Tq >= (int64_t(1) << 31) || B * Hkv * Tk >= (int64_t(1) << 31))
     return set_error(LINATTN_EUNSUPPORTED, "block_sparse_prefill: too many rows for 32-bit TMA coordinates");
+  if (offset < -(int64_t(1) << 30) || offset + Tq >= (int64_t(1) << 30))
+    return set_error(LINATTN_EUNSUPPORTED, "block_sparse_prefill: query positions must lie in (-2^30, 2^30)");
   if (B == 0 || Hq == 0 || Tq == 0) return LINATTN_OK;
   // q / K / V: contiguous (B, H, T, 128) rows, viewed as 2-D [rows, 128]
   const CUtensorMapDataType cu = dtype == LINATTN_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
