@@ -175,8 +175,9 @@ int linattn_page_topk(const float* scores, int64_t B, int64_t Hq, int64_t Tq, in
  * query head and the union per kv head in one kernel (one CTA per sequence and kv
  * head).  Metadata is [B, H_kv, max_pages, 2, D] (logical page order, min row then
  * max row, f16/bf16).  The query of sequence b sits at position seq_lens[b] - 1: pages
- * below n_pages_b[b] are visible, the last one and the first `sink_pages` are forced
- * in.  ids (B, H_q, topk) int32 sorted by (score desc, page asc), -1 padded; scores
+ * below n_pages_b[b] are visible; the first `sink_pages` and, with `force_last`, the last
+ * one are forced in (a shard of a sequence-sharded cache that does not hold the query's
+ * page passes force_last = 0).  ids (B, H_q, topk) int32 sorted by (score desc, page asc), -1 padded; scores
  * (B, H_q, max_pages) optional; union_ids (B, H_kv, max_union) ascending with counts
  * and token counts.  Group size H_q / H_kv in {1, 2, 4, 8}; D in {64, 128}.
  * Replaces, for T_q == 1, page_select_torch (src/linattn/kernels/triton/quest_pages.py:57-78)
@@ -187,8 +188,9 @@ int linattn_quest_decode_select(const void* q, int32_t q_dtype, int64_t B, int64
                                 const int64_t* q_strides /*[4]*/, const void* meta, int32_t meta_dtype,
                                 int64_t n_kv_heads, int64_t max_pages, const int32_t* n_pages_b,
                                 const int32_t* seq_lens, int64_t page_size, int64_t topk, int32_t sink_pages,
-                                int32_t* ids, float* scores, int32_t* union_ids, int32_t* union_count,
-                                int64_t max_union, int32_t* union_tokens, int32_t* status, void* stream);
+                                int32_t force_last, int32_t* ids, float* scores, int32_t* union_ids,
+                                int32_t* union_count, int64_t max_union, int32_t* union_tokens, int32_t* status,
+                                void* stream);
 
 /*
  * Exact softmax attention of each query over the KV rows of its list's pages.
@@ -207,6 +209,18 @@ int linattn_sparse_attention(const void* q, int32_t q_dtype, int64_t B, int64_t 
                              const linattn_lists_t* lists, int32_t causal, int64_t offset, float scale,
                              void* out, const int64_t* out_strides /*[4]*/, float* lse_out, int32_t n_splits,
                              float* workspace, int64_t workspace_bytes, int32_t* status, void* stream);
+
+/*
+ * linattn_sparse_attention with an explicit output dtype (f32, f16 or bf16): f32 keeps
+ * the partial results of a sequence-sharded decode at full precision until their
+ * log-sum-exp merge (linattn_lse_combine).  No counterpart in the reference.
+ */
+int linattn_sparse_attention_out(const void* q, int32_t q_dtype, int64_t B, int64_t Hq, int64_t Tq,
+                                 const int64_t* q_strides /*[4]*/, const linattn_kv_t* kv,
+                                 const linattn_lists_t* lists, int32_t causal, int64_t offset, float scale,
+                                 void* out, int32_t out_dtype, const int64_t* out_strides /*[4]*/, float* lse_out,
+                                 int32_t n_splits, float* workspace, int64_t workspace_bytes, int32_t* status,
+                                 void* stream);
 
 /* Workspace bytes linattn_sparse_attention needs for n_splits > 1. */
 int64_t linattn_sparse_attention_workspace(int64_t B, int64_t Hq, int64_t Tq, int64_t D, int32_t n_splits);
@@ -356,6 +370,23 @@ int linattn_block_sparse_prefill(const void* q, int32_t dtype, int64_t B, int64_
                                  int64_t rows_per_list, const int64_t* count_strides /*[3]*/, int64_t sink,
                                  int32_t causal, int64_t offset, float scale, void* out,
                                  const int64_t* out_strides /*[4]*/, float* lse_out, int32_t* status, void* stream);
+
+/*
+ * Sequence-sharded Quest decode, merge step.  scores / ids (R, B, H_q, K): the R
+ * shards' local top-K candidates (fp32 scores, global page ids, -1 = none), rank-major
+ * as an all-gather leaves them.  Per (b, query head) the global top-`topk` by (score
+ * desc, page asc) is taken (written to sel (B, H_q, topk), -1 padded, when sel is not
+ * NULL); the pages of this shard, [page_lo[b], page_hi[b]), selected by any head of a
+ * kv head's group go to union_ids (B, H_kv, max_union) as ascending LOCAL ids
+ * (page - page_lo[b]), -1 padded, with union_count (B, H_kv).  R * K <= 4096.
+ * No counterpart in the reference (which never shards the KV sequence); the selection
+ * equals page_select_torch's (src/linattn/kernels/triton/quest_pages.py:57-78) over
+ * the whole cache.
+ */
+int linattn_shard_merge(const float* scores, const int32_t* ids, int64_t R, int64_t B, int64_t Hq, int64_t K,
+                        int64_t topk, int64_t n_kv_heads, const int32_t* page_lo, const int32_t* page_hi,
+                        int64_t max_local, int32_t* sel, int32_t* union_ids, int32_t* union_count,
+                        int64_t max_union, void* stream);
 
 #ifdef __cplusplus
 }

@@ -89,6 +89,10 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.linattn_sparse_attention.argtypes = [c_vp, c_i32, c_i64, c_i64, c_i64, P(c_i64), P(KV), P(Lists), c_i32,
                                              c_i64, ctypes.c_float, c_vp, P(c_i64), c_vp, c_i32, c_vp, c_i64, c_vp,
                                              c_vp]
+    lib.linattn_sparse_attention_out.argtypes = [c_vp, c_i32, c_i64, c_i64, c_i64, P(c_i64), P(KV), P(Lists), c_i32,
+                                                 c_i64, ctypes.c_float, c_vp, c_i32, P(c_i64), c_vp, c_i32, c_vp,
+                                                 c_i64, c_vp, c_vp]
+    lib.linattn_sparse_attention_out.restype = ctypes.c_int
     lib.linattn_sparse_attention_workspace.argtypes = [c_i64, c_i64, c_i64, c_i64, c_i32]
     lib.linattn_sparse_attention_workspace.restype = c_i64
     lib.linattn_lse_combine.argtypes = [c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_i32, c_vp, c_vp]
@@ -98,8 +102,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.linattn_sparse_attention_noalloc.restype = ctypes.c_int
     lib.linattn_sparse_attention_noalloc_limit.restype = c_i64
     lib.linattn_quest_decode_select.argtypes = [c_vp, c_i32, c_i64, c_i64, c_i64, P(c_i64), c_vp, c_i32, c_i64, c_i64,
-                                                c_vp, c_vp, c_i64, c_i64, c_i32, c_vp, c_vp, c_vp, c_vp, c_i64, c_vp,
-                                                c_vp, c_vp]
+                                                c_vp, c_vp, c_i64, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp, c_i64,
+                                                c_vp, c_vp, c_vp]
     lib.linattn_quest_decode_select.restype = ctypes.c_int
     lib.linattn_indexer_scores.argtypes = [c_vp, c_i32, P(c_i64), c_vp, c_i32, P(c_i64), c_vp, c_i64, c_i64, c_vp,
                                            c_i32, P(c_i64), c_i64, c_i64, c_i64, c_i64, c_i64, c_i32, c_i64, c_i64,
@@ -115,7 +119,9 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.linattn_block_sparse_prefill.argtypes = [c_vp, c_i32, c_i64, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64,
                                                  c_vp, c_vp, P(c_i64), c_i64, c_i64, P(c_i64), c_i64, c_i32, c_i64,
                                                  ctypes.c_float, c_vp, P(c_i64), c_vp, c_vp, c_vp]
-    for name in ("linattn_block_sparse_prefill", "linattn_block_mean", "linattn_merge_block_lists", "linattn_token_attention", "linattn_indexer_scores", "linattn_row_topk", "linattn_page_bounds", "linattn_paged_page_bounds", "linattn_quest_scores", "linattn_page_topk",
+    lib.linattn_shard_merge.argtypes = [c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_i64, c_vp,
+                                        c_vp, c_vp, c_i64, c_vp]
+    for name in ("linattn_shard_merge", "linattn_block_sparse_prefill", "linattn_block_mean", "linattn_merge_block_lists", "linattn_token_attention", "linattn_indexer_scores", "linattn_row_topk", "linattn_page_bounds", "linattn_paged_page_bounds", "linattn_quest_scores", "linattn_page_topk",
                  "linattn_sparse_attention", "linattn_lse_combine"):
         getattr(lib, name).restype = ctypes.c_int
 

@@ -214,7 +214,18 @@ int linattn_sparse_attention(const void* q, int32_t q_dtype, int64_t B, int64_t 
                              int32_t causal, int64_t offset, float scale, void* out, const int64_t* out_strides,
                              float* lse_out, int32_t n_splits, float* workspace, int64_t workspace_bytes,
                              int32_t* status, void* stream) {
+  return linattn_sparse_attention_out(q, q_dtype, B, Hq, Tq, q_strides, kv, lists, causal, offset, scale, out,
+                                      q_dtype, out_strides, lse_out, n_splits, workspace, workspace_bytes, status,
+                                      stream);
+}
+
+int linattn_sparse_attention_out(const void* q, int32_t q_dtype, int64_t B, int64_t Hq, int64_t Tq,
+                                 const int64_t* q_strides, const linattn_kv_t* kv, const linattn_lists_t* lists,
+                                 int32_t causal, int64_t offset, float scale, void* out, int32_t out_dtype,
+                                 const int64_t* out_strides, float* lse_out, int32_t n_splits, float* workspace,
+                                 int64_t workspace_bytes, int32_t* status, void* stream) {
   int rc = check_kv(kv);
+  if (!is_float16_32(out_dtype)) return fail(LINATTN_EUNSUPPORTED, "sparse_attention: out dtype %d", out_dtype);
   if (rc) return rc;
   if (!q || !q_strides || !out || !out_strides || !lists || !lists->ids)
     return fail(LINATTN_EINVAL, "sparse_attention: NULL pointer");
@@ -237,7 +248,7 @@ int linattn_sparse_attention(const void* q, int32_t q_dtype, int64_t B, int64_t 
   const int64_t rows = B * Hq * Tq;
   if (rows == 0) return LINATTN_OK;
   AttnParams p;
-  p.q = q; p.q_dtype = q_dtype; p.B = B; p.Hq = Hq; p.Tq = Tq;
+  p.q = q; p.q_dtype = q_dtype; p.out_dtype = out_dtype; p.B = B; p.Hq = Hq; p.Tq = Tq;
   for (int i = 0; i < 4; ++i) { p.qs[i] = q_strides[i]; p.os[i] = out_strides[i]; }
   p.kv = *kv; p.lists = *lists; p.causal = causal; p.offset = offset;
   p.scale_log2 = scale * 1.4426950408889634f;
@@ -306,7 +317,7 @@ int linattn_sparse_attention(const void* q, int32_t q_dtype, int64_t B, int64_t 
   }
   rc = cuda_status(e, "sparse_attention");
   if (rc || n_splits == 1) return rc;
-  return cuda_status(launch_lse_combine(p.ws_o, p.ws_lse, n_splits, rows, D, out, q_dtype, Hq, Tq, out_strides,
+  return cuda_status(launch_lse_combine(p.ws_o, p.ws_lse, n_splits, rows, D, out, out_dtype, Hq, Tq, out_strides,
                                         lse_out, st),
                      "sparse_attention combine");
 }

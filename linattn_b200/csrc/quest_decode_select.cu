@@ -60,6 +60,7 @@ struct DecodeSelectParams {
   int64_t P;
   int topk;
   int sink_pages;
+  int force_last;  // the own (last visible) page is forced in
   int32_t* ids;      // (B, Hq, topk)
   float* scores;     // optional (B, Hq, max_pages)
   int32_t* union_ids;
@@ -152,7 +153,7 @@ __global__ void __launch_bounds__(256, 1) quest_decode_select_kernel(const Decod
       group_reduce<G, LPR>(acc, lane);
       if (pg < pages && (cl % REP) == 0) {
         const int64_t page = c * CH + pg;
-        const bool forced = page == nb - 1 || page < p.sink_pages;
+        const bool forced = (p.force_last && page == nb - 1) || page < p.sink_pages;
 #pragma unroll
         for (int i = 0; i < NV; ++i) {
           const int g = G >= LPR ? cl * NV + i : cl / REP;
@@ -342,7 +343,8 @@ extern "C" int linattn_quest_decode_select(const void* q, int32_t q_dtype, int64
                                            const int64_t* q_strides, const void* meta, int32_t meta_dtype,
                                            int64_t n_kv_heads, int64_t max_pages, const int32_t* n_pages_b,
                                            const int32_t* seq_lens, int64_t page_size, int64_t topk,
-                                           int32_t sink_pages, int32_t* ids, float* scores, int32_t* union_ids,
+                                           int32_t sink_pages, int32_t force_last, int32_t* ids, float* scores,
+                                           int32_t* union_ids,
                                            int32_t* union_count, int64_t max_union, int32_t* union_tokens,
                                            int32_t* status, void* stream) {
   if (!q || !q_strides || !meta || !n_pages_b || !seq_lens || !ids || !union_ids || !union_count)
@@ -367,7 +369,8 @@ extern "C" int linattn_quest_decode_select(const void* q, int32_t q_dtype, int64
   p.q = q; p.q_dtype = q_dtype; p.B = B; p.Hq = Hq; p.Hkv = n_kv_heads;
   for (int i = 0; i < 4; ++i) p.qs[i] = q_strides[i];
   p.meta = meta; p.max_pages = max_pages; p.n_pages_b = n_pages_b; p.seq_lens = seq_lens; p.P = page_size;
-  p.topk = static_cast<int>(topk); p.sink_pages = sink_pages; p.ids = ids; p.scores = scores;
+  p.topk = static_cast<int>(topk); p.sink_pages = sink_pages; p.force_last = force_last ? 1 : 0;
+  p.ids = ids; p.scores = scores;
   p.union_ids = union_ids; p.union_count = union_count; p.max_union = max_union; p.union_tokens = union_tokens;
   p.status = status;
   cudaStream_t st = static_cast<cudaStream_t>(stream);

@@ -24,6 +24,7 @@ namespace linattn {
 struct AttnParams {
   const void* q;
   int q_dtype;
+  int out_dtype;  // of `out` (q's dtype, or f32 for partials that are merged later)
   int64_t B, Hq, Tq;
   int64_t qs[4];
   linattn_kv_t kv;
@@ -370,7 +371,7 @@ __global__ void __launch_bounds__(256, 2) sparse_attention_kernel(const AttnPara
     const int64_t row = (b * p.Hq + h) * p.Tq + t;
     const float lse = l > 0.f ? (m_fin[g] + log2f(l)) * 0.69314718055994531f : -INFINITY;
     if (p.n_splits == 1) {
-      store_any(p.out, b * p.os[0] + h * p.os[1] + t * p.os[2] + c * p.os[3], p.q_dtype, o);
+      store_any(p.out, b * p.os[0] + h * p.os[1] + t * p.os[2] + c * p.os[3], p.out_dtype, o);
       if (p.lse_out && c == 0) p.lse_out[row] = lse;
     } else {
       p.ws_o[(static_cast<int64_t>(split) * rows_total + row) * D + c] = o;

@@ -205,7 +205,7 @@ __global__ void __launch_bounds__(32 * MmaShape<D>::NW, 1)
           const int64_t row = (b * p.Hq + h) * p.Tq + t;
           if (p.n_splits == 1) {
             for (int cc = lane; cc < D; cc += 32)
-              store_any(p.out, b * p.os[0] + h * p.os[1] + t * p.os[2] + cc * p.os[3], p.q_dtype, 0.f);
+              store_any(p.out, b * p.os[0] + h * p.os[1] + t * p.os[2] + cc * p.os[3], p.out_dtype, 0.f);
             if (p.lse_out && lane == 0) p.lse_out[row] = -INFINITY;
           } else if (lane == 0) {
             p.ws_lse[static_cast<int64_t>(split) * rows_total + row] = -INFINITY;
@@ -496,8 +496,8 @@ __global__ void __launch_bounds__(32 * MmaShape<D>::NW, 1)
           const int64_t ob = static_cast<int64_t>(cb) * p.os[0] + h * p.os[1] + static_cast<int64_t>(ct) * p.os[2];
 #pragma unroll
           for (int dm = 0; dm < S::KS; ++dm) {
-            store_any(p.out, ob + (dm * 16 + tk) * p.os[3], p.q_dtype, o[dm][j] * inv);
-            store_any(p.out, ob + (dm * 16 + tk + 8) * p.os[3], p.q_dtype, o[dm][2 + j] * inv);
+            store_any(p.out, ob + (dm * 16 + tk) * p.os[3], p.out_dtype, o[dm][j] * inv);
+            store_any(p.out, ob + (dm * 16 + tk + 8) * p.os[3], p.out_dtype, o[dm][2 + j] * inv);
           }
           if (p.lse_out && tk == 0) p.lse_out[row] = j ? lseB : lseA;
         } else {

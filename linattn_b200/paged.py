@@ -199,8 +199,10 @@ class QuestDecoder:
 
     def __init__(self, cache: PagedKVCache, n_heads: int, topk: int, *, sink_pages: int = 0,
                  scale: Optional[float] = None, gqa_union: bool = True, n_splits: Optional[int] = None,
-                 q_dtype: torch.dtype = torch.bfloat16, keep_scores: bool = False):
+                 q_dtype: torch.dtype = torch.bfloat16, keep_scores: bool = False, force_last: bool = True):
         self.cache = cache
+        # False on a shard of a sequence-sharded cache that does not hold the query's page
+        self.force_last = force_last
         self.n_heads = n_heads
         self.group = n_heads // cache.n_kv_heads if gqa_union else 1
         self.topk = max(1, min(topk, cache.max_pages))
@@ -245,7 +247,8 @@ class QuestDecoder:
             L.check(lib.linattn_quest_decode_select(
                 q.data_ptr(), L.dtype_code(q), b, hq, d, L.strides4(q), c.meta.data_ptr(), L.dtype_code(c.meta),
                 c.n_kv_heads, c.max_pages, c.n_pages_b.data_ptr(), c.seq_lens.data_ptr(), c.page_size, self.topk,
-                self.sink_pages, self.ids.data_ptr(), L.ptr(self.scores), self.union_ids.data_ptr(),
+                self.sink_pages, int(self.force_last), self.ids.data_ptr(), L.ptr(self.scores),
+                self.union_ids.data_ptr(),
                 self.union_count.data_ptr(), self.max_union, self.union_tokens.data_ptr(), status.data_ptr(), stream))
             return QuestSelection(self.ids, self.scores, self.union_ids, self.union_count, self.union_tokens)
         L.check(lib.linattn_quest_scores(q.data_ptr(), L.dtype_code(q), b, hq, tq, d, L.strides4(q), c.meta_desc(),
