@@ -14,6 +14,14 @@ GQA union per kv head.  A step = page scoring + top-k/union + sparse attention
 prints one JSON line.  For N > 1 (torchrun) every rank runs its own 16 sequences
 (weak scaling, no data-path collective) and the step time is the max over ranks.
 ``--impl reference`` times the reference's CPU path on the host cores (rank 0 only).
+At N = 1 the line also carries ``secondary``: config 4 (block selection + tcgen05
+block-sparse causal prefill, B=2, T=131072; its TFLOP/s is ``prefill_tflops``) and
+config 3 (lightning indexer + causal top-2048 + token attention, T=32768), each timed
+with CUDA events over a few steps with the L2 flushed before each.
+
+``--workload c5`` runs config 5 instead: B=64 sequences of 1,048,576 tokens (fp8 KV)
+split across the N ranks (strong scaling), with NCCL all-gathers of the selection
+candidates and of the partial (o, lse).
 """
 
 from __future__ import annotations
@@ -38,6 +46,9 @@ if str(ROOT) not in sys.path:
 
 METRIC = "sparse decode tok/s + HBM GB/s @64K ctx; prefill TFLOP/s @128K; % roofline"
 C2 = dict(B=16, Hq=32, Hkv=8, D=128, T=65536, P=64, topk=34, sink_pages=1, needle_frac=0.01)
+C3 = dict(B=1, T=32768, Hq=32, Hkv=8, D=128, HI=4, DI=64, topk=2048, scale_group=64)
+C4 = dict(B=2, T=131072, Hq=32, Hkv=8, D=128, block=64, sink_blocks=1, window_blocks=16, topk=16, rank=8, amp=0.5)
+C5 = dict(B=64, Hq=64, Hkv=8, D=128, T=1 << 20, P=64, topk=64, needle_frac=0.005)
 L2_FLUSH_BYTES = 256 << 20
 
 
@@ -156,6 +167,167 @@ def build_c2(device, seed: int, n_q: int, batch: int = C2["B"]):
     qs = (q0.unsqueeze(0) + 0.25 * torch.randn(n_q, b, hq, d, generator=gen, device=device))
     qs = qs.view(n_q, b, hq, 1, d).to(torch.bfloat16)
     return cache, qs
+
+
+def build_c5(device, rank: int, world: int, n_q: int, batch: int = C5["B"]):
+    """This rank's shard of the config-5 cache (pages [lo, hi) of every sequence, fp8
+    e4m3 with per-(page, kv head) scales, seeded N(0,1) values before quantisation,
+    0.5% needle pages at global positions shared by all ranks, a random page table over
+    the shard's pool) plus `n_q` step queries (identical on every rank)."""
+    from linattn_b200 import PagedKVCache
+    from linattn_b200.sharded import shard_page_ranges
+
+    c = C5
+    b, hq, hkv, d, t, p = batch, c["Hq"], c["Hkv"], c["D"], c["T"], c["P"]
+    n_glob = t // p
+    lo, hi = shard_page_ranges(n_glob, world, rank)
+    n_loc = hi - lo
+    n_phys = b * n_loc
+    cache = PagedKVCache(b, hkv, d, p, n_loc, num_phys_pages=n_phys, dtype=torch.float8_e4m3fn, device=device)
+    gen = torch.Generator(device=device).manual_seed(5000 + rank)
+
+    def quantise(x, pool, sc, at):
+        amax = x.abs().amax(dim=(2, 3)).clamp_min(1e-8)
+        scale = amax / torch.full_like(amax, 448.0)
+        pool[at] = (x / scale[:, :, None, None]).to(torch.float8_e4m3fn).view(torch.uint8)
+        sc[at] = scale
+
+    chunk = 1024
+    for s0 in range(0, n_phys, chunk):
+        s1 = min(n_phys, s0 + chunk)
+        for pool, sc in ((cache.k_pool, cache.k_scale), (cache.v_pool, cache.v_scale)):
+            quantise(torch.randn(s1 - s0, hkv, p, d, generator=gen, device=device), pool, sc, slice(s0, s1))
+    table = torch.randperm(n_phys, generator=gen, device=device).view(b, n_loc).to(torch.int32)
+    gq = torch.Generator(device=device).manual_seed(4242)  # same stream on every rank
+    q0 = torch.randn(b, hq, d, generator=gq, device=device)
+    u = torch.nn.functional.normalize(q0.view(b, hkv, hq // hkv, d).sum(2), dim=-1)
+    n_needle = max(1, int(round(c["needle_frac"] * n_glob)))
+    for bi in range(b):
+        pages = torch.randperm(n_glob, generator=gq, device=device)[:n_needle]
+        mine = pages[(pages >= lo) & (pages < hi)] - lo
+        if mine.numel() == 0:
+            continue
+        phys = table[bi, mine].long()
+        x = cache.k_pool[phys].view(torch.float8_e4m3fn).float() * cache.k_scale[phys][:, :, None, None]
+        quantise(x + (0.3 * math.sqrt(d)) * u[bi].view(1, hkv, 1, d), cache.k_pool, cache.k_scale, phys)
+    cache.set_page_table(table, [n_loc * p] * b)
+    cache.refresh_meta()
+    qs = (q0.unsqueeze(0) + 0.25 * torch.randn(n_q, b, hq, d, generator=gq, device=device))
+    return cache, qs.view(n_q, b, hq, 1, d).to(torch.bfloat16), (lo, hi)
+
+
+def build_c4(device, seed: int):
+    """Config-4 inputs: Q/K N(0,1) plus a shared rank-8 component of amplitude 0.5, V N(0,1), bf16."""
+    c = C4
+    b, hq, hkv, d, t = c["B"], c["Hq"], c["Hkv"], c["D"], c["T"]
+    g = torch.Generator(device=device).manual_seed(seed)
+    u = torch.randn(c["rank"], d, generator=g, device=device)
+    q = torch.randn(b, hq, t, d, generator=g, device=device)
+    q.add_(c["amp"] * torch.randn(b, hq, t, c["rank"], generator=g, device=device) @ u)
+    q = q.to(torch.bfloat16)
+    k = torch.randn(b, hkv, t, d, generator=g, device=device)
+    k.add_(c["amp"] * torch.randn(b, hkv, t, c["rank"], generator=g, device=device) @ u)
+    k = k.to(torch.bfloat16)
+    v = torch.randn(b, hkv, t, d, generator=g, device=device).to(torch.bfloat16)
+    return q, k, v
+
+
+def build_c3(device, seed: int):
+    """Config-3 inputs: bf16 Q/K/V N(0,1), indexer q/k N(0,1) with fp8 keys (per-64-token
+    scales), indexer weights N(0, 1/64)."""
+    from linattn_b200 import quantize_keys_fp8
+
+    c = C3
+    g = torch.Generator(device=device).manual_seed(seed)
+    b, t = c["B"], c["T"]
+    q = torch.randn(b, c["Hq"], t, c["D"], generator=g, device=device).to(torch.bfloat16)
+    k = torch.randn(b, c["Hkv"], t, c["D"], generator=g, device=device).to(torch.bfloat16)
+    v = torch.randn(b, c["Hkv"], t, c["D"], generator=g, device=device).to(torch.bfloat16)
+    q_idx = torch.randn(b, t, c["HI"], c["DI"], generator=g, device=device).to(torch.bfloat16)
+    k_idx = torch.randn(b, t, c["HI"], c["DI"], generator=g, device=device).to(torch.bfloat16)
+    w = (torch.randn(b, t, c["HI"], generator=g, device=device) / 8).to(torch.bfloat16)
+    codes, scales = quantize_keys_fp8(k_idx, c["scale_group"])
+    return q, k, v, q_idx, codes, scales, w
+
+
+def _time_events(fn_parts, steps: int, warmup: int, flush, stream):
+    """Runs the phases of one step (callables) `warmup` + `steps` times with an L2 flush
+    before every step; returns the mean ms of each phase over the timed steps."""
+    for _ in range(warmup):
+        flush.zero_()
+        for f in fn_parts:
+            f()
+    torch.cuda.synchronize()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(fn_parts) + 1)] for _ in range(steps)]
+    for i in range(steps):
+        flush.zero_()
+        ev[i][0].record(stream)
+        for j, f in enumerate(fn_parts):
+            f()
+            ev[i][j + 1].record(stream)
+    torch.cuda.synchronize()
+    return [statistics.mean(ev[i][j].elapsed_time(ev[i][j + 1]) for i in range(steps)) for j in range(len(fn_parts))]
+
+
+def secondary_c4(device, steps: int, warmup: int, flush, stream):
+    """Config 4 on this GPU: block selection + block-sparse causal prefill (tcgen05)."""
+    from linattn_b200.blocks import block_select, block_sparse_prefill
+
+    c = C4
+    q, k, v = build_c4(device, 44)
+    res = {}
+
+    def sel():
+        res["ids"], res["cnt"] = block_select(q, k, c["block"], c["topk"], sink_blocks=c["sink_blocks"],
+                                              window_blocks=c["window_blocks"])
+    sel()
+    out = torch.empty_like(q)
+
+    def att():
+        block_sparse_prefill(q, k, v, res["ids"], counts=res["cnt"], rows_per_list=c["block"], out=out)
+    ms_sel, ms_att = _time_events([sel, att], steps, warmup, flush, stream)
+    cnt = res["cnt"].long()
+    bs, d, t = c["block"], c["D"], c["T"]
+    # allowed (query, key) pairs, causal-exact: full 64x64 blocks off the diagonal, a triangle on it
+    pairs = (cnt - 1).sum().item() * bs * bs + c["B"] * c["Hq"] * (t // bs) * (bs * (bs + 1) // 2)
+    flops = 4 * d * pairs
+    _, peak, kind = measured_peaks()
+    tfl = flops / (ms_att * 1e-3) / 1e12
+    return {"workload": "block_sparse_prefill_c4", "B": c["B"], "T": t, "select_ms": round(ms_sel, 3),
+            "prefill_ms": round(ms_att, 3), "prefill_tflops": round(tfl, 1), "frac_of_bf16_peak": round(tfl / peak, 4),
+            "peak_kind": kind, "mean_blocks_per_query_block": round(cnt.float().mean().item(), 2),
+            "algorithmic_flops": int(flops), "end_to_end_tflops": round(flops / ((ms_sel + ms_att) * 1e-3) / 1e12, 1),
+            "launches_per_step": 5}
+
+
+def secondary_c3(device, steps: int, warmup: int, flush, stream):
+    """Config 3 on this GPU: lightning indexer + causal top-2048 + token attention."""
+    from linattn_b200 import indexer_topk
+    from linattn_b200.dsa import token_sparse_attention
+
+    c = C3
+    q, k, v, q_idx, codes, scales, w = build_c3(device, 33)
+    res = {}
+
+    def sel():
+        _, res["ids"] = indexer_topk(q_idx, codes, w, c["topk"], causal=True, k_scale=scales,
+                                     scale_group=c["scale_group"], index_dtype=torch.int32, sorted=False)
+    sel()
+    out = torch.empty_like(q)
+
+    def att():
+        token_sparse_attention(q, k, v, res["ids"].unsqueeze(1), causal=True, out=out)
+    ms_sel, ms_att = _time_events([sel, att], steps, warmup, flush, stream)
+    t, kk, d = c["T"], c["topk"], c["D"]
+    vis = sum(min(i + 1, kk) for i in range(t))  # selected tokens per query, causal
+    gather = vis * c["Hkv"] * d * 2 * 2
+    hbm, _, kind = measured_peaks()
+    return {"workload": "dsa_indexer_attention_c3", "T": t, "select_ms": round(ms_sel, 3),
+            "attention_ms": round(ms_att, 3), "total_ms": round(ms_sel + ms_att, 3),
+            "attention_gathered_gbs": round(gather / (ms_att * 1e-3) / 1e9, 1),
+            "attention_gathered_frac_of_hbm": round(gather / (ms_att * 1e-3) / 1e9 / hbm, 4), "peak_kind": kind,
+            "attention_tflops": round(4 * c["Hq"] * d * vis / (ms_att * 1e-3) / 1e12, 1),
+            "launches_per_step": 2 * -(-t // max(1, min(t, (1 << 29) // (t * 4)))) + 1}
 
 
 # ---------------------------------------------------------------------------------
@@ -351,12 +523,15 @@ def run_ours(args, rank, world, local_rank):
     qo_bytes = 2 * b * hq * d * elt
     meta_bytes = 2 * b * hkv * (t // p) * d * elt
     score_bytes = 0 if dec.fused else 2 * b * hq * (t // p) * 4  # the fused selection keeps scores on chip
+    if dec.fused and dec.chunks > 1:
+        score_bytes = 2 * dec.cand.numel() * 4  # candidates written by the chunk CTAs, read by the merge
     step_bytes = kv_bytes + qo_bytes + meta_bytes + score_bytes
     hbm_peak, _, peak_kind = measured_peaks()
     att_bytes = kv_bytes + qo_bytes
     achieved_att = att_bytes / (mean_att * 1e-3) / 1e9
     traffic = profile_traffic("sparse_attention_c2.md")
-    n_launch_step = 3 + (1 if dec.n_splits > 1 else 0)
+    # this library's kernels per step: selection (fused, or candidates + merge), attention, split merge
+    n_launch_step = (2 if dec.fused and dec.chunks > 1 else 1 if dec.fused else 2) + 1 + (1 if dec.n_splits > 1 else 0)
     clock = clocks.summary()
     line = {
         "metric": METRIC,
@@ -375,7 +550,7 @@ def run_ours(args, rank, world, local_rank):
                    "page_size": p, "n_heads": hq, "n_kv_heads": hkv, "head_dim": d,
                    "budget_pages": c["topk"], "sink_pages": c["sink_pages"], "parallelism": f"dp{world} (batch)",
                    "l2": "flushed (256 MiB write) before every step, outside the timed events",
-                   "n_splits": dec.n_splits},
+                   "n_splits": dec.n_splits, "select_chunks": dec.chunks},
         "hbm_gbs": round(step_bytes / (mean_step * 1e-3) / 1e9, 1),
         "step_breakdown_ms": {"select": round(mean_sel, 4), "attend": round(mean_att, 4)},
         "bytes_per_step": {"kv_union": int(kv_bytes), "meta": meta_bytes, "scores": score_bytes, "q_o": qo_bytes},
@@ -390,8 +565,13 @@ def run_ours(args, rank, world, local_rank):
                 "ms_per_step": round(e2e_ms, 4), "api": "linattn_b200.QuestDecoder.step"},
         "gpu_launches": n_launch_step * args.steps,
         "clocks": clock,
-        "prefill_tflops": None,
     }
+    if world == 1 and not args.no_secondary:
+        sec_steps, sec_warm = max(3, min(args.steps, 10)), 3
+        c4 = secondary_c4(device, sec_steps, sec_warm, flush, stream)
+        line["prefill_tflops"] = c4["prefill_tflops"]
+        line["secondary"] = {"block_sparse_prefill_c4": c4,
+                             "dsa_c3": secondary_c3(device, sec_steps, sec_warm, flush, stream)}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
         fn, kind, desc = cpu_reference_step_fn(cache, qs[args.warmup], 2, threads)
@@ -399,6 +579,158 @@ def run_ours(args, rank, world, local_rank):
         line["cpu_baseline"] = {"value": round(2 / sec, 3), "unit": "tok/s", "cores": threads, "kind": kind,
                                 "sample": desc + f"; {iters} timed iterations of {sec * 1e3:.1f} ms"}
     return line
+
+
+def run_c5(args, rank, world, local_rank):
+    """Config 5: million-token decode with the KV sequence split over the ranks (strong
+    scaling): local fused selection -> all-gather of (score, page) candidates -> global
+    top-k + owned GQA union -> fp32 partial attention -> all-gather of [o | lse] ->
+    log-sum-exp combine.  Both exchanges are NCCL all-gathers over NVLink (N > 1)."""
+    from linattn_b200.sharded import ShardedQuestDecoder, exchange_packed
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    c = C5
+    b, hq, hkv, d, t, p = args.batch or c["B"], c["Hq"], c["Hkv"], c["D"], c["T"], c["P"]
+    n_q = args.warmup + args.steps
+    t_build = time.perf_counter()
+    cache, qs, (lo, hi) = build_c5(device, rank, world, n_q, b)
+    torch.cuda.synchronize(device)
+    build_s = time.perf_counter() - t_build
+    n_glob = t // p
+    dec = ShardedQuestDecoder(cache, hq, c["topk"], [lo] * b, [hi] * b, last_here=(hi == n_glob),
+                              sink_here=(lo == 0))
+    exchange = (lambda x: exchange_packed(x)) if world > 1 else (lambda x: x.unsqueeze(0))
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    box = {}
+
+    def phase_select():
+        dec.candidates(box["q"])
+
+    def phase_merge():
+        dec.merge_packed(exchange(dec.cand))
+
+    def phase_attend():
+        dec.partial(box["q"])
+
+    def phase_combine():
+        dec.combine_packed(exchange(dec.part))
+
+    phases = [phase_select, phase_merge, phase_attend, phase_combine]
+    for i in range(args.warmup):
+        box["q"] = qs[i]
+        flush.zero_()
+        for f in phases:
+            f()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(device)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(phases) + 1)] for _ in range(args.steps)]
+    union_pages = torch.zeros(args.steps, dtype=torch.int64, device=device)
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+    phys_gpu = int(visible.split(",")[local_rank]) if visible else local_rank
+    with ClockSampler(phys_gpu) as clocks:
+        t_wall = time.perf_counter()
+        for i in range(args.steps):
+            box["q"] = qs[args.warmup + i]
+            flush.zero_()
+            ev[i][0].record(stream)
+            for j, f in enumerate(phases):
+                f()
+                ev[i][j + 1].record(stream)
+            union_pages[i] = dec.union_count.sum()
+        torch.cuda.synchronize(device)
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(device)
+        wall_s = time.perf_counter() - t_wall
+    ph = [statistics.mean(ev[i][j].elapsed_time(ev[i][j + 1]) for i in range(args.steps)) for j in range(len(phases))]
+    step_ms = statistics.mean(ev[i][0].elapsed_time(ev[i][-1]) for i in range(args.steps))
+    pages_loc = union_pages.float().mean().item()
+
+    # ---- end to end through the public API: pinned host q -> ShardedQuestDecoder.step -> pinned host o
+    q_host = qs.cpu().pin_memory()
+    o_host = torch.empty((b, hq, 1, d), dtype=torch.bfloat16).pin_memory()
+    q_dev = torch.empty_like(qs[0])
+    for i in range(args.warmup):
+        q_dev.copy_(q_host[i], non_blocking=True)
+        o_host.copy_(dec.step(q_dev, exchange=exchange), non_blocking=True)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+    e2e_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush.zero_()
+        e2e_ev[i][0].record(stream)
+        q_dev.copy_(q_host[args.warmup + i], non_blocking=True)
+        o_host.copy_(dec.step(q_dev, exchange=exchange), non_blocking=True)
+        e2e_ev[i][1].record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = statistics.mean(e.elapsed_time(f) for e, f in e2e_ev)
+
+    n_loc = hi - lo
+    meta_bytes = b * hkv * n_loc * 2 * d * 2
+    score_bytes = 0  # the fused kernel keeps page scores on chip; candidates are (chunks, B, H_q, topk)
+    sel_bytes = meta_bytes + dec.cand.numel() * 4
+    # per selected (page, kv head): fp8 K and V rows and their two fp32 scales; plus q in and f32 (o, lse) out
+    kv_bytes = pages_loc * (p * d * 2 + 8) + b * hq * d * 2 + b * hq * (d + 1) * 4
+    achieved_sel = sel_bytes / (ph[0] * 1e-3) / 1e9
+    achieved_att = kv_bytes / (ph[2] * 1e-3) / 1e9
+    vals = torch.tensor([step_ms, e2e_ms, wall_s, *ph, achieved_sel, achieved_att, build_s], dtype=torch.float64,
+                        device=device)
+    mins = vals.clone()
+    if world > 1:
+        torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX)
+        torch.distributed.all_reduce(mins, op=torch.distributed.ReduceOp.MIN)
+    step_ms, e2e_ms, wall_s, *rest = vals.tolist()
+    ph_max, build_max = rest[:4], rest[6]
+    sel_min_gbs, att_min_gbs = mins[7].item(), mins[8].item()
+    hbm_peak, _, peak_kind = measured_peaks()
+    dominant = "select" if ph[0] >= ph[2] else "attend"
+    ach = sel_min_gbs if dominant == "select" else att_min_gbs
+    kname = "quest_decode_candidates (fused page scoring + per-chunk top-k)" if dominant == "select" else \
+        "sparse_attention (fp8 paged, f32 partial o + lse)"
+    traffic = profile_traffic("quest_select_c5.md" if dominant == "select" else "sparse_attention_c5.md")
+    n_mine = 4  # candidates, merge, attention, combine
+    return {
+        "metric": METRIC,
+        "value": round(b / (step_ms * 1e-3), 1),
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(step_ms, 4),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "fp8e4m3 KV, bf16 q, f32 accumulate",
+        "data": "synthetic (seeded N(0,1) values quantised to e4m3 per (page, kv head), 0.5% needle pages at "
+                "global positions shared by every rank, random page table per shard)",
+        "config": {"workload": "sharded_decode_c5" if b == C5["B"] else f"sharded_decode_c5_b{b}", "batch": b,
+                   "seq_len": t, "page_size": p, "n_heads": hq, "n_kv_heads": hkv, "head_dim": d,
+                   "budget_pages": c["topk"], "pages_per_gpu_per_seq": n_loc,
+                   "parallelism": f"sequence-sharded x{world} (KV pages split, NCCL all-gathers)",
+                   "l2": "flushed (256 MiB write) before every step, outside the timed events; per-step inputs "
+                         "(page metadata + selected pages) exceed L2 anyway"},
+        "step_breakdown_ms": {"select": round(ph_max[0], 4), "exchange_candidates+merge": round(ph_max[1], 4),
+                              "attend": round(ph_max[2], 4), "exchange_partials+combine": round(ph_max[3], 4)},
+        "bytes_per_step_per_gpu": {"meta": int(meta_bytes), "scores": int(score_bytes), "kv_selected": int(kv_bytes)},
+        "selected_pages_per_kv_head_per_gpu": round(pages_loc / (b * hkv), 2),
+        "select_chunks_per_gpu": dec.chunks, "pages_per_select_cta": dec.chunk_pages,
+        "wall_ms_per_step": round(wall_s * 1e3 / args.steps, 4),
+        "build_s": round(build_max, 1),
+        "roofline": {"bound": "hbm", "kernel": kname, "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(ach / hbm_peak, 4), "peak_kind": peak_kind, "traffic": traffic,
+                     "algorithmic_bytes_per_launch": int(sel_bytes if dominant == "select" else kv_bytes),
+                     "note": "slowest rank's achieved bandwidth"},
+        "e2e": {"value": round(b / (e2e_ms * 1e-3), 1), "unit": "tok/s", "h2d_bytes_per_step": int(qs[0].numel() * 2),
+                "d2h_bytes_per_step": int(o_host.numel() * 2), "ms_per_step": round(e2e_ms, 4),
+                "api": "linattn_b200.sharded.ShardedQuestDecoder.step"},
+        "gpu_launches": n_mine * args.steps,
+        "clocks": clocks.summary(),
+    }
 
 
 def run_reference(args):
@@ -446,8 +778,12 @@ def main(argv=None) -> int:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--batch", type=int, default=C2["B"],
-                    help="sequences per GPU (16 = config 2; smaller only for profiling captures)")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="sequences per GPU (default: the config's; smaller only for profiling captures)")
+    ap.add_argument("--workload", default="c2", choices=["c2", "c5"],
+                    help="c2: paged Quest decode (the headline); c5: million-token sequence-sharded decode")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="skip the config-3 / config-4 legs reported beside the config-2 line")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -456,6 +792,11 @@ def main(argv=None) -> int:
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         if rank != 0:
+            return 0
+        if args.workload == "c5":
+            print(json.dumps({"impl": "reference", "unavailable": "the reference has no sequence-sharded decode and "
+                              "no fp8 paged CPU path at 1M tokens; its CPU arm is timed on the config-2 workload"}),
+                  flush=True)
             return 0
         print(json.dumps(run_reference(args)), flush=True)
         return 0
@@ -466,7 +807,12 @@ def main(argv=None) -> int:
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local_rank))
     try:
-        line = run_ours(args, rank, world, local_rank)
+        if args.workload == "c5":
+            line = run_c5(args, rank, world, local_rank)
+        else:
+            if args.batch is None:
+                args.batch = C2["B"]
+            line = run_ours(args, rank, world, local_rank)
         if rank == 0:
             print(json.dumps(line), flush=True)
     finally:

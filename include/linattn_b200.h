@@ -193,6 +193,28 @@ int linattn_quest_decode_select(const void* q, int32_t q_dtype, int64_t B, int64
                                 void* stream);
 
 /*
+ * The candidates form of linattn_quest_decode_select, for long sequences and the
+ * sequence-sharded decode: the page axis is cut into chunks of chunk_pages pages, one
+ * CTA per (sequence, kv head, chunk), and each writes, for every query head, the top
+ * `topk` pages of its chunk as candidates: cand_scores / cand_ids at
+ * [c * cand_stride + (b * H_q + h) * topk + r], sorted by (score desc, page asc), page
+ * ids offset by page_base[b] (NULL = 0), padded with (-inf, -1).  Forced pages (the
+ * last page when force_last, the first sink_pages) score +inf.  scores (B, H_q,
+ * max_pages), when not NULL, receives every page score.  linattn_shard_merge over the
+ * chunks (R = n_chunks, rank_stride = cand_stride) then gives the same top-k and GQA
+ * union as linattn_quest_decode_select (page_select_torch,
+ * src/linattn/kernels/triton/quest_pages.py:57-78): a page of the global top-k is in
+ * its chunk's top-k.  No single reference counterpart (the reference scores and
+ * selects in one pass over the whole sequence).
+ */
+int linattn_quest_decode_candidates(const void* q, int32_t q_dtype, int64_t B, int64_t Hq, int64_t D,
+                                    const int64_t* q_strides, const void* meta, int32_t meta_dtype,
+                                    int64_t n_kv_heads, int64_t max_pages, const int32_t* n_pages_b, int64_t topk,
+                                    int32_t sink_pages, int32_t force_last, int64_t chunk_pages,
+                                    const int32_t* page_base, float* cand_scores, int32_t* cand_ids,
+                                    int64_t cand_stride, float* scores, int32_t* status, void* stream);
+
+/*
  * Exact softmax attention of each query over the KV rows of its list's pages.
  * q and out are (B, H_q, T_q, D) with element strides; out has q's dtype.  Rows at
  * positions >= seq_len_b are skipped; with `causal`, rows after offset + t too.
@@ -235,6 +257,16 @@ int64_t linattn_sparse_attention_workspace(int64_t B, int64_t Hq, int64_t Tq, in
  */
 int linattn_lse_combine(const float* o_parts, const float* lse_parts, int64_t S, int64_t rows, int64_t D,
                         void* out, int32_t out_dtype, float* lse_out, void* stream);
+
+/*
+ * linattn_lse_combine over parts that are not packed densely: part s of o starts at
+ * o_parts + s * o_part_stride floats and its lse at lse_parts + s * lse_part_stride
+ * (0 = rows * D / rows, the dense layout).  Lets the sequence-sharded decode gather one
+ * [o | lse] block per rank with a single all-gather and merge it in place.
+ */
+int linattn_lse_combine_strided(const float* o_parts, int64_t o_part_stride, const float* lse_parts,
+                                int64_t lse_part_stride, int64_t S, int64_t rows, int64_t D, void* out,
+                                int32_t out_dtype, float* lse_out, void* stream);
 
 /*
  * linattn_sparse_attention without a workspace argument, for callers that cannot
@@ -381,12 +413,18 @@ int linattn_block_sparse_prefill(const void* q, int32_t dtype, int64_t B, int64_
  * (page - page_lo[b]), -1 padded, with union_count (B, H_kv).  R * K <= 4096.
  * No counterpart in the reference (which never shards the KV sequence); the selection
  * equals page_select_torch's (src/linattn/kernels/triton/quest_pages.py:57-78) over
- * the whole cache.
+ * the whole cache.  rank_stride: elements from one shard's (B, H_q, K) block to the
+ * next in both scores and ids (0 = B * H_q * K, dense), so a gathered buffer holding
+ * each rank's [scores | ids] pair is read in place.  union_tokens (B, H_kv), when not
+ * NULL, receives the tokens of the union pages: sum over pages g of
+ * clamp(seq_lens[b] - g * page_size, 0, page_size), g the global page.
  */
 int linattn_shard_merge(const float* scores, const int32_t* ids, int64_t R, int64_t B, int64_t Hq, int64_t K,
-                        int64_t topk, int64_t n_kv_heads, const int32_t* page_lo, const int32_t* page_hi,
+                        int64_t rank_stride, int64_t topk, int64_t n_kv_heads, const int32_t* page_lo, const int32_t* page_hi,
                         int64_t max_local, int32_t* sel, int32_t* union_ids, int32_t* union_count,
-                        int64_t max_union, void* stream);
+                        int64_t max_union, const int32_t* seq_lens, int64_t page_size, int32_t* union_tokens,
+                        void* stream);
+
 
 #ifdef __cplusplus
 }

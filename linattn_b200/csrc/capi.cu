@@ -322,15 +322,23 @@ int linattn_sparse_attention_out(const void* q, int32_t q_dtype, int64_t B, int6
                      "sparse_attention combine");
 }
 
-int linattn_lse_combine(const float* o_parts, const float* lse_parts, int64_t S, int64_t rows, int64_t D, void* out,
-                        int32_t out_dtype, float* lse_out, void* stream) {
+int linattn_lse_combine_strided(const float* o_parts, int64_t o_part_stride, const float* lse_parts,
+                                int64_t lse_part_stride, int64_t S, int64_t rows, int64_t D, void* out,
+                                int32_t out_dtype, float* lse_out, void* stream) {
   if (!o_parts || !lse_parts || !out) return fail(LINATTN_EINVAL, "lse_combine: NULL pointer");
   if (!is_float16_32(out_dtype)) return fail(LINATTN_EUNSUPPORTED, "lse_combine: out dtype %d", out_dtype);
   if (S < 1 || rows < 0 || D < 1 || D > 256) return fail(LINATTN_EINVAL, "lse_combine: bad sizes (D <= 256)");
+  if ((o_part_stride != 0 && o_part_stride < rows * D) || (lse_part_stride != 0 && lse_part_stride < rows))
+    return fail(LINATTN_EINVAL, "lse_combine: part strides overlap");
   const int64_t os[4] = {0, 0, D, 1};
   return cuda_status(launch_lse_combine(o_parts, lse_parts, S, rows, D, out, out_dtype, 1, rows > 0 ? rows : 1, os,
-                                        lse_out, static_cast<cudaStream_t>(stream)),
+                                        lse_out, static_cast<cudaStream_t>(stream), o_part_stride, lse_part_stride),
                      "lse_combine");
+}
+
+int linattn_lse_combine(const float* o_parts, const float* lse_parts, int64_t S, int64_t rows, int64_t D, void* out,
+                        int32_t out_dtype, float* lse_out, void* stream) {
+  return linattn_lse_combine_strided(o_parts, 0, lse_parts, 0, S, rows, D, out, out_dtype, lse_out, stream);
 }
 
 }  // extern "C"

@@ -41,7 +41,7 @@ size_t page_topk_smem_bytes(int64_t n, int64_t topk);
 cudaError_t launch_page_topk(const TopkParams& p, cudaStream_t stream);
 cudaError_t launch_lse_combine(const float* o_parts, const float* lse_parts, int64_t S, int64_t rows, int64_t D,
                                void* out, int out_dtype, int64_t H, int64_t Tq, const int64_t* os, float* lse_out,
-                               cudaStream_t stream);
+                               cudaStream_t stream, int64_t o_part_stride = 0, int64_t lse_part_stride = 0);
 cudaError_t launch_sparse_attention_f32(const AttnParams& p, int D, int G, unsigned grid, cudaStream_t stream);
 cudaError_t launch_sparse_attention_f16(const AttnParams& p, int D, int G, unsigned grid, cudaStream_t stream);
 cudaError_t launch_sparse_attention_bf16(const AttnParams& p, int D, int G, unsigned grid, cudaStream_t stream);

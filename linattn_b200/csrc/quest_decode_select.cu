@@ -15,6 +15,18 @@
 // Decode semantics: the query sits at position seq_len_b - 1, so every page below
 // n_pages_b is visible, the own page is n_pages_b - 1, and it and the first
 // `sink_pages` pages are forced to +inf (quest_pages.py:67-75 at T_q == 1).
+//
+// Candidates form (linattn_quest_decode_candidates): the page axis is cut into chunks
+// of `chunk` pages, one CTA per (sequence, kv head, chunk); each CTA writes every
+// head's top-k of its chunk as (score, page + page_base[b]) candidates sorted by
+// (score desc, page asc), and the global top-k + GQA union is taken by the shard
+// merge kernel over all chunks (and, in the sequence-sharded decode, all ranks).  A
+// page of the global top-k is in its chunk's top-k, so the result is the same
+// selection; long sequences get many CTAs and short per-CTA selections.
+//
+// Histogram passes aggregate equal bins across the warp (match.any) before the shared
+// memory atomic, so keys that share a digit (most keys share the top byte) cost one
+// atomic per warp instead of 32 serialised ones.
 #include <cstdio>
 
 #include "launchers.cuh"
@@ -23,8 +35,7 @@ namespace linattn {
 
 namespace {
 
-constexpr int NSTG = 8;   // ring stages
-constexpr int CH = 32;    // pages per chunk
+constexpr int CH = 32;    // pages per ring stage
 
 template <int G, int LPR>
 __device__ __forceinline__ void group_reduce(float (&v)[G], int lane) {
@@ -68,11 +79,16 @@ struct DecodeSelectParams {
   int64_t max_union;
   int32_t* union_tokens;
   int32_t* status;
+  int64_t chunk;              // pages per CTA (blockIdx.y = chunk index)
+  float* cand_scores;         // candidates form: (n_chunks, B, Hq, topk), chunk stride cand_stride
+  int32_t* cand_ids;
+  int64_t cand_stride;
+  const int32_t* page_base;   // per sequence, added to candidate page ids (NULL = 0)
 };
 
 }  // namespace
 
-template <typename TM, int D, int G>
+template <typename TM, int D, int G, int NSTG>
 __global__ void __launch_bounds__(256, 1) quest_decode_select_kernel(const DecodeSelectParams p) {
   constexpr int LPR = D / 8;               // lanes per page
   constexpr int PPW = 32 / LPR;            // pages per warp step
@@ -82,18 +98,20 @@ __global__ void __launch_bounds__(256, 1) quest_decode_select_kernel(const Decod
   constexpr int REP = G >= LPR ? 1 : LPR / G;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* ring = smem;                                                   // NSTG chunks
-  float* sc = reinterpret_cast<float*>(smem + NSTG * CHUNK_BYTES);        // [G][max_pages]
-  uint32_t* hist = reinterpret_cast<uint32_t*>(sc + G * p.max_pages);     // [8 warps][256]
-  uint32_t* bitmap = hist + 8 * 256;                                      // [ceil(max_pages/32)]
-  uint32_t* sel = bitmap + (p.max_pages + 31) / 32;                       // [8 warps][2][topk]
+  float* sc = reinterpret_cast<float*>(smem + NSTG * CHUNK_BYTES);        // [G][chunk]
+  uint32_t* hist = reinterpret_cast<uint32_t*>(sc + G * p.chunk);         // [8 warps][256]
+  uint32_t* bitmap = hist + 8 * 256;                                      // [ceil(chunk/32)]
+  uint32_t* sel = bitmap + (p.chunk + 31) / 32;                           // [8 warps][2][topk]
   __shared__ __align__(8) uint64_t bar[NSTG];
   __shared__ uint32_t scan_tmp[9];
   __shared__ uint32_t sh_tokens;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t kvh = blockIdx.x % p.Hkv, b = blockIdx.x / p.Hkv;
-  const int64_t nb = lmin(p.n_pages_b[b], p.max_pages);
-  const int64_t W = (p.max_pages + 31) / 32;
+  const int64_t nb_all = lmin(p.n_pages_b[b], p.max_pages);  // the sequence's pages
+  const int64_t pg0 = static_cast<int64_t>(blockIdx.y) * p.chunk;  // this CTA's first page
+  const int64_t nb = lmax(0, lmin(nb_all - pg0, p.chunk));      // and its page count
+  const int64_t W = (p.chunk + 31) / 32;
   for (int64_t w = tid; w < W; w += 256) bitmap[w] = 0u;
   if (tid == 0) {
     for (int s = 0; s < NSTG; ++s) mbar_init(&bar[s], 1);
@@ -102,7 +120,7 @@ __global__ void __launch_bounds__(256, 1) quest_decode_select_kernel(const Decod
   }
   __syncthreads();
 
-  const TM* base = static_cast<const TM*>(p.meta) + (b * p.Hkv + kvh) * p.max_pages * PAGE_ELEMS;
+  const TM* base = static_cast<const TM*>(p.meta) + ((b * p.Hkv + kvh) * p.max_pages + pg0) * PAGE_ELEMS;
   const int64_t n_chunks = (nb + CH - 1) / CH;
   auto issue = [&](int64_t c) {
     const int s = static_cast<int>(c % NSTG);
@@ -153,11 +171,12 @@ __global__ void __launch_bounds__(256, 1) quest_decode_select_kernel(const Decod
       group_reduce<G, LPR>(acc, lane);
       if (pg < pages && (cl % REP) == 0) {
         const int64_t page = c * CH + pg;
-        const bool forced = (p.force_last && page == nb - 1) || page < p.sink_pages;
+        const int64_t gpage = pg0 + page;
+        const bool forced = (p.force_last && gpage == nb_all - 1) || gpage < p.sink_pages;
 #pragma unroll
         for (int i = 0; i < NV; ++i) {
           const int g = G >= LPR ? cl * NV + i : cl / REP;
-          sc[g * p.max_pages + page] = forced ? INFINITY : acc[i];
+          sc[g * p.chunk + page] = forced ? INFINITY : acc[i];
         }
       }
     }
@@ -178,22 +197,30 @@ __global__ void __launch_bounds__(256, 1) quest_decode_select_kernel(const Decod
   if (warp < G) {
     const int g = warp;
     const int64_t h = kvh * G + g;
-    const float* srow = sc + g * p.max_pages;
+    const float* srow = sc + g * p.chunk;
     uint32_t* hw = hist + warp * 256;
     uint32_t* sel_idx = sel + warp * 2 * p.topk;
     uint32_t* sel_key = sel_idx + p.topk;
     if (p.scores) {
-      float* dst = p.scores + (b * p.Hq + h) * p.max_pages;
-      for (int64_t i = lane; i < p.max_pages; i += 32) dst[i] = i < nb ? srow[i] : -INFINITY;
+      float* dst = p.scores + (b * p.Hq + h) * p.max_pages + pg0;
+      const int64_t span = lmin(p.chunk, p.max_pages - pg0);
+      for (int64_t i = lane; i < span; i += 32) dst[i] = i < nb ? srow[i] : -INFINITY;
     }
     uint32_t prefix = 0u, mask = 0u, remaining = static_cast<uint32_t>(kb);
     for (int shift = 24; shift >= 0 && kb > 0; shift -= 8) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) hw[lane * 8 + j] = 0u;
       __syncwarp();
-      for (int64_t i = lane; i < nb; i += 32) {
-        const uint32_t key = float_key(srow[i]);
-        if ((key & mask) == prefix) atomicAdd(&hw[(key >> shift) & 255u], 1u);
+      for (int64_t i0 = 0; i0 < nb; i0 += 32) {  // warp-uniform trip count
+        const int64_t i = i0 + lane;
+        const uint32_t key = i < nb ? float_key(srow[i]) : 0u;
+        const bool act = i < nb && (key & mask) == prefix;
+        const uint32_t bin = (key >> shift) & 255u;
+        const unsigned am = __ballot_sync(0xffffffffu, act);
+        if (act) {
+          const unsigned peers = __match_any_sync(am, bin);
+          if ((peers & ((1u << lane) - 1u)) == 0u) atomicAdd(&hw[bin], static_cast<uint32_t>(__popc(peers)));
+        }
       }
       __syncwarp();
       // lane owns the 8 bins 255 - (lane*8 + j): counts in descending bin order
@@ -249,20 +276,40 @@ __global__ void __launch_bounds__(256, 1) quest_decode_select_kernel(const Decod
       eq_taken += __popc(eq_mask);
     }
     __syncwarp();
-    // rank sort (score desc, index asc), write ids, mark the union
-    int32_t* out = p.ids + (b * p.Hq + h) * p.topk;
-    for (int64_t i = lane; i < kb; i += 32) {
-      const uint32_t ki = sel_key[i], ii = sel_idx[i];
-      int rank = 0;
-      for (int64_t j = 0; j < kb; ++j) {
-        const uint32_t kj = sel_key[j], ij = sel_idx[j];
-        rank += (kj > ki || (kj == ki && ij < ii)) ? 1 : 0;
+    // rank sort (score desc, index asc), write ids (or candidates), mark the union
+    if (p.cand_scores) {
+      const int64_t off = static_cast<int64_t>(blockIdx.y) * p.cand_stride + (b * p.Hq + h) * p.topk;
+      const int64_t id0 = pg0 + (p.page_base ? static_cast<int64_t>(p.page_base[b]) : 0);
+      for (int64_t i = lane; i < kb; i += 32) {
+        const uint32_t ki = sel_key[i], ii = sel_idx[i];
+        int rank = 0;
+        for (int64_t j = 0; j < kb; ++j) {
+          const uint32_t kj = sel_key[j], ij = sel_idx[j];
+          rank += (kj > ki || (kj == ki && ij < ii)) ? 1 : 0;
+        }
+        p.cand_scores[off + rank] = srow[ii];
+        p.cand_ids[off + rank] = static_cast<int32_t>(id0 + ii);
       }
-      out[rank] = static_cast<int32_t>(ii);
-      if (ki > neg_inf_key) atomicOr(&bitmap[ii >> 5], 1u << (ii & 31u));
+      for (int64_t r = kb + lane; r < p.topk; r += 32) {
+        p.cand_scores[off + r] = -INFINITY;
+        p.cand_ids[off + r] = -1;
+      }
+    } else {
+      int32_t* out = p.ids + (b * p.Hq + h) * p.topk;
+      for (int64_t i = lane; i < kb; i += 32) {
+        const uint32_t ki = sel_key[i], ii = sel_idx[i];
+        int rank = 0;
+        for (int64_t j = 0; j < kb; ++j) {
+          const uint32_t kj = sel_key[j], ij = sel_idx[j];
+          rank += (kj > ki || (kj == ki && ij < ii)) ? 1 : 0;
+        }
+        out[rank] = static_cast<int32_t>(ii);
+        if (ki > neg_inf_key) atomicOr(&bitmap[ii >> 5], 1u << (ii & 31u));
+      }
+      for (int64_t r = kb + lane; r < p.topk; r += 32) out[r] = -1;
     }
-    for (int64_t r = kb + lane; r < p.topk; r += 32) out[r] = -1;
   }
+  if (p.cand_scores) return;  // the union is taken after the merge of all chunks
   __syncthreads();
   // ---- compact the union into an ascending page list
   const int64_t wpt = (W + 255) / 256;
@@ -295,42 +342,54 @@ __global__ void __launch_bounds__(256, 1) quest_decode_select_kernel(const Decod
   }
 }
 
-size_t quest_decode_select_smem(int64_t max_pages, int64_t G, int64_t topk, int64_t D, int elem_bytes) {
-  return static_cast<size_t>(NSTG) * CH * 2 * D * elem_bytes + static_cast<size_t>(G) * max_pages * 4 +
-         8 * 256 * 4 + static_cast<size_t>((max_pages + 31) / 32) * 4 + static_cast<size_t>(8) * 2 * topk * 4;
+// ring stages: 8 for the single-CTA form (one CTA per SM streams the whole sequence),
+// 4 for the candidates form (several CTAs per SM share the memory pipe)
+size_t quest_decode_select_smem(int64_t chunk, int64_t G, int64_t topk, int64_t D, int elem_bytes, int nstg) {
+  return static_cast<size_t>(nstg) * CH * 2 * D * elem_bytes + static_cast<size_t>(G) * chunk * 4 +
+         8 * 256 * 4 + static_cast<size_t>((chunk + 31) / 32) * 4 + static_cast<size_t>(8) * 2 * topk * 4;
 }
 
-template <typename TM, int D, int G>
-static cudaError_t launch_ds(const DecodeSelectParams& p, size_t smem, cudaStream_t stream) {
+template <typename TM, int D, int G, int NSTG>
+static cudaError_t launch_ds(const DecodeSelectParams& p, unsigned n_chunks, size_t smem, cudaStream_t stream) {
   static int configured[64] = {};
   const int dev = device_index();
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (configured[dev] < static_cast<int>(smem)) {
-    cudaError_t e = cudaFuncSetAttribute(quest_decode_select_kernel<TM, D, G>,
+    cudaError_t e = cudaFuncSetAttribute(quest_decode_select_kernel<TM, D, G, NSTG>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     configured[dev] = static_cast<int>(smem);
   }
-  quest_decode_select_kernel<TM, D, G><<<static_cast<unsigned>(p.B * p.Hkv), 256, smem, stream>>>(p);
+  quest_decode_select_kernel<TM, D, G, NSTG>
+      <<<dim3(static_cast<unsigned>(p.B * p.Hkv), n_chunks), 256, smem, stream>>>(p);
   return cudaGetLastError();
 }
 
+template <typename TM, int D, int G>
+static cudaError_t launch_ds_s(const DecodeSelectParams& p, int nstg, unsigned n_chunks, size_t smem,
+                               cudaStream_t stream) {
+  return nstg == 8 ? launch_ds<TM, D, G, 8>(p, n_chunks, smem, stream)
+                   : launch_ds<TM, D, G, 4>(p, n_chunks, smem, stream);
+}
+
 template <typename TM, int D>
-static cudaError_t launch_ds_g(const DecodeSelectParams& p, int G, size_t smem, cudaStream_t stream) {
+static cudaError_t launch_ds_g(const DecodeSelectParams& p, int G, int nstg, unsigned n_chunks, size_t smem,
+                               cudaStream_t stream) {
   switch (G) {
-    case 1: return launch_ds<TM, D, 1>(p, smem, stream);
-    case 2: return launch_ds<TM, D, 2>(p, smem, stream);
-    case 4: return launch_ds<TM, D, 4>(p, smem, stream);
-    case 8: return launch_ds<TM, D, 8>(p, smem, stream);
+    case 1: return launch_ds_s<TM, D, 1>(p, nstg, n_chunks, smem, stream);
+    case 2: return launch_ds_s<TM, D, 2>(p, nstg, n_chunks, smem, stream);
+    case 4: return launch_ds_s<TM, D, 4>(p, nstg, n_chunks, smem, stream);
+    case 8: return launch_ds_s<TM, D, 8>(p, nstg, n_chunks, smem, stream);
     default: return cudaErrorInvalidValue;
   }
 }
 
 template <typename TM>
-static cudaError_t launch_ds_d(const DecodeSelectParams& p, int D, int G, size_t smem, cudaStream_t stream) {
+static cudaError_t launch_ds_d(const DecodeSelectParams& p, int D, int G, int nstg, unsigned n_chunks, size_t smem,
+                               cudaStream_t stream) {
   switch (D) {
-    case 64: return launch_ds_g<TM, 64>(p, G, smem, stream);
-    case 128: return launch_ds_g<TM, 128>(p, G, smem, stream);
+    case 64: return launch_ds_g<TM, 64>(p, G, nstg, n_chunks, smem, stream);
+    case 128: return launch_ds_g<TM, 128>(p, G, nstg, n_chunks, smem, stream);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -338,6 +397,56 @@ static cudaError_t launch_ds_d(const DecodeSelectParams& p, int D, int G, size_t
 }  // namespace linattn
 
 using namespace linattn;
+
+namespace {
+
+int check_select_args(const void* q, int32_t q_dtype, int64_t Hq, int64_t D, const int64_t* q_strides,
+                      const void* meta, int32_t meta_dtype, int64_t n_kv_heads, int64_t max_pages,
+                      const int32_t* n_pages_b, int64_t topk, const char* who) {
+  char msg[160];
+  auto fail = [&](int code, const char* what) {
+    snprintf(msg, sizeof(msg), "%s: %s", who, what);
+    return set_error(code, msg);
+  };
+  if (!q || !q_strides || !meta || !n_pages_b) return fail(LINATTN_EINVAL, "NULL pointer");
+  if (q_dtype != LINATTN_F32 && q_dtype != LINATTN_F16 && q_dtype != LINATTN_BF16)
+    return fail(LINATTN_EUNSUPPORTED, "q dtype");
+  if (meta_dtype != LINATTN_F16 && meta_dtype != LINATTN_BF16)
+    return fail(LINATTN_EUNSUPPORTED, "metadata must be f16 or bf16");
+  if (D != 64 && D != 128) return fail(LINATTN_EUNSUPPORTED, "head_dim must be 64 or 128");
+  if (n_kv_heads <= 0 || Hq % n_kv_heads) return fail(LINATTN_EINVAL, "H_kv must divide H_q");
+  const int64_t G = Hq / n_kv_heads;
+  if (G != 1 && G != 2 && G != 4 && G != 8) return fail(LINATTN_EUNSUPPORTED, "group size must be 1, 2, 4 or 8");
+  if (topk < 1 || topk > 1024 || max_pages < 1) return fail(LINATTN_EINVAL, "bad topk / max_pages");
+  if (reinterpret_cast<uintptr_t>(meta) % 16) return fail(LINATTN_EINVAL, "meta alignment");
+  return LINATTN_OK;
+}
+
+int launch_select_on(const DecodeSelectParams& p, int32_t meta_dtype, int64_t D, unsigned n_chunks, int nstg,
+                     const char* who, void* stream) {
+  const int64_t G = p.Hq / p.Hkv;
+  const size_t smem = quest_decode_select_smem(p.chunk, G, p.topk, D, 2, nstg);
+  if (smem > 220 * 1024) {
+    char msg[160];
+    snprintf(msg, sizeof(msg), "%s: too many pages per CTA for the fused kernel", who);
+    return set_error(LINATTN_EUNSUPPORTED, msg);
+  }
+  if (p.B * p.Hkv == 0 || n_chunks == 0) return LINATTN_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const cudaError_t e = meta_dtype == LINATTN_BF16
+                            ? launch_ds_d<__nv_bfloat16>(p, static_cast<int>(D), static_cast<int>(G), nstg, n_chunks,
+                                                         smem, st)
+                            : launch_ds_d<__half>(p, static_cast<int>(D), static_cast<int>(G), nstg, n_chunks, smem,
+                                                  st);
+  if (e != cudaSuccess) {
+    char msg[256];
+    snprintf(msg, sizeof(msg), "%s: %s", who, cudaGetErrorString(e));
+    return set_error(LINATTN_ECUDA, msg);
+  }
+  return LINATTN_OK;
+}
+
+}  // namespace
 
 extern "C" int linattn_quest_decode_select(const void* q, int32_t q_dtype, int64_t B, int64_t Hq, int64_t D,
                                            const int64_t* q_strides, const void* meta, int32_t meta_dtype,
@@ -347,25 +456,13 @@ extern "C" int linattn_quest_decode_select(const void* q, int32_t q_dtype, int64
                                            int32_t* union_ids,
                                            int32_t* union_count, int64_t max_union, int32_t* union_tokens,
                                            int32_t* status, void* stream) {
-  if (!q || !q_strides || !meta || !n_pages_b || !seq_lens || !ids || !union_ids || !union_count)
+  int rc = check_select_args(q, q_dtype, Hq, D, q_strides, meta, meta_dtype, n_kv_heads, max_pages, n_pages_b, topk,
+                             "quest_decode_select");
+  if (rc) return rc;
+  if (!seq_lens || !ids || !union_ids || !union_count)
     return set_error(LINATTN_EINVAL, "quest_decode_select: NULL pointer");
-  if (q_dtype != LINATTN_F32 && q_dtype != LINATTN_F16 && q_dtype != LINATTN_BF16)
-    return set_error(LINATTN_EUNSUPPORTED, "quest_decode_select: q dtype");
-  if (meta_dtype != LINATTN_F16 && meta_dtype != LINATTN_BF16)
-    return set_error(LINATTN_EUNSUPPORTED, "quest_decode_select: metadata must be f16 or bf16");
-  if (D != 64 && D != 128) return set_error(LINATTN_EUNSUPPORTED, "quest_decode_select: head_dim must be 64 or 128");
-  if (n_kv_heads <= 0 || Hq % n_kv_heads) return set_error(LINATTN_EINVAL, "quest_decode_select: H_kv must divide H_q");
-  const int64_t G = Hq / n_kv_heads;
-  if (G != 1 && G != 2 && G != 4 && G != 8)
-    return set_error(LINATTN_EUNSUPPORTED, "quest_decode_select: group size must be 1, 2, 4 or 8");
-  if (topk < 1 || topk > 1024 || max_pages < 1 || page_size < 1 || max_union < 1)
-    return set_error(LINATTN_EINVAL, "quest_decode_select: bad topk / max_pages / page_size / max_union");
-  if (reinterpret_cast<uintptr_t>(meta) % 16) return set_error(LINATTN_EINVAL, "quest_decode_select: meta alignment");
-  const size_t smem = quest_decode_select_smem(max_pages, G, topk, D, 2);
-  if (smem > 220 * 1024)
-    return set_error(LINATTN_EUNSUPPORTED, "quest_decode_select: too many pages for the fused kernel");
-  if (B * n_kv_heads == 0) return LINATTN_OK;
-  DecodeSelectParams p;
+  if (page_size < 1 || max_union < 1) return set_error(LINATTN_EINVAL, "quest_decode_select: bad page_size / max_union");
+  DecodeSelectParams p{};
   p.q = q; p.q_dtype = q_dtype; p.B = B; p.Hq = Hq; p.Hkv = n_kv_heads;
   for (int i = 0; i < 4; ++i) p.qs[i] = q_strides[i];
   p.meta = meta; p.max_pages = max_pages; p.n_pages_b = n_pages_b; p.seq_lens = seq_lens; p.P = page_size;
@@ -373,13 +470,32 @@ extern "C" int linattn_quest_decode_select(const void* q, int32_t q_dtype, int64
   p.ids = ids; p.scores = scores;
   p.union_ids = union_ids; p.union_count = union_count; p.max_union = max_union; p.union_tokens = union_tokens;
   p.status = status;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const cudaError_t e = meta_dtype == LINATTN_BF16 ? launch_ds_d<__nv_bfloat16>(p, static_cast<int>(D), static_cast<int>(G), smem, st)
-                                                   : launch_ds_d<__half>(p, static_cast<int>(D), static_cast<int>(G), smem, st);
-  if (e != cudaSuccess) {
-    char msg[256];
-    snprintf(msg, sizeof(msg), "quest_decode_select: %s", cudaGetErrorString(e));
-    return set_error(LINATTN_ECUDA, msg);
-  }
-  return LINATTN_OK;
+  p.chunk = max_pages;
+  return launch_select_on(p, meta_dtype, D, 1u, 8, "quest_decode_select", stream);
+}
+
+extern "C" int linattn_quest_decode_candidates(const void* q, int32_t q_dtype, int64_t B, int64_t Hq, int64_t D,
+                                               const int64_t* q_strides, const void* meta, int32_t meta_dtype,
+                                               int64_t n_kv_heads, int64_t max_pages, const int32_t* n_pages_b,
+                                               int64_t topk, int32_t sink_pages, int32_t force_last,
+                                               int64_t chunk_pages, const int32_t* page_base, float* cand_scores,
+                                               int32_t* cand_ids, int64_t cand_stride, float* scores,
+                                               int32_t* status, void* stream) {
+  int rc = check_select_args(q, q_dtype, Hq, D, q_strides, meta, meta_dtype, n_kv_heads, max_pages, n_pages_b, topk,
+                             "quest_decode_candidates");
+  if (rc) return rc;
+  if (!cand_scores || !cand_ids) return set_error(LINATTN_EINVAL, "quest_decode_candidates: NULL pointer");
+  if (chunk_pages < 1) return set_error(LINATTN_EINVAL, "quest_decode_candidates: chunk_pages must be >= 1");
+  const int64_t n_chunks = (max_pages + chunk_pages - 1) / chunk_pages;
+  if (cand_stride < B * Hq * topk) return set_error(LINATTN_EINVAL, "quest_decode_candidates: cand_stride");
+  if (n_chunks > 65535) return set_error(LINATTN_EUNSUPPORTED, "quest_decode_candidates: too many chunks");
+  DecodeSelectParams p{};
+  p.q = q; p.q_dtype = q_dtype; p.B = B; p.Hq = Hq; p.Hkv = n_kv_heads;
+  for (int i = 0; i < 4; ++i) p.qs[i] = q_strides[i];
+  p.meta = meta; p.max_pages = max_pages; p.n_pages_b = n_pages_b; p.P = 1;
+  p.topk = static_cast<int>(topk); p.sink_pages = sink_pages; p.force_last = force_last ? 1 : 0;
+  p.scores = scores; p.status = status;
+  p.chunk = lmin(chunk_pages, max_pages);
+  p.cand_scores = cand_scores; p.cand_ids = cand_ids; p.cand_stride = cand_stride; p.page_base = page_base;
+  return launch_select_on(p, meta_dtype, D, static_cast<unsigned>(n_chunks), 4, "quest_decode_candidates", stream);
 }

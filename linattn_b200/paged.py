@@ -29,7 +29,7 @@ from linattn_b200 import _lib as L
 from linattn_b200.block_sparse import plan_splits, sparse_attention
 from linattn_b200.quest_pages import DECODE_OFFSET, QuestSelection
 
-__all__ = ["PagedKVCache", "QuestDecoder"]
+__all__ = ["PagedKVCache", "QuestDecoder", "fused_select_smem", "plan_select_chunks"]
 
 
 class PagedKVCache:
@@ -187,6 +187,32 @@ class PagedKVCache:
             L.check_status(self.device)
 
 
+def fused_select_smem(chunk: int, g: int, topk: int, d: int, stages: int) -> int:
+    """Shared memory of the fused selection kernel for `chunk` pages per CTA."""
+    return stages * 32 * 2 * d * 2 + g * chunk * 4 + 8 * 256 * 4 + ((chunk + 31) // 32) * 4 + 8 * 2 * topk * 4
+
+
+def plan_select_chunks(n: int, g: int, topk: int, d: int, units: int, device, chunks: Optional[int] = None,
+                       ranks: int = 1):
+    """(pages per CTA, chunks) for the fused selection over `n` pages and `units`
+    (sequence, kv head) pairs: enough CTAs for two per SM, at least 128 pages per
+    chunk, the chunk's scores in shared memory, and at most 4096 candidates per head
+    across the chunks of all `ranks` (the merge kernel's bound)."""
+    if chunks is None:
+        sms = torch.cuda.get_device_properties(device).multi_processor_count
+        chunks = max(1, min(-(-2 * sms // max(1, units)), n // 128))
+    chunks = max(1, min(chunks, n))
+    chunk = -(-n // chunks)
+    stages = 8 if chunks == 1 else 4
+    while fused_select_smem(chunk, g, topk, d, stages) > 200 * 1024 and chunk > 32:
+        chunk = -(-chunk // 2)
+        stages = 4
+    chunks = -(-n // chunk)
+    if chunks * ranks * topk > 4096:
+        return chunk, 0
+    return chunk, chunks
+
+
 class QuestDecoder:
     """One Quest decode step over a :class:`PagedKVCache`, with every buffer allocated
     once: page scores -> top-k + GQA union -> sparse attention (split-KV + merge).
@@ -199,7 +225,8 @@ class QuestDecoder:
 
     def __init__(self, cache: PagedKVCache, n_heads: int, topk: int, *, sink_pages: int = 0,
                  scale: Optional[float] = None, gqa_union: bool = True, n_splits: Optional[int] = None,
-                 q_dtype: torch.dtype = torch.bfloat16, keep_scores: bool = False, force_last: bool = True):
+                 q_dtype: torch.dtype = torch.bfloat16, keep_scores: bool = False, force_last: bool = True,
+                 select_chunks: Optional[int] = None):
         self.cache = cache
         # False on a shard of a sequence-sharded cache that does not hold the query's page
         self.force_last = force_last
@@ -211,11 +238,24 @@ class QuestDecoder:
         dev = cache.device
         b, n = cache.batch, cache.max_pages
         group_size = n_heads // cache.n_kv_heads
-        # fused selection kernel (one CTA per sequence and kv head) when it applies
+        # fused selection: one CTA per (sequence, kv head), or per (sequence, kv head,
+        # chunk of pages) followed by the merge of the chunks' candidates when the
+        # sequence is long or the batch too small to fill the GPU
         self.fused = (gqa_union and group_size in (1, 2, 4, 8) and cache.head_dim in (64, 128)
-                      and cache.meta_dtype in (torch.float16, torch.bfloat16) and self._fused_smem(n, group_size) <= 220 * 1024)
+                      and cache.meta_dtype in (torch.float16, torch.bfloat16))
+        self.chunks = 1
+        if self.fused:
+            self.chunk_pages, self.chunks = plan_select_chunks(n, group_size, self.topk, cache.head_dim,
+                                                               b * cache.n_kv_heads, dev, select_chunks)
+            if self.chunks == 1 and fused_select_smem(n, group_size, self.topk, cache.head_dim, 8) > 220 * 1024:
+                self.chunks = 0  # no chunking fits: unfused path
+            self.fused = self.chunks >= 1
         self.keep_scores = keep_scores or not self.fused
         self.scores = torch.empty(b, n_heads, 1, n, dtype=torch.float32, device=dev) if self.keep_scores else None
+        if self.fused and self.chunks > 1:
+            # candidates (chunk, [scores | ids], B, H_q, topk) and the zero page base
+            self.cand = torch.empty(self.chunks, 2, b, n_heads, self.topk, dtype=torch.int32, device=dev)
+            self.page_zero = torch.zeros(b, dtype=torch.int32, device=dev)
         self.ids = torch.empty(b, n_heads, 1, self.topk, dtype=torch.int32, device=dev)
         self.max_union = min(self.group * self.topk, n)
         n_lists = n_heads // self.group
@@ -232,10 +272,6 @@ class QuestDecoder:
         self._lists = L.Lists(self.union_ids.data_ptr(), L.I32, n_lists, *self.union_ids.stride()[:3],
                               self.max_union, self.union_count.data_ptr(), *self.union_count.stride())
 
-    def _fused_smem(self, n: int, g: int) -> int:
-        d = self.cache.head_dim
-        return 8 * 32 * 2 * d * 2 + g * n * 4 + 8 * 256 * 4 + ((n + 31) // 32) * 4 + 8 * 2 * self.topk * 4
-
     def select(self, q: torch.Tensor) -> QuestSelection:
         c = self.cache
         dev = c.device
@@ -243,6 +279,19 @@ class QuestDecoder:
         stream = L.stream_of(q)
         b, hq, tq, d = q.shape
         lib = L.lib()
+        if self.fused and self.chunks > 1:
+            bhk = b * hq * self.topk
+            L.check(lib.linattn_quest_decode_candidates(
+                q.data_ptr(), L.dtype_code(q), b, hq, d, L.strides4(q), c.meta.data_ptr(), L.dtype_code(c.meta),
+                c.n_kv_heads, c.max_pages, c.n_pages_b.data_ptr(), self.topk, self.sink_pages, int(self.force_last),
+                self.chunk_pages, None, self.cand.data_ptr(), self.cand[:, 1].data_ptr(), 2 * bhk,
+                L.ptr(self.scores), status.data_ptr(), stream))
+            L.check(lib.linattn_shard_merge(
+                self.cand.data_ptr(), self.cand[:, 1].data_ptr(), self.chunks, b, hq, self.topk, 2 * bhk, self.topk,
+                c.n_kv_heads, self.page_zero.data_ptr(), c.n_pages_b.data_ptr(), c.max_pages, self.ids.data_ptr(),
+                self.union_ids.data_ptr(), self.union_count.data_ptr(), self.max_union, c.seq_lens.data_ptr(),
+                c.page_size, self.union_tokens.data_ptr(), stream))
+            return QuestSelection(self.ids, self.scores, self.union_ids, self.union_count, self.union_tokens)
         if self.fused:
             L.check(lib.linattn_quest_decode_select(
                 q.data_ptr(), L.dtype_code(q), b, hq, d, L.strides4(q), c.meta.data_ptr(), L.dtype_code(c.meta),

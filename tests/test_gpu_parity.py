@@ -365,11 +365,13 @@ def _make_paged(b, hkv, d, page, lens, dtype, gen, needles=0.0, q_dirs=None, per
     return cache, table
 
 
-def _check_decode(cache, table, q, topk, sink, tol):
+def _check_decode(cache, table, q, topk, sink, tol, chunks=None):
     from linattn_b200 import QuestDecoder
 
     hq = q.shape[1]
-    dec = QuestDecoder(cache, hq, topk, sink_pages=sink, q_dtype=q.dtype, keep_scores=True)
+    dec = QuestDecoder(cache, hq, topk, sink_pages=sink, q_dtype=q.dtype, keep_scores=True, select_chunks=chunks)
+    if chunks is not None:
+        assert dec.chunks == chunks
     out = dec.step(q)
     torch.cuda.synchronize()
     b, hkv, page, d = cache.batch, cache.n_kv_heads, cache.page_size, cache.head_dim
@@ -430,6 +432,19 @@ def test_quest_decode_config2_shape_reduced(cuda, lens):
     q = torch.randn(b, hq, 1, d, generator=gen)
     cache, table = _make_paged(b, hkv, d, page, lens, torch.bfloat16, gen)
     _check_decode(cache, table, q.to(torch.bfloat16).to(cuda), 34, 1, TOL_16)
+
+
+@pytest.mark.parametrize("chunks", [1, 2, 3, 7])
+def test_quest_decode_select_chunks(cuda, chunks):
+    """The single-CTA fused selection (1 chunk) and the candidates form + merge (several
+    chunks, ragged sequences ending inside and before chunks) give the same top-k, union
+    and output."""
+    gen = torch.Generator().manual_seed(100 + chunks)
+    lens = [8192, 5000, 64, 6401, 8129]
+    b, hq, hkv, d, page = len(lens), 16, 2, 128, 64
+    q = torch.randn(b, hq, 1, d, generator=gen)
+    cache, table = _make_paged(b, hkv, d, page, lens, torch.bfloat16, gen)
+    _check_decode(cache, table, q.to(torch.bfloat16).to(cuda), 34, 1, TOL_16, chunks=chunks)
 
 
 def test_paged_bad_page_id_reports_status(cuda, monkeypatch):

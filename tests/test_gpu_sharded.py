@@ -51,15 +51,15 @@ def test_sharded_decode_matches_single_cache(cuda, dtype, world):
     ref_dec = QuestDecoder(full, hq, topk, sink_pages=sink, keep_scores=True)
     ref_out = ref_dec.step(q)
     decs = [ShardedQuestDecoder(c, hq, topk, [lo] * b, [hi] * b, sink_pages=sink, last_here=(hi == n_pages),
-                                sink_here=(lo == 0)) for c, lo, hi in shards]
+                                sink_here=(lo == 0), n_ranks=world) for c, lo, hi in shards]
     cands = [dec.candidates(q) for dec in decs]
-    all_s = torch.stack([c[0] for c in cands])
-    all_i = torch.stack([c[1] for c in cands])
+    all_s = torch.stack([c[0] for c in cands]).flatten(0, 1)  # (R * chunks, B, H_q, K)
+    all_i = torch.stack([c[1] for c in cands]).flatten(0, 1)
     for dec in decs:
         dec.merge(all_s, all_i)
     parts = [dec.partial(q) for dec in decs]
-    all_o = torch.stack([p[0].reshape(-1, d).clone() for p in parts])
-    all_l = torch.stack([p[1].reshape(-1).clone() for p in parts])
+    all_o = torch.stack([p[0].reshape(-1, d) for p in parts])
+    all_l = torch.stack([p[1].reshape(-1) for p in parts])
     out = decs[0].combine(all_o, all_l)
     torch.cuda.synchronize()
     # the global selection equals the single cache's, order included
@@ -89,3 +89,38 @@ def test_sharded_decode_matches_single_cache(cuda, dtype, world):
     assert np.all(err <= tol + 2.0 ** -8 * np.abs(ref)), err.max()
     # and the single-cache decoder agrees with it too
     assert np.abs(_np(ref_out[:, :, 0]) - ref).max() <= tol + 2.0 ** -8 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("world,chunks", [(1, None), (1, 5), (2, None), (2, 3), (4, 2)])
+def test_sharded_decode_packed_exchange(cuda, world, chunks):
+    """The packed path of ``step``: one gathered [scores | ids] buffer and one gathered
+    [o | lse] buffer per rank, read in place by the merge and combine kernels through
+    their rank strides; several chunks per shard."""
+    from linattn_b200 import QuestDecoder
+    from linattn_b200.sharded import ShardedQuestDecoder
+
+    gen = torch.Generator().manual_seed(31 + world)
+    b, hq, hkv, d, page, n_pages, topk = 3, 8, 2, 128, 64, 36, 6
+    full, shards, k, v = _build(torch.bfloat16, b, hkv, d, page, n_pages, world, gen)
+    q = torch.randn(b, hq, 1, d, generator=gen).bfloat16().cuda()
+    ref_dec = QuestDecoder(full, hq, topk, keep_scores=True)
+    ref_out = ref_dec.step(q).clone()
+    decs = [ShardedQuestDecoder(c, hq, topk, [lo] * b, [hi] * b, last_here=(hi == n_pages), sink_here=(lo == 0),
+                                n_ranks=world, select_chunks=chunks) for c, lo, hi in shards]
+    if world == 1:
+        out = decs[0].step(q, exchange=lambda t: t.unsqueeze(0))
+    else:
+        for dec in decs:
+            dec.candidates(q)
+        allc = torch.stack([dec.cand for dec in decs])
+        for dec in decs:
+            dec.merge_packed(allc)
+        for dec in decs:
+            dec.partial(q)
+        out = decs[0].combine_packed(torch.stack([dec.part for dec in decs]))
+    torch.cuda.synchronize()
+    ref_ids = ref_dec.ids[:, :, 0].cpu().numpy()
+    for dec in decs:
+        assert np.array_equal(dec.sel.cpu().numpy(), ref_ids)
+    err = (out.float() - ref_out.float()).abs().max().item()
+    assert err <= 2e-3 + 2.0 ** -8 * ref_out.float().abs().max().item(), err

@@ -41,7 +41,7 @@ def _worker(rank, world, port, seed, q):
         os.environ["MASTER_ADDR"] = "127.0.0.1"
         os.environ["MASTER_PORT"] = str(port)
         dist.init_process_group("gloo", rank=rank, world_size=world)
-        from linattn_b200.sharded import exchange_candidates, exchange_partials, shard_page_ranges
+        from linattn_b200.sharded import exchange_candidates, exchange_packed, exchange_partials, shard_page_ranges
 
         rng = np.random.default_rng(seed)
         b, h, n_pages, topk = 2, 4, 37, 6
@@ -65,6 +65,11 @@ def _worker(rank, world, port, seed, q):
         lse = torch.full((3,), float(rank))
         all_o, all_l = exchange_partials(o, lse)
         assert torch.equal(all_o[1], torch.ones(3, 5)) and torch.equal(all_l[0], torch.zeros(3))
+        # packed buffers: one (2, B, H, K) int32 candidate block per rank, rank-major
+        cand = torch.stack([torch.from_numpy(sc).view(torch.int32), torch.from_numpy(ids)])
+        allc = exchange_packed(cand)
+        assert tuple(allc.shape) == (world, 2, b, h, topk)
+        assert torch.equal(allc[:, 0].view(torch.float32), all_s) and torch.equal(allc[:, 1], all_i)
         q.put((rank, "ok"))
     except Exception as e:  # reported to the parent
         q.put((rank, repr(e)))
