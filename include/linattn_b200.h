@@ -405,8 +405,10 @@ int linattn_block_sparse_prefill(const void* q, int32_t dtype, int64_t B, int64_
 
 /*
  * Sequence-sharded Quest decode, merge step.  scores / ids (R, B, H_q, K): the R
- * shards' local top-K candidates (fp32 scores, global page ids, -1 = none), rank-major
- * as an all-gather leaves them.  Per (b, query head) the global top-`topk` by (score
+ * shards' (or chunks') local top-K candidates (fp32 scores, global page ids, -1 =
+ * none), rank-major as an all-gather leaves them; each row of K sorted by (score desc,
+ * page asc) with the -1 slots last, and no page in two blocks (as
+ * linattn_quest_decode_candidates writes them).  Per (b, query head) the global top-`topk` by (score
  * desc, page asc) is taken (written to sel (B, H_q, topk), -1 padded, when sel is not
  * NULL); the pages of this shard, [page_lo[b], page_hi[b]), selected by any head of a
  * kv head's group go to union_ids (B, H_kv, max_union) as ascending LOCAL ids

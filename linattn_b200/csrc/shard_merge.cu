@@ -6,9 +6,11 @@
 // candidates (rank-major).  One CTA per (sequence, kv head) ranks each head's
 // candidates by a 64-bit key (order-preserving score, then the bitwise complement of
 // the page id, so equal scores go to the lowest page: the single-cache top-k's
-// tie-break), bitonic-sorted in shared memory, takes the first k, and marks the pages
-// of this shard's range [page_lo_b, page_hi_b) in a bitmap; the bitmap compacts to the
-// ascending local page list the attention reads.  No counterpart in the reference (it
+// tie-break); each block of K arrives sorted by that key (the candidates kernel
+// writes them so) and the blocks hold disjoint pages, so a candidate's rank is its
+// position in its block plus a binary search in every other block.  The first k go
+// to `sel`, and those in this shard's range [page_lo_b, page_hi_b) to a bitmap that
+// compacts to the ascending local page list the attention reads.  No counterpart in the reference (it
 // never shards the KV sequence); the selection equals page_select_torch's top-k
 // (src/linattn/kernels/triton/quest_pages.py:57-78) over the union of the shards' pages
 // whenever each shard's k candidates include its share of the global top-k, which
@@ -24,7 +26,7 @@ namespace {
 struct ShardMergeParams {
   const float* scores;   // (R, B, Hq, K)
   const int32_t* ids;    // (R, B, Hq, K) global page ids, -1 = none
-  int64_t R, B, Hq, K, rs, topk, G, np2;  // rs: elements between shards' blocks
+  int64_t R, B, Hq, K, rs, topk, G;  // rs: elements between shards' blocks
   const int32_t* page_lo;  // (B) first global page of this shard
   const int32_t* page_hi;  // (B) one past its last
   int64_t max_local;       // local pages (bitmap size)
@@ -37,12 +39,26 @@ struct ShardMergeParams {
   int32_t* union_tokens;    // (B, Hkv) tokens of the union pages, or NULL
 };
 
-__global__ void __launch_bounds__(256) shard_merge_kernel(const ShardMergeParams p) {
+__device__ __forceinline__ unsigned long long cand_key(const ShardMergeParams& p, int64_t off) {
+  const int32_t id = p.ids[off];
+  return id >= 0 ? (static_cast<unsigned long long>(float_key(p.scores[off])) << 32) |
+                       static_cast<unsigned long long>(~static_cast<uint32_t>(id))
+                 : 0ull;  // empty slots rank last
+}
+
+// WARP: one warp per head merges the R sorted blocks (at most 64, two per lane): each
+// step the warp takes the largest block head (two 32-bit warp max-reductions over the
+// unique 64-bit keys) and its lane advances, so the top-k come out in order after k
+// steps.  Heads run in waves of `hpw` warps, each staging its head's keys in its own
+// shared-memory slice.  Otherwise: all threads rank every candidate by binary search.
+template <bool WARP>
+__global__ void __launch_bounds__(256) shard_merge_kernel(const ShardMergeParams p, int hpw) {
   extern __shared__ unsigned long long msm[];
-  unsigned long long* keys = msm;                                    // [np2]
-  uint32_t* bits = reinterpret_cast<uint32_t*>(keys + p.np2);        // [(max_local + 31) / 32]
+  const int64_t n = p.R * p.K;
+  unsigned long long* keys = msm;                                    // [R * K] or [hpw][R * K]
+  uint32_t* bits = reinterpret_cast<uint32_t*>(keys + (WARP ? hpw : 1) * n);  // [(max_local + 31) / 32]
   __shared__ uint32_t scratch[256 / 32 + 1];
-  __shared__ uint32_t sh_tokens;
+  __shared__ uint32_t sh_tokens, sh_valid;
   const int tid = threadIdx.x;
   if (tid == 0) sh_tokens = 0u;
   const int64_t bk = blockIdx.x;  // (b, kv head)
@@ -51,46 +67,84 @@ __global__ void __launch_bounds__(256) shard_merge_kernel(const ShardMergeParams
   const int64_t lo = p.page_lo[b], hi = p.page_hi[b];
   const int64_t nwords = (p.max_local + 31) / 32;
   for (int64_t i = tid; i < nwords; i += 256) bits[i] = 0u;
-  const int64_t n = p.R * p.K;
+  __syncthreads();
+  if constexpr (WARP) {
+    const int warp = tid >> 5, lane = tid & 31;
+    unsigned long long* kw = keys + warp * n;
+    for (int64_t g = warp; g < p.G && warp < hpw; g += hpw) {
+      const int64_t h = kvh * p.G + g;
+      for (int64_t i = lane; i < n; i += 32) {
+        const int64_t r = i / p.K, e = i % p.K;
+        kw[i] = cand_key(p, r * p.rs + (b * p.Hq + h) * p.K + e);
+      }
+      __syncwarp();
+      const int64_t r0 = lane, r1 = lane + 32;
+      int64_t p0 = 0, p1 = 0;
+      int64_t i = 0;
+      for (; i < p.topk; ++i) {
+        const unsigned long long k0 = (r0 < p.R && p0 < p.K) ? kw[r0 * p.K + p0] : 0ull;
+        const unsigned long long k1 = (r1 < p.R && p1 < p.K) ? kw[r1 * p.K + p1] : 0ull;
+        const unsigned long long mine = k0 > k1 ? k0 : k1;
+        const uint32_t khi = static_cast<uint32_t>(mine >> 32), klo = static_cast<uint32_t>(mine);
+        const uint32_t hmax = __reduce_max_sync(0xffffffffu, khi);
+        const uint32_t lmax = __reduce_max_sync(0xffffffffu, khi == hmax ? klo : 0u);
+        if (hmax == 0u && lmax == 0u) break;  // every block exhausted (warp-uniform)
+        if (khi == hmax && klo == lmax) {     // the unique winner
+          const int32_t id = static_cast<int32_t>(~lmax);
+          if (p.sel) p.sel[(b * p.Hq + h) * p.topk + i] = id;
+          if (id >= lo && id < hi && id - lo < p.max_local)
+            atomicOr(&bits[(id - lo) >> 5], 1u << ((id - lo) & 31));
+          if (k0 > k1) ++p0;
+          else ++p1;
+        }
+      }
+      if (p.sel)
+        for (int64_t r = i + lane; r < p.topk; r += 32) p.sel[(b * p.Hq + h) * p.topk + r] = -1;
+      __syncwarp();
+    }
+  } else {
   for (int64_t g = 0; g < p.G; ++g) {
     const int64_t h = kvh * p.G + g;
     __syncthreads();
-    for (int64_t i = tid; i < p.np2; i += 256) {
-      unsigned long long key = 0ull;  // padding and empty slots sort last
-      if (i < n) {
-        const int64_t r = i / p.K, e = i % p.K;
-        const int64_t off = r * p.rs + (b * p.Hq + h) * p.K + e;
-        const int32_t id = p.ids[off];
-        if (id >= 0)
-          key = (static_cast<unsigned long long>(float_key(p.scores[off])) << 32) |
-                static_cast<unsigned long long>(~static_cast<uint32_t>(id));
-      }
-      keys[i] = key;
+    if (tid == 0) sh_valid = 0u;
+    for (int64_t i = tid; i < n; i += 256) {
+      const int64_t r = i / p.K, e = i % p.K;
+      keys[i] = cand_key(p, r * p.rs + (b * p.Hq + h) * p.K + e);
     }
     __syncthreads();
-    // bitonic sort, descending
-    for (int64_t size = 2; size <= p.np2; size <<= 1) {
-      for (int64_t stride = size >> 1; stride > 0; stride >>= 1) {
-        for (int64_t i = tid; i < p.np2; i += 256) {
-          const int64_t j = i ^ stride;
-          if (j > i) {
-            const bool desc = (i & size) == 0;
-            const unsigned long long a = keys[i], c = keys[j];
-            if ((a > c) != desc && a != c) {
-              keys[i] = c;
-              keys[j] = a;
-            }
-          }
+    // Every block is sorted by key, descending, empty slots last, and keys are unique,
+    // so a candidate's global rank is its position in its own block plus, for every
+    // other block, the number of keys there above it (a binary search).
+    uint32_t my_valid = 0u;
+    for (int64_t i = tid; i < n; i += 256) {
+      const unsigned long long kx = keys[i];
+      if (kx == 0ull) continue;
+      ++my_valid;
+      const int64_t r = i / p.K;
+      int64_t rank = i - r * p.K;
+      for (int64_t r2 = 0; r2 < p.R && rank < p.topk; ++r2) {
+        if (r2 == r) continue;
+        const unsigned long long* blk = keys + r2 * p.K;
+        int64_t a = 0, z = p.K;
+        while (a < z) {
+          const int64_t mid = (a + z) >> 1;
+          if (blk[mid] > kx) a = mid + 1;
+          else z = mid;
         }
-        __syncthreads();
+        rank += a;
+      }
+      if (rank < p.topk) {
+        const int32_t id = static_cast<int32_t>(~static_cast<uint32_t>(kx & 0xffffffffull));
+        if (p.sel) p.sel[(b * p.Hq + h) * p.topk + rank] = id;
+        if (id >= lo && id < hi && id - lo < p.max_local) atomicOr(&bits[(id - lo) >> 5], 1u << ((id - lo) & 31));
       }
     }
-    for (int64_t i = tid; i < p.topk; i += 256) {
-      const unsigned long long key = i < n ? keys[i] : 0ull;
-      const int32_t id = key ? static_cast<int32_t>(~static_cast<uint32_t>(key & 0xffffffffull)) : -1;
-      if (p.sel) p.sel[(b * p.Hq + h) * p.topk + i] = id;
-      if (id >= lo && id < hi && id - lo < p.max_local) atomicOr(&bits[(id - lo) >> 5], 1u << ((id - lo) & 31));
-    }
+    atomicAdd(&sh_valid, my_valid);
+    __syncthreads();
+    if (p.sel)
+      for (int64_t r = lmin(static_cast<int64_t>(sh_valid), p.topk) + tid; r < p.topk; r += 256)
+        p.sel[(b * p.Hq + h) * p.topk + r] = -1;
+  }
   }
   __syncthreads();
   // ascending local union: popcount scan over the bitmap words
@@ -138,26 +192,32 @@ extern "C" int linattn_shard_merge(const float* scores, const int32_t* ids, int6
   if (R < 1 || K < 1 || topk < 1 || n_kv_heads < 1 || Hq % n_kv_heads || max_local < 1 || max_union < 1)
     return set_error(LINATTN_EINVAL, "shard_merge: bad sizes");
   if (rank_stride != 0 && rank_stride < B * Hq * K) return set_error(LINATTN_EINVAL, "shard_merge: rank_stride");
-  int64_t np2 = 1;
-  while (np2 < R * K) np2 <<= 1;
-  if (np2 > 4096 || max_local > (int64_t(1) << 20))
+  if (R * K > 4096 || max_local > (int64_t(1) << 20))
     return set_error(LINATTN_EUNSUPPORTED, "shard_merge: at most 4096 candidates and 2^20 local pages");
   if (B * n_kv_heads == 0) return LINATTN_OK;
   ShardMergeParams p;
   p.scores = scores; p.ids = ids; p.R = R; p.B = B; p.Hq = Hq; p.K = K;
   p.rs = rank_stride ? rank_stride : B * Hq * K; p.topk = topk; p.G = Hq / n_kv_heads;
-  p.np2 = np2; p.page_lo = page_lo; p.page_hi = page_hi; p.max_local = max_local; p.sel = sel;
+  p.page_lo = page_lo; p.page_hi = page_hi; p.max_local = max_local; p.sel = sel;
   p.union_ids = union_ids; p.union_count = union_count; p.max_union = max_union;
   if (union_tokens && (!seq_lens || page_size < 1))
     return set_error(LINATTN_EINVAL, "shard_merge: union_tokens needs seq_lens and page_size");
   p.seq_lens = seq_lens; p.P = page_size; p.union_tokens = union_tokens;
-  const size_t smem = static_cast<size_t>(np2) * 8 + static_cast<size_t>((max_local + 31) / 32) * 4;
+  const size_t bits_bytes = static_cast<size_t>((max_local + 31) / 32) * 4;
+  const size_t head_bytes = static_cast<size_t>(R * K) * 8;
+  // the warp merge for up to 64 blocks, with as many heads per wave as 160 KiB hold
+  const int hpw = static_cast<int>(lmin(lmin(8, p.G), static_cast<int64_t>((160 * 1024) / head_bytes)));
+  const bool warp = R <= 64 && hpw >= 1;
+  const size_t smem = (warp ? hpw : 1) * head_bytes + bits_bytes;
   if (smem > 200 * 1024) return set_error(LINATTN_EUNSUPPORTED, "shard_merge: shared memory");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaFuncSetAttribute(shard_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
+  cudaError_t e = warp ? cudaFuncSetAttribute(shard_merge_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              static_cast<int>(smem))
+                       : cudaFuncSetAttribute(shard_merge_kernel<false>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e == cudaSuccess) {
-    shard_merge_kernel<<<static_cast<unsigned>(B * n_kv_heads), 256, smem, st>>>(p);
+    if (warp) shard_merge_kernel<true><<<static_cast<unsigned>(B * n_kv_heads), 256, smem, st>>>(p, hpw);
+    else shard_merge_kernel<false><<<static_cast<unsigned>(B * n_kv_heads), 256, smem, st>>>(p, 1);
     e = cudaGetLastError();
   }
   if (e != cudaSuccess) {

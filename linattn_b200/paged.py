@@ -187,28 +187,45 @@ class PagedKVCache:
             L.check_status(self.device)
 
 
-def fused_select_smem(chunk: int, g: int, topk: int, d: int, stages: int) -> int:
-    """Shared memory of the fused selection kernel for `chunk` pages per CTA."""
-    return stages * 32 * 2 * d * 2 + g * chunk * 4 + 8 * 256 * 4 + ((chunk + 31) // 32) * 4 + 8 * 2 * topk * 4
+def fused_select_smem(chunk: int, g: int, topk: int, d: int, mma: bool, cand: bool) -> int:
+    """Shared memory of the fused selection kernel for `chunk` pages per CTA: the
+    tensor-core path (q and metadata of one 16-bit type) streams 4 (single-CTA form) or
+    2 (candidates form) stages of 64 pages, the CUDA-core path 8 or 4 stages of 32."""
+    rest = g * chunk * 4 + 8 * 256 * 4 + ((chunk + 31) // 32) * 4 + 8 * 2 * topk * 4
+    if mma:
+        return 1024 + (2 if cand else 4) * 2 * d * 64 * 2 + rest
+    return (4 if cand else 8) * 32 * 2 * d * 2 + rest
+
+
+_SMEM_MAX = 220 * 1024
+_SMEM_TWO_PER_SM = 113 * 1024
 
 
 def plan_select_chunks(n: int, g: int, topk: int, d: int, units: int, device, chunks: Optional[int] = None,
-                       ranks: int = 1):
+                       ranks: int = 1, mma: bool = True, cand_only: bool = False):
     """(pages per CTA, chunks) for the fused selection over `n` pages and `units`
-    (sequence, kv head) pairs: enough CTAs for two per SM, at least 128 pages per
-    chunk, the chunk's scores in shared memory, and at most 4096 candidates per head
-    across the chunks of all `ranks` (the merge kernel's bound)."""
+    (sequence, kv head) pairs.  One chunk (the single-CTA form, no merge) when the
+    pairs alone fill the GPU and the whole sequence's scores fit in shared memory;
+    else chunks small enough for two CTAs per SM and numerous enough for two CTAs per
+    SM.  Returns 0 chunks when the merge's bound (4096 candidates per head across the
+    chunks of all `ranks`) or shared memory rules the fused kernel out."""
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
     if chunks is None:
-        sms = torch.cuda.get_device_properties(device).multi_processor_count
-        chunks = max(1, min(-(-2 * sms // max(1, units)), n // 128))
+        if not cand_only and units >= 0.8 * sms and fused_select_smem(n, g, topk, d, mma, False) <= _SMEM_MAX:
+            chunks = 1
+        else:
+            cap = 64
+            while cap * 2 <= n and fused_select_smem(cap * 2, g, topk, d, mma, True) <= _SMEM_TWO_PER_SM:
+                cap *= 2
+            chunks = max(-(-n // cap), min(-(-2 * sms // max(1, units)), -(-n // 128)))
     chunks = max(1, min(chunks, n))
     chunk = -(-n // chunks)
-    stages = 8 if chunks == 1 else 4
-    while fused_select_smem(chunk, g, topk, d, stages) > 200 * 1024 and chunk > 32:
+    single = chunks == 1 and not cand_only
+    while fused_select_smem(chunk, g, topk, d, mma, not single) > _SMEM_MAX and chunk > 32:
         chunk = -(-chunk // 2)
-        stages = 4
+        single = False
     chunks = -(-n // chunk)
-    if chunks * ranks * topk > 4096:
+    if chunks * ranks * topk > 4096 or fused_select_smem(chunk, g, topk, d, mma, not single) > _SMEM_MAX:
         return chunk, 0
     return chunk, chunks
 
@@ -245,11 +262,10 @@ class QuestDecoder:
                       and cache.meta_dtype in (torch.float16, torch.bfloat16))
         self.chunks = 1
         if self.fused:
+            mma = q_dtype == cache.meta_dtype
             self.chunk_pages, self.chunks = plan_select_chunks(n, group_size, self.topk, cache.head_dim,
-                                                               b * cache.n_kv_heads, dev, select_chunks)
-            if self.chunks == 1 and fused_select_smem(n, group_size, self.topk, cache.head_dim, 8) > 220 * 1024:
-                self.chunks = 0  # no chunking fits: unfused path
-            self.fused = self.chunks >= 1
+                                                               b * cache.n_kv_heads, dev, select_chunks, mma=mma)
+            self.fused = self.chunks >= 1  # else the unfused path (scores, then top-k)
         self.keep_scores = keep_scores or not self.fused
         self.scores = torch.empty(b, n_heads, 1, n, dtype=torch.float32, device=dev) if self.keep_scores else None
         if self.fused and self.chunks > 1:

@@ -111,7 +111,8 @@ class ShardedQuestDecoder:
             raise NotImplementedError("sharded decode needs f16/bf16 page metadata, head_dim 64 or 128 and a GQA "
                                       "group of 1, 2, 4 or 8 query heads")
         self.chunk_pages, self.chunks = plan_select_chunks(cache.max_pages, g, topk, d, b * hkv, dev, select_chunks,
-                                                           ranks=n_ranks)
+                                                           ranks=n_ranks, mma=q_dtype == cache.meta_dtype,
+                                                           cand_only=True)
         if self.chunks == 0:
             raise NotImplementedError(f"sharded decode: {n_ranks} ranks x topk {topk} exceed the merge kernel's 4096 "
                                       "candidates per head")
