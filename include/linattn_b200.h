@@ -395,13 +395,27 @@ int linattn_merge_block_lists(const int32_t* topk, int64_t rows, int64_t k, int6
  * MInferenceAttention._block_sparse and MoBAAttention.select
  * (src/linattn/variants/selection.py:339-353, 635-649, 86-116) and
  * block_sparse_attention_torch for prefill (src/linattn/kernels/triton/block_sparse.py:40-75).
+ * With bf16 inputs, v_f16 / v_scale (from linattn_prefill_v_to_f16, or NULL) let the
+ * P V product run in f16 with a single P part: V is read from v_f16 and O multiplied
+ * by v_scale[b * H_kv + kv head]; without them P is split into bf16 hi + lo parts.
  */
 int linattn_block_sparse_prefill(const void* q, int32_t dtype, int64_t B, int64_t Hq, int64_t Tq, const void* k,
                                  const void* v, int64_t Hkv, int64_t Tk, int64_t D, const int32_t* ids,
                                  const int32_t* counts, const int64_t* id_strides /*[3]*/, int64_t n_max,
                                  int64_t rows_per_list, const int64_t* count_strides /*[3]*/, int64_t sink,
                                  int32_t causal, int64_t offset, float scale, void* out,
-                                 const int64_t* out_strides /*[4]*/, float* lse_out, int32_t* status, void* stream);
+                                 const int64_t* out_strides /*[4]*/, float* lse_out, const void* v_f16,
+                                 const float* v_scale, int32_t* status, void* stream);
+
+/*
+ * f16 copy of a contiguous bf16 V for linattn_block_sparse_prefill: `heads` blocks of
+ * `per_head` elements (B * H_kv blocks of T_k * 128); per block a power-of-two scale
+ * s >= 1 with max|V| / s <= 2^15 (s = 1 unless |V| exceeds 2^15), out = V / s rounded
+ * to f16 (exact for every value in f16's normal range), scale[block] = s.
+ * amax_scratch: `heads` uint32 of device scratch.  No reference counterpart.
+ */
+int linattn_prefill_v_to_f16(const void* v, int64_t heads, int64_t per_head, void* out, float* scale,
+                             uint32_t* amax_scratch, void* stream);
 
 /*
  * Sequence-sharded Quest decode, merge step.  scores / ids (R, B, H_q, K): the R

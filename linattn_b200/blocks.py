@@ -110,10 +110,15 @@ def moba_select(q: torch.Tensor, k: torch.Tensor, block: int, topk: int, *,
 def block_sparse_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ids: torch.Tensor, *,
                          counts: Optional[torch.Tensor] = None, rows_per_list: int = 64, sink: int = 0,
                          causal: bool = True, offset: int = 0, scale: Optional[float] = None,
-                         lse_out: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                         lse_out: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                         v_f16: Optional[bool] = None) -> torch.Tensor:
     """Block-sparse causal prefill on the tcgen05 tensor cores: query ``t`` reads the
     64-token key blocks of ``ids[b, h, t // rows_per_list]`` (ascending, -1 padded) plus
-    the tokens below ``sink``.  ``q (B,H_q,T_q,128)``, ``k, v (B,H_kv,T_k,128)``, bf16 or f16."""
+    the tokens below ``sink``.  ``q (B,H_q,T_q,128)``, ``k, v (B,H_kv,T_k,128)``, bf16 or f16.
+
+    For bf16 inputs, ``v_f16`` (default on) first copies V to f16 (exact up to a
+    per-(b, kv head) power-of-two scale) so that the P V product takes one f16 P part
+    instead of bf16 hi + lo parts."""
     dev = L.require_cuda(q, k, v, ids, counts, lse_out)
     if q.dtype != k.dtype or k.dtype != v.dtype:
         raise ValueError("q, k and v must have one dtype (bf16 or f16)")
@@ -132,10 +137,18 @@ def block_sparse_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ids:
         out = torch.empty_like(q)
     scale = (1.0 / math.sqrt(d)) if scale is None else float(scale)
     status = L.status_word(dev)
+    v16 = vsc = None
+    if q.dtype == torch.bfloat16 and v_f16 is not False:
+        v16 = torch.empty(v.shape, dtype=torch.float16, device=dev)
+        vsc = torch.empty(b * hkv, dtype=torch.float32, device=dev)
+        amax = torch.empty(b * hkv, dtype=torch.int32, device=dev)
+        L.check(L.lib().linattn_prefill_v_to_f16(v.data_ptr(), b * hkv, tk * d, v16.data_ptr(), vsc.data_ptr(),
+                                                 amax.data_ptr(), L.stream_of(q)))
     L.check(L.lib().linattn_block_sparse_prefill(
         q.data_ptr(), L.dtype_code(q), b, hq, tq, k.data_ptr(), v.data_ptr(), hkv, tk, d, ids.data_ptr(),
         L.ptr(counts), (L.c_i64 * 3)(*ids.stride()[:3]), ids.shape[-1], rows_per_list, cs, sink, int(causal), offset,
-        scale, out.data_ptr(), L.strides4(out), L.ptr(lse_out), status.data_ptr(), L.stream_of(q)))
+        scale, out.data_ptr(), L.strides4(out), L.ptr(lse_out), L.ptr(v16), L.ptr(vsc), status.data_ptr(),
+        L.stream_of(q)))
     if L.strict():
         L.check_status(dev)
     return out

@@ -27,9 +27,10 @@
 //              running (O, m, l), the two O accumulators merged in the epilogue.
 //              tcgen05.ld of the scores,
 //              masks, online softmax in the log2 domain, then P written back over its
-//              scores (tcgen05.st): bf16 as hi + lo parts (two products, P to ~2^-17),
-//              f16 as one part with the row sum of the rounded P (O / l an exact
-//              weighted mean of V rows).  O is rescaled in TMEM only when a row's
+//              scores (tcgen05.st): one f16 part when V is f16 (f16 inputs, or a bf16
+//              V copied to f16 beforehand with a per-(b, kv head) power-of-two scale),
+//              else bf16 hi + lo parts (two products, P to ~2^-17); a block that no row
+//              of a warp reads is skipped (P = 0 without exponentials).  O is rescaled in TMEM only when a row's
 //              running maximum grows by more than 8, so P stays below 2^8; the rare
 //              rescale waits for the PV in flight.  The epilogue reads O from TMEM,
 //              divides by the row sum and stores (full tiles: staged in the Q tile and
@@ -59,6 +60,7 @@ struct PrefillParams {
   int64_t os[4];
   int out_dtype;
   float* lse;             // (B, Hq, Tq) or NULL
+  const float* v_scale;   // (B, Hkv) factor of an f16 V copy, or NULL
   int64_t n_tiles;        // query tiles of 128 per (b, head)
   int64_t n_kb;           // key blocks
   int tma_out;            // out is contiguous (B, H_q, T_q, 128): full tiles leave through TMA stores
@@ -149,12 +151,6 @@ __device__ __forceinline__ void tma_prefetch_2d(const void* tmap, int x, int y) 
                "r"(x), "r"(y)
                : "memory");
 }
-__device__ __forceinline__ void tma_prefetch_kv(const void* tk, const void* tv, int y) {
-  tma_prefetch_2d(tk, 0, y);
-  tma_prefetch_2d(tk, 64, y);
-  tma_prefetch_2d(tv, 0, y);
-  tma_prefetch_2d(tv, 64, y);
-}
 // 2^x with the hardware approximation (ex2.approx.ftz: relative error ~2^-22; 2^-inf = 0)
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
@@ -166,16 +162,18 @@ __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.
 
 }  // namespace
 
-template <typename T>
+template <typename TQ, typename TV>
 __global__ void __launch_bounds__(320, 1)
     prefill_umma_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tmq,
                         const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                         const __grid_constant__ CUtensorMap tmo) {
-  using M = MmaOp<T>;
-  constexpr int AB = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
-  constexpr bool SPLIT = AB == 1;  // bf16 P as hi + lo
-  constexpr uint32_t IDESC_S = umma_idesc(AB, PQ, PSTEP, 0);
-  constexpr uint32_t IDESC_O = umma_idesc(AB, PQ, 128, 1);
+  using M = MmaOp<TV>;   // P, packed in V's type
+  using MQ = MmaOp<TQ>;  // the output, in q's type
+  constexpr int AB_S = std::is_same<TQ, __nv_bfloat16>::value ? 1 : 0;
+  constexpr int AB_O = std::is_same<TV, __nv_bfloat16>::value ? 1 : 0;
+  constexpr bool SPLIT = AB_O == 1;  // bf16 P as hi + lo
+  constexpr uint32_t IDESC_S = umma_idesc(AB_S, PQ, PSTEP, 0);
+  constexpr uint32_t IDESC_O = umma_idesc(AB_O, PQ, 128, 1);
   extern __shared__ __align__(128) uint8_t psmem_raw[];
   uint8_t* smem = psmem_raw + ((1024 - (smem_u32(psmem_raw) & 1023)) & 1023);
   uint8_t* sq = smem;          // Q boxes
@@ -372,8 +370,10 @@ __global__ void __launch_bounds__(320, 1)
         for (int kk = 0; kk < PSTEP / 16; ++kk) {
           const uint32_t od = tmem + 256 + (kk >> 2) * 128;
           const uint64_t bd = umma_desc(vb + kk * 2048, HALFB, 1024);
-          umma_f16_ts(od, pt + kk * 8, bd, IDESC_O, (j > 0 || (kk & 3) > 0) ? 1u : 0u);
-          if (SPLIT) umma_f16_ts(od, pt + 64 + kk * 8, bd, IDESC_O, 1u);
+          // keys [16 kk, 16 kk + 16): P columns 64 (kk / 4) + 8 (kk % 4), lo 32 further
+          const uint32_t pcol = pt + 64 * (kk >> 2) + 8 * (kk & 3);
+          umma_f16_ts(od, pcol, bd, IDESC_O, (j > 0 || (kk & 3) > 0) ? 1u : 0u);
+          if (SPLIT) umma_f16_ts(od, pcol + 32, bd, IDESC_O, 1u);
         }
         umma_commit(&pv_done[pb]);
         umma_commit(&v_empty[j % PVS]);
@@ -441,11 +441,14 @@ __global__ void __launch_bounds__(320, 1)
         if (p.causal) kend = min(kend, pos32 - key0 + 1);
         ke = max(0, kend);
       }
-      // raw scores; masks only where needed (scale > 0: max of raw = max / scale)
+      // raw scores; masks only where needed (scale > 0: max of raw = max / scale).  A
+      // block that no row of the warp reads is skipped: P = 0 without exponentials.
+      const bool none_in = __all_sync(0xffffffffu, ke == 0);
       float mx8[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) mx8[i] = -INFINITY;
-      if (ke >= PK) {
+      if (none_in) {
+      } else if (ke >= PK) {
 #pragma unroll
         for (int c = 0; c < 64; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], __uint_as_float(sv[c >> 5][c & 31]));
       } else {
@@ -487,31 +490,37 @@ __global__ void __launch_bounds__(320, 1)
         l *= alpha;
       }
       if (first || grow) m_used = mx;
-      // P = 2^(s * scale - m) over the scores: hi columns [32 hb, 32 hb + 32), lo 64 further;
-      // masked scores are -inf (P = 0); a row with nothing read yet has m = -inf: P = 0
+      // P = 2^(s * scale - m); masked scores are -inf (P = 0); a row with nothing read
+      // yet has m = -inf: P = 0
       const float sl = p.scale_log2;
       const float neg = m_used == -INFINITY ? -INFINITY : -m_used;
       float sum8[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) sum8[i] = 0.f;
       uint32_t hi[32], lo[32];
+      if (none_in) {
 #pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const int c = 2 * e;
-        const float a = ex2_approx(fmaf(__uint_as_float(sv[c >> 5][c & 31]), sl, neg));
-        const float c2 = ex2_approx(fmaf(__uint_as_float(sv[(c + 1) >> 5][(c + 1) & 31]), sl, neg));
-        hi[e] = M::pack(a, c2);
-        const float2 rp = M::unpack(hi[e]);
-        if (SPLIT) {
-          lo[e] = M::pack(a - rp.x, c2 - rp.y);
+        for (int e = 0; e < 32; ++e) hi[e] = lo[e] = 0u;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int c = 2 * e;
+          const float a = ex2_approx(fmaf(__uint_as_float(sv[c >> 5][c & 31]), sl, neg));
+          const float c2 = ex2_approx(fmaf(__uint_as_float(sv[(c + 1) >> 5][(c + 1) & 31]), sl, neg));
+          hi[e] = M::pack(a, c2);
+          if (SPLIT) {
+            const float2 rp = M::unpack(hi[e]);
+            lo[e] = M::pack(a - rp.x, c2 - rp.y);
+          } else {
+            lo[e] = 0u;
+          }
           sum8[e & 7] += a + c2;
-        } else {
-          lo[e] = 0u;
-          sum8[e & 7] += rp.x + rp.y;
         }
       }
-      tmem_st32(lane_addr + sb * 128 + hb * 32, hi);
-      if (SPLIT) tmem_st32(lane_addr + sb * 128 + 64 + hb * 32, lo);
+      // P of this half over its own 64 score columns (hi at [64 hb, 64 hb + 32), lo 32
+      // further): the other half may still be reading its scores
+      tmem_st32(lane_addr + sb * 128 + hb * 64, hi);
+      if (SPLIT) tmem_st32(lane_addr + sb * 128 + hb * 64 + 32, lo);
       l += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
       tmem_wait_st();
       tc_fence_before();
@@ -539,7 +548,8 @@ __global__ void __launch_bounds__(320, 1)
     l = l * f_me + l_o * f_o;
     m_used = m_all;
     tc_fence_after();
-    const float inv = l > 0.f ? 1.f / l : 0.f;
+    const float vs = p.v_scale ? p.v_scale[b * p.Hkv + kvh] : 1.f;
+    const float inv = l > 0.f ? vs / l : 0.f;
     const int64_t ob = b * p.os[0] + h * p.os[1] + t * p.os[2];
     // full tiles with contiguous output: rows staged (swizzled, as TMA boxes) in the Q
     // tile, which every MMA has finished reading, then two TMA stores
@@ -566,7 +576,7 @@ __global__ void __launch_bounds__(320, 1)
           uint32_t w[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e)
-            w[e] = M::pack(__uint_as_float(ov[q4 * 8 + 2 * e]) * inv, __uint_as_float(ov[q4 * 8 + 2 * e + 1]) * inv);
+            w[e] = MQ::pack(__uint_as_float(ov[q4 * 8 + 2 * e]) * inv, __uint_as_float(ov[q4 * 8 + 2 * e + 1]) * inv);
           *reinterpret_cast<uint4*>(sq + hb * (PQ * 128) + r * 128 + ((c ^ (r & 7)) << 4)) =
               make_uint4(w[0], w[1], w[2], w[3]);
         }
@@ -608,12 +618,59 @@ __global__ void __launch_bounds__(320, 1)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
 }
 
+// bf16 V -> f16 copy for the single-part P product: per (b, kv head) a power-of-two
+// scale s >= 1 with max|V| / s <= 2^15 (s = 1 unless |V| exceeds 2^15, so the copy is
+// exact for every value in f16's normal range); the prefill multiplies O by s.
+__global__ void v_amax_kernel(const __nv_bfloat16* __restrict__ v, int64_t per_head, uint32_t* __restrict__ amax) {
+  const int64_t hd = blockIdx.y;
+  const __nv_bfloat16* src = v + hd * per_head;
+  float m = 0.f;
+  for (int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8; i < per_head;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x * 8) {
+    const uint4 w = *reinterpret_cast<const uint4*>(src + i);
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ws[e]));
+      m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(amax + hd, __float_as_uint(m));  // m >= 0: bit order = value order
+}
+
+__global__ void v_to_f16_kernel(const __nv_bfloat16* __restrict__ v, int64_t per_head,
+                                const uint32_t* __restrict__ amax, __half* __restrict__ out, float* __restrict__ scale) {
+  const int64_t hd = blockIdx.y;
+  const float a = __uint_as_float(amax[hd]);
+  float s = 1.f;
+  while (a / s > 32768.f && s < 1e30f) s *= 2.f;  // a NaN maximum keeps s = 1 (it propagates)
+  const float inv = 1.f / s;                      // a power of two: exact
+  if (blockIdx.x == 0 && threadIdx.x == 0) scale[hd] = s;
+  const __nv_bfloat16* src = v + hd * per_head;
+  __half* dst = out + hd * per_head;
+  for (int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8; i < per_head;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x * 8) {
+    const uint4 w = *reinterpret_cast<const uint4*>(src + i);
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ws[e]));
+      const __half2 hh = __floats2half2_rn(f.x * inv, f.y * inv);
+      o[e] = *reinterpret_cast<const uint32_t*>(&hh);
+    }
+    *reinterpret_cast<uint4*>(dst + i) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 namespace {
 
-template <typename T>
+template <typename TQ, typename TV>
 cudaError_t launch_prefill(const PrefillParams& p, const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
                            const CUtensorMap& o, cudaStream_t st) {
-  auto kern = prefill_umma_kernel<T>;
+  auto kern = prefill_umma_kernel<TQ, TV>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_DYN);
   if (e != cudaSuccess) return e;
   const int64_t grid = p.B * p.Hq * p.n_tiles;
@@ -627,13 +684,38 @@ cudaError_t launch_prefill(const PrefillParams& p, const CUtensorMap& q, const C
 
 using namespace linattn;
 
+extern "C" int linattn_prefill_v_to_f16(const void* v, int64_t heads, int64_t per_head, void* out, float* scale,
+                                        uint32_t* amax_scratch, void* stream) {
+  if (!v || !out || !scale || !amax_scratch) return set_error(LINATTN_EINVAL, "prefill_v_to_f16: NULL pointer");
+  if (per_head % 8 || reinterpret_cast<uintptr_t>(v) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
+    return set_error(LINATTN_EINVAL, "prefill_v_to_f16: 16-byte aligned rows of a multiple of 8 elements");
+  if (heads < 1 || heads > 65535) return set_error(LINATTN_EINVAL, "prefill_v_to_f16: 1 .. 65535 heads");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(amax_scratch, 0, static_cast<size_t>(heads) * 4, st);
+  const int64_t per_block = 256 * 8;
+  const unsigned gx = static_cast<unsigned>(lmin((per_head + per_block - 1) / per_block, 4096));
+  if (e == cudaSuccess) {
+    v_amax_kernel<<<dim3(gx, static_cast<unsigned>(heads)), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(v),
+                                                                          per_head, amax_scratch);
+    v_to_f16_kernel<<<dim3(gx, static_cast<unsigned>(heads)), 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(v), per_head, amax_scratch, static_cast<__half*>(out), scale);
+    e = cudaGetLastError();
+  }
+  if (e != cudaSuccess) {
+    char msg[256];
+    snprintf(msg, sizeof(msg), "prefill_v_to_f16: %s", cudaGetErrorString(e));
+    return set_error(LINATTN_ECUDA, msg);
+  }
+  return LINATTN_OK;
+}
+
 extern "C" int linattn_block_sparse_prefill(const void* q, int32_t dtype, int64_t B, int64_t Hq, int64_t Tq,
                                             const void* k, const void* v, int64_t Hkv, int64_t Tk, int64_t D,
                                             const int32_t* ids, const int32_t* counts, const int64_t* id_strides,
                                             int64_t n_max, int64_t rows_per_list, const int64_t* count_strides,
                                             int64_t sink, int32_t causal, int64_t offset, float scale, void* out,
-                                            const int64_t* out_strides, float* lse_out, int32_t* status,
-                                            void* stream) {
+                                            const int64_t* out_strides, float* lse_out, const void* v_f16,
+                                            const float* v_scale, int32_t* status, void* stream) {
   if (!q || !k || !v || !ids || !out || !id_strides || !out_strides)
     return set_error(LINATTN_EINVAL, "block_sparse_prefill: NULL pointer");
   if (dtype != LINATTN_BF16 && dtype != LINATTN_F16)
@@ -645,7 +727,10 @@ extern "C" int linattn_block_sparse_prefill(const void* q, int32_t dtype, int64_
   const int64_t n_kb = (Tk + PK - 1) / PK;
   if (n_kb > PMAXKB) return set_error(LINATTN_EUNSUPPORTED, "block_sparse_prefill: T_k above 2^18");
   if (counts && !count_strides) return set_error(LINATTN_EINVAL, "block_sparse_prefill: counts need strides");
-  if (reinterpret_cast<uintptr_t>(q) % 16 || reinterpret_cast<uintptr_t>(k) % 16 || reinterpret_cast<uintptr_t>(v) % 16)
+  if (v_f16 && (dtype != LINATTN_BF16 || !v_scale))
+    return set_error(LINATTN_EINVAL, "block_sparse_prefill: an f16 V copy goes with bf16 inputs and its scales");
+  if (reinterpret_cast<uintptr_t>(q) % 16 || reinterpret_cast<uintptr_t>(k) % 16 || reinterpret_cast<uintptr_t>(v) % 16 ||
+      reinterpret_cast<uintptr_t>(v_f16) % 16)
     return set_error(LINATTN_EINVAL, "block_sparse_prefill: q / K / V must be 16-byte aligned");
   if (B * Hq * Tq >= (int64_t(1) << 31) || B * Hkv * Tk >= (int64_t(1) << 31))
     return set_error(LINATTN_EUNSUPPORTED, "block_sparse_prefill: too many rows for 32-bit TMA coordinates");
@@ -656,7 +741,8 @@ extern "C" int linattn_block_sparse_prefill(const void* q, int32_t dtype, int64_
   const CUtensorMapDataType cu = dtype == LINATTN_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap tq, tk, tv;
   if (!tensor_map_2d(&tq, q, cu, 128, B * Hq * Tq, 256, 64, PQ) || !tensor_map_2d(&tk, k, cu, 128, B * Hkv * Tk, 256, 64, PK) ||
-      !tensor_map_2d(&tv, v, cu, 128, B * Hkv * Tk, 256, 64, PK))
+      !tensor_map_2d(&tv, v_f16 ? v_f16 : v, v_f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : cu, 128, B * Hkv * Tk, 256,
+                     64, PK))
     return set_error(LINATTN_ECUDA, "block_sparse_prefill: tensor map encoding failed");
   PrefillParams p;
   p.B = B; p.Hq = Hq; p.Hkv = Hkv; p.Tq = Tq; p.Tk = Tk;
@@ -667,6 +753,7 @@ extern "C" int linattn_block_sparse_prefill(const void* q, int32_t dtype, int64_
   p.sink = sink < 0 ? 0 : sink; p.causal = causal; p.offset = offset;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.out = out; p.out_dtype = dtype; p.lse = lse_out; p.status = status;
+  p.v_scale = v_f16 ? v_scale : nullptr;
   for (int i = 0; i < 4; ++i) p.os[i] = out_strides[i];
   p.n_tiles = (Tq + PQ - 1) / PQ;
   p.n_kb = n_kb;
@@ -676,8 +763,10 @@ extern "C" int linattn_block_sparse_prefill(const void* q, int32_t dtype, int64_
                               (B == 1 || out_strides[0] == Hq * Tq * 128) && reinterpret_cast<uintptr_t>(out) % 16 == 0;
   p.tma_out = contiguous_out && tensor_map_2d(&to, out, cu, 128, B * Hq * Tq, 256, 64, PQ) ? 1 : 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const cudaError_t e = dtype == LINATTN_BF16 ? launch_prefill<__nv_bfloat16>(p, tq, tk, tv, to, st)
-                                              : launch_prefill<__half>(p, tq, tk, tv, to, st);
+  cudaError_t e;
+  if (dtype == LINATTN_F16) e = launch_prefill<__half, __half>(p, tq, tk, tv, to, st);
+  else if (v_f16) e = launch_prefill<__nv_bfloat16, __half>(p, tq, tk, tv, to, st);
+  else e = launch_prefill<__nv_bfloat16, __nv_bfloat16>(p, tq, tk, tv, to, st);
   if (e != cudaSuccess) {
     char msg[256];
     snprintf(msg, sizeof(msg), "block_sparse_prefill: %s", cudaGetErrorString(e));

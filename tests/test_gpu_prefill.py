@@ -67,21 +67,22 @@ def _qkv(b, hq, hkv, tq, tk, d, dtype, seed, rank=0):
     return q.to(dtype), k.to(dtype), v.to(dtype)
 
 
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_prefill_full_lists_is_dense_causal(cuda, dtype):
+@pytest.mark.parametrize("dtype,v_f16", [(torch.bfloat16, None), (torch.bfloat16, False), (torch.float16, None)])
+def test_prefill_full_lists_is_dense_causal(cuda, dtype, v_f16):
     from linattn_b200.blocks import block_sparse_prefill
 
     b, hq, hkv, t, d = 1, 2, 1, 256, 128
     q, k, v = _qkv(b, hq, hkv, t, t, d, dtype, seed=1)
     nb = t // 64
     ids = torch.arange(nb, dtype=torch.int32).view(1, 1, 1, nb).expand(b, hq, nb, nb).contiguous()
-    out = block_sparse_prefill(q.cuda(), k.cuda(), v.cuda(), ids.cuda(), rows_per_list=64)
+    out = block_sparse_prefill(q.cuda(), k.cuda(), v.cuda(), ids.cuda(), rows_per_list=64, v_f16=v_f16)
     ref = oracle.dense_attention(_np(q), _np(k), _np(v), causal=True)
     assert_close_16(out, ref, dtype)
 
 
-@pytest.mark.parametrize("t,offset", [(512, 0), (300, 0), (200, 77)])
-def test_prefill_block_lists_vs_oracle(cuda, t, offset):
+@pytest.mark.parametrize("t,offset,v_f16", [(512, 0, None), (300, 0, None), (200, 77, None), (512, 0, False),
+                                            (200, 77, False)])
+def test_prefill_block_lists_vs_oracle(cuda, t, offset, v_f16):
     from linattn_b200.blocks import block_select, block_sparse_prefill
 
     b, hq, hkv, d = 2, 4, 2, 128
@@ -90,7 +91,8 @@ def test_prefill_block_lists_vs_oracle(cuda, t, offset):
     qd, kd, vd = q.cuda(), k.cuda(), v.cuda()
     ids, counts = block_select(qd, kd, 64, 2, sink_blocks=1, window_blocks=2, offset=offset)
     lse = torch.empty(b, hq, t, dtype=torch.float32, device="cuda")
-    out = block_sparse_prefill(qd, kd, vd, ids, counts=counts, rows_per_list=64, offset=offset, lse_out=lse)
+    out = block_sparse_prefill(qd, kd, vd, ids, counts=counts, rows_per_list=64, offset=offset, lse_out=lse,
+                               v_f16=v_f16)
     mask = token_mask(ids.cpu().numpy(), counts.cpu().numpy(), 64, t, tk, offset)
     assert_close_16(out, _oracle(q, k, v, mask), torch.bfloat16)
     # lse against the masked scores
@@ -100,6 +102,22 @@ def test_prefill_block_lists_vs_oracle(cuda, t, offset):
     mx = s.max(-1, keepdims=True)
     ref_lse = (mx + np.log(np.exp(s - mx).sum(-1, keepdims=True)))[..., 0]
     assert np.allclose(lse.cpu().numpy(), ref_lse, atol=2e-3)
+
+
+@pytest.mark.parametrize("v_gain", [1.0, 1e5])
+def test_prefill_f16_v_copy_scale(cuda, v_gain):
+    """bf16 inputs through the f16 V copy: with |V| up to ~4e5 the copy takes a
+    power-of-two scale above 1, which the epilogue multiplies back in."""
+    from linattn_b200.blocks import block_select, block_sparse_prefill
+
+    b, hq, hkv, t, d = 1, 4, 2, 640, 128
+    q, k, v = _qkv(b, hq, hkv, t, t, d, torch.bfloat16, seed=17, rank=8)
+    v = (v.float() * v_gain).to(torch.bfloat16)
+    qd, kd, vd = q.cuda(), k.cuda(), v.cuda()
+    ids, counts = block_select(qd, kd, 64, 3, sink_blocks=1, window_blocks=2)
+    out = block_sparse_prefill(qd, kd, vd, ids, counts=counts, rows_per_list=64, v_f16=True)
+    mask = token_mask(ids.cpu().numpy(), counts.cpu().numpy(), 64, t, t, 0)
+    assert_close_16(out.float() / v_gain, _oracle(q, k, v, mask) / v_gain, torch.bfloat16)
 
 
 def test_prefill_per_token_lists_and_sink(cuda):
