@@ -19,7 +19,8 @@ block-sparse causal prefill, B=2, T=131072; its TFLOP/s is ``prefill_tflops``) a
 config 3 (lightning indexer + causal top-2048 + token attention, T=32768), each timed
 with CUDA events over a few steps with the L2 flushed before each.
 
-``--workload c5`` runs config 5 instead: B=64 sequences of 1,048,576 tokens (fp8 KV)
+``--workload c3`` / ``--workload c4`` print config 3 / config 4 alone (one GPU;
+``--seq-len`` shortens T for profiling captures).  ``--workload c5`` runs config 5 instead: B=64 sequences of 1,048,576 tokens (fp8 KV)
 split across the N ranks (strong scaling), with NCCL all-gathers of the selection
 candidates and of the partial (o, lse).
 """
@@ -216,10 +217,10 @@ def build_c5(device, rank: int, world: int, n_q: int, batch: int = C5["B"]):
     return cache, qs.view(n_q, b, hq, 1, d).to(torch.bfloat16), (lo, hi)
 
 
-def build_c4(device, seed: int):
+def build_c4(device, seed: int, t: int = C4["T"]):
     """Config-4 inputs: Q/K N(0,1) plus a shared rank-8 component of amplitude 0.5, V N(0,1), bf16."""
     c = C4
-    b, hq, hkv, d, t = c["B"], c["Hq"], c["Hkv"], c["D"], c["T"]
+    b, hq, hkv, d = c["B"], c["Hq"], c["Hkv"], c["D"]
     g = torch.Generator(device=device).manual_seed(seed)
     u = torch.randn(c["rank"], d, generator=g, device=device)
     q = torch.randn(b, hq, t, d, generator=g, device=device)
@@ -232,14 +233,14 @@ def build_c4(device, seed: int):
     return q, k, v
 
 
-def build_c3(device, seed: int):
+def build_c3(device, seed: int, t: int = C3["T"]):
     """Config-3 inputs: bf16 Q/K/V N(0,1), indexer q/k N(0,1) with fp8 keys (per-64-token
     scales), indexer weights N(0, 1/64)."""
     from linattn_b200 import quantize_keys_fp8
 
     c = C3
     g = torch.Generator(device=device).manual_seed(seed)
-    b, t = c["B"], c["T"]
+    b = c["B"]
     q = torch.randn(b, c["Hq"], t, c["D"], generator=g, device=device).to(torch.bfloat16)
     k = torch.randn(b, c["Hkv"], t, c["D"], generator=g, device=device).to(torch.bfloat16)
     v = torch.randn(b, c["Hkv"], t, c["D"], generator=g, device=device).to(torch.bfloat16)
@@ -269,12 +270,12 @@ def _time_events(fn_parts, steps: int, warmup: int, flush, stream):
     return [statistics.mean(ev[i][j].elapsed_time(ev[i][j + 1]) for i in range(steps)) for j in range(len(fn_parts))]
 
 
-def secondary_c4(device, steps: int, warmup: int, flush, stream):
+def secondary_c4(device, steps: int, warmup: int, flush, stream, t: int = C4["T"]):
     """Config 4 on this GPU: block selection + block-sparse causal prefill (tcgen05)."""
     from linattn_b200.blocks import block_select, block_sparse_prefill
 
     c = C4
-    q, k, v = build_c4(device, 44)
+    q, k, v = build_c4(device, 44, t)
     res = {}
 
     def sel():
@@ -287,7 +288,7 @@ def secondary_c4(device, steps: int, warmup: int, flush, stream):
         block_sparse_prefill(q, k, v, res["ids"], counts=res["cnt"], rows_per_list=c["block"], out=out)
     ms_sel, ms_att = _time_events([sel, att], steps, warmup, flush, stream)
     cnt = res["cnt"].long()
-    bs, d, t = c["block"], c["D"], c["T"]
+    bs, d = c["block"], c["D"]
     # allowed (query, key) pairs, causal-exact: full 64x64 blocks off the diagonal, a triangle on it
     pairs = (cnt - 1).sum().item() * bs * bs + c["B"] * c["Hq"] * (t // bs) * (bs * (bs + 1) // 2)
     flops = 4 * d * pairs
@@ -300,13 +301,13 @@ def secondary_c4(device, steps: int, warmup: int, flush, stream):
             "launches_per_step": 5}
 
 
-def secondary_c3(device, steps: int, warmup: int, flush, stream):
+def secondary_c3(device, steps: int, warmup: int, flush, stream, t: int = C3["T"]):
     """Config 3 on this GPU: lightning indexer + causal top-2048 + token attention."""
     from linattn_b200 import indexer_topk
     from linattn_b200.dsa import token_sparse_attention
 
     c = C3
-    q, k, v, q_idx, codes, scales, w = build_c3(device, 33)
+    q, k, v, q_idx, codes, scales, w = build_c3(device, 33, t)
     res = {}
 
     def sel():
@@ -318,7 +319,7 @@ def secondary_c3(device, steps: int, warmup: int, flush, stream):
     def att():
         token_sparse_attention(q, k, v, res["ids"].unsqueeze(1), causal=True, out=out)
     ms_sel, ms_att = _time_events([sel, att], steps, warmup, flush, stream)
-    t, kk, d = c["T"], c["topk"], c["D"]
+    kk, d = c["topk"], c["D"]
     vis = sum(min(i + 1, kk) for i in range(t))  # selected tokens per query, causal
     gather = vis * c["Hkv"] * d * 2 * 2
     hbm, _, kind = measured_peaks()
@@ -328,6 +329,48 @@ def secondary_c3(device, steps: int, warmup: int, flush, stream):
             "attention_gathered_frac_of_hbm": round(gather / (ms_att * 1e-3) / 1e9 / hbm, 4), "peak_kind": kind,
             "attention_tflops": round(4 * c["Hq"] * d * vis / (ms_att * 1e-3) / 1e12, 1),
             "launches_per_step": 2 * -(-t // max(1, min(t, (1 << 29) // (t * 4)))) + 1}
+
+
+def run_prefill_workload(args):
+    """Config 3 or 4 alone on one GPU (``--workload c3|c4``; ``--seq-len`` shortens T for
+    profiling captures): one JSON line with the prefill's own metric and roofline."""
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    hbm, peak, kind = measured_peaks()
+    base = {"n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1); config-4 Q/K with a shared "
+            "rank-8 component)", "gpu_launches": None}
+    with ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[0])) as clocks:
+        if args.workload == "c4":
+            t = args.seq_len or C4["T"]
+            r = secondary_c4(device, args.steps, args.warmup, flush, stream, t)
+            line = dict(base, metric="block-sparse causal prefill TFLOP/s", value=r["prefill_tflops"], unit="TFLOP/s",
+                        ms_per_step=r["prefill_ms"],
+                        config={"workload": "block_sparse_prefill_c4" if t == C4["T"] else f"block_sparse_prefill_c4_t{t}",
+                                "l2": "flushed (256 MiB write) before every step, outside the timed events", **C4,
+                                "T": t},
+                        roofline={"bound": "tensor", "kernel": "prefill_umma_kernel", "achieved": r["prefill_tflops"],
+                                  "peak": peak, "unit": "TFLOP/s", "frac": r["frac_of_bf16_peak"], "peak_kind": kind,
+                                  "traffic": None, "algorithmic_flops_per_launch": r["algorithmic_flops"]},
+                        detail=r)
+            line["gpu_launches"] = r["launches_per_step"] * args.steps
+        else:
+            t = args.seq_len or C3["T"]
+            r = secondary_c3(device, args.steps, args.warmup, flush, stream, t)
+            line = dict(base, metric="DSA prefill tok/s", value=round(t / (r["total_ms"] * 1e-3), 1), unit="tok/s",
+                        ms_per_step=r["total_ms"],
+                        config={"workload": "dsa_indexer_attention_c3" if t == C3["T"] else f"dsa_c3_t{t}",
+                                "l2": "flushed (256 MiB write) before every step, outside the timed events", **C3,
+                                "T": t},
+                        roofline={"bound": "hbm", "kernel": "token_attention_kernel (gathered rows; L2 hits)",
+                                  "achieved": r["attention_gathered_gbs"], "peak": hbm, "unit": "GB/s",
+                                  "frac": r["attention_gathered_frac_of_hbm"], "peak_kind": kind, "traffic": None},
+                        detail=r)
+            line["gpu_launches"] = r["launches_per_step"] * args.steps
+    line["clocks"] = clocks.summary()
+    return line
 
 
 # ---------------------------------------------------------------------------------
@@ -780,8 +823,11 @@ def main(argv=None) -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences per GPU (default: the config's; smaller only for profiling captures)")
-    ap.add_argument("--workload", default="c2", choices=["c2", "c5"],
-                    help="c2: paged Quest decode (the headline); c5: million-token sequence-sharded decode")
+    ap.add_argument("--workload", default="c2", choices=["c2", "c3", "c4", "c5"],
+                    help="c2: paged Quest decode (the headline); c3: DSA indexer + token attention; c4: block-sparse "
+                         "prefill; c5: million-token sequence-sharded decode")
+    ap.add_argument("--seq-len", type=int, default=None,
+                    help="c3 / c4 only: a shorter sequence (profiling captures)")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the config-3 / config-4 legs reported beside the config-2 line")
     args = ap.parse_args(argv)
@@ -793,10 +839,10 @@ def main(argv=None) -> int:
     if args.impl == "reference":
         if rank != 0:
             return 0
-        if args.workload == "c5":
-            print(json.dumps({"impl": "reference", "unavailable": "the reference has no sequence-sharded decode and "
-                              "no fp8 paged CPU path at 1M tokens; its CPU arm is timed on the config-2 workload"}),
-                  flush=True)
+        if args.workload != "c2":
+            print(json.dumps({"impl": "reference", "unavailable": "the reference's CPU arm is timed on the config-2 "
+                              "workload (its torch paths for configs 3-5 need O(T^2) masks or more host memory than "
+                              "this box has)"}), flush=True)
             return 0
         print(json.dumps(run_reference(args)), flush=True)
         return 0
@@ -809,6 +855,10 @@ def main(argv=None) -> int:
     try:
         if args.workload == "c5":
             line = run_c5(args, rank, world, local_rank)
+        elif args.workload in ("c3", "c4"):
+            if world > 1:
+                raise SystemExit("--workload c3 / c4 run on one GPU")
+            line = run_prefill_workload(args)
         else:
             if args.batch is None:
                 args.batch = C2["B"]
