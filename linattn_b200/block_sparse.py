@@ -39,16 +39,18 @@ def plan_splits(b: int, hq: int, tq: int, d: int, kv_dtype: int, q_dtype: int, l
                 page_size: int, device: torch.device) -> int:
     """Split-KV factor for a call.
 
-    Tensor-core path: about 2 work items per resident warp (148 SMs x 8 warps), each
-    item keeping at least 4 tiles (and at most 128 list entries).  CUDA-core path: about 4 CTAs per SM, each split
-    keeping at least 2 tiles."""
+    Tensor-core path: at most one work item per resident warp (148 SMs x 8 warps), so
+    that every item starts in the first wave (a second partial wave of items costs more
+    than the longer items save), each item keeping at least 4 tiles (and at most 128
+    list entries).  CUDA-core path: about 4 CTAs per SM, each split keeping at least 2
+    tiles."""
     sms = torch.cuda.get_device_properties(device).multi_processor_count
     g_total = hq // list_heads
     if uses_tensor_cores(kv_dtype, q_dtype, d):
         tr = 2048 // d
         units = b * list_heads * tq * ((g_total + 7) // 8)
         tiles = max(1, (max_len * page_size + tr - 1) // tr) if page_size <= tr else max_len * -(-page_size // tr)
-        target, min_tiles = 16 * sms, 4
+        target, min_tiles = 8 * sms, 4
     else:
         eb = {L.F32: 4, L.F16: 2, L.BF16: 2, L.FP8E4M3: 1}[kv_dtype]
         tr = tile_rows(eb, d)
@@ -61,7 +63,8 @@ def plan_splits(b: int, hq: int, tq: int, d: int, kv_dtype: int, q_dtype: int, l
     floor = -(-max_len // 128) if uses_tensor_cores(kv_dtype, q_dtype, d) else 1  # <= 128 entries per split
     if units >= target or tiles < 2 * min_tiles:
         return max(1, floor)
-    return int(max(floor, min(math.ceil(target / max(units, 1)), tiles // min_tiles, 64)))
+    per = target // max(units, 1) if uses_tensor_cores(kv_dtype, q_dtype, d) else math.ceil(target / max(units, 1))
+    return int(max(floor, min(per, tiles // min_tiles, 64)))
 
 
 def kv_contiguous(k: torch.Tensor, v: torch.Tensor, block_size: int) -> L.KV:
