@@ -734,9 +734,9 @@ def run_c5(args, rank, world, local_rank):
     dominant = "select" if ph[0] >= ph[2] else "attend"
     ach = sel_min_gbs if dominant == "select" else att_min_gbs
     kname = "quest_decode_candidates (fused page scoring + per-chunk top-k)" if dominant == "select" else \
-        "sparse_attention (fp8 paged, f32 partial o + lse)"
+        "sparse_attention (fp8 paged on tensor cores, f32 partial o + lse)"
     traffic = profile_traffic("quest_select_c5.md" if dominant == "select" else "sparse_attention_c5.md")
-    n_mine = 4  # candidates, merge, attention, combine
+    n_mine = 4 + (dec.n_splits > 1)  # candidates, merge, attention (+ its split merge), combine
     return {
         "metric": METRIC,
         "value": round(b / (step_ms * 1e-3), 1),
@@ -761,7 +761,7 @@ def run_c5(args, rank, world, local_rank):
                               "attend": round(ph_max[2], 4), "exchange_partials+combine": round(ph_max[3], 4)},
         "bytes_per_step_per_gpu": {"meta": int(meta_bytes), "scores": int(score_bytes), "kv_selected": int(kv_bytes)},
         "selected_pages_per_kv_head_per_gpu": round(pages_loc / (b * hkv), 2),
-        "select_chunks_per_gpu": dec.chunks, "pages_per_select_cta": dec.chunk_pages,
+        "select_chunks_per_gpu": dec.chunks, "pages_per_select_cta": dec.chunk_pages, "attend_splits": dec.n_splits,
         "wall_ms_per_step": round(wall_s * 1e3 / args.steps, 4),
         "build_s": round(build_max, 1),
         "roofline": {"bound": "hbm", "kernel": kname, "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",

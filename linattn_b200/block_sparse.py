@@ -29,10 +29,18 @@ def tile_rows(elem_bytes: int, head_dim: int) -> int:
     return min(64, 16384 // (head_dim * elem_bytes))
 
 
-def uses_tensor_cores(kv_dtype: int, q_dtype: int, head_dim: int) -> bool:
-    """The C ABI's dispatch rule: 16-bit KV with q of the same dtype and D in {64, 128}
-    run the tensor-core kernel (persistent grid, 2048/D rows per warp tile)."""
+def uses_tensor_cores(kv_dtype: int, q_dtype: int, head_dim: int, page_size: Optional[int] = None) -> bool:
+    """The C ABI's dispatch rule: 16-bit KV with q of the same dtype and D in {64, 128},
+    or fp8 KV with a bf16 / f16 q, D = 128 and pages of >= 32 rows, run the tensor-core
+    kernel (persistent grid, 4 KiB K / V tiles per warp)."""
+    if kv_dtype == L.FP8E4M3:
+        return q_dtype in (L.F16, L.BF16) and head_dim == 128 and (page_size is None or page_size >= 32)
     return kv_dtype in (L.F16, L.BF16) and q_dtype == kv_dtype and head_dim in (64, 128)
+
+
+def mma_tile_rows(kv_dtype: int, head_dim: int) -> int:
+    """Rows per warp tile of the tensor-core kernel (4 KiB of K or V)."""
+    return 4096 // (head_dim * (1 if kv_dtype == L.FP8E4M3 else 2))
 
 
 def plan_splits(b: int, hq: int, tq: int, d: int, kv_dtype: int, q_dtype: int, list_heads: int, max_len: int,
@@ -46,8 +54,9 @@ def plan_splits(b: int, hq: int, tq: int, d: int, kv_dtype: int, q_dtype: int, l
     tiles."""
     sms = torch.cuda.get_device_properties(device).multi_processor_count
     g_total = hq // list_heads
-    if uses_tensor_cores(kv_dtype, q_dtype, d):
-        tr = 2048 // d
+    tc = uses_tensor_cores(kv_dtype, q_dtype, d, page_size)
+    if tc:
+        tr = mma_tile_rows(kv_dtype, d)
         units = b * list_heads * tq * ((g_total + 7) // 8)
         tiles = max(1, (max_len * page_size + tr - 1) // tr) if page_size <= tr else max_len * -(-page_size // tr)
         target, min_tiles = 8 * sms, 4
@@ -60,10 +69,10 @@ def plan_splits(b: int, hq: int, tq: int, d: int, kv_dtype: int, q_dtype: int, l
         units = b * list_heads * tq * ((g_total + g_t - 1) // g_t)
         tiles = max(1, (max_len * page_size + tr - 1) // tr)
         target, min_tiles = 4 * sms, 2
-    floor = -(-max_len // 128) if uses_tensor_cores(kv_dtype, q_dtype, d) else 1  # <= 128 entries per split
+    floor = -(-max_len // 128) if tc else 1  # <= 128 entries per split
     if units >= target or tiles < 2 * min_tiles:
         return max(1, floor)
-    per = target // max(units, 1) if uses_tensor_cores(kv_dtype, q_dtype, d) else math.ceil(target / max(units, 1))
+    per = target // max(units, 1) if tc else math.ceil(target / max(units, 1))
     return int(max(floor, min(per, tiles // min_tiles, 64)))
 
 
@@ -102,13 +111,16 @@ def sparse_attention(q: torch.Tensor, kv: L.KV, lists: L.Lists, *, causal: bool 
                      scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
                      lse_out: Optional[torch.Tensor] = None, n_splits: Optional[int] = None,
                      workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Attention of ``q (B,H_q,T_q,D)`` over the listed pages of ``kv``."""
+    """Attention of ``q (B,H_q,T_q,D)`` over the listed pages of ``kv``; ``out`` (f32,
+    f16 or bf16, default q's dtype) receives the result in its own dtype."""
     dev = L.require_cuda(q)
     b, hq, tq, d = q.shape
     if d != kv.head_dim:
         raise ValueError(f"head_dim mismatch: q has {d}, kv has {kv.head_dim}")
     if out is None:
         out = torch.empty_like(q, memory_format=torch.contiguous_format)
+    elif out.shape != q.shape:
+        raise ValueError(f"out must have q's shape {tuple(q.shape)}, got {tuple(out.shape)}")
     scale = (1.0 / math.sqrt(d)) if scale is None else float(scale)
     if n_splits is None:
         n_splits = plan_splits(b, hq, tq, d, kv.dtype, L.dtype_code(q), lists.n_heads, lists.max_len, kv.page_size,
@@ -117,9 +129,9 @@ def sparse_attention(q: torch.Tensor, kv: L.KV, lists: L.Lists, *, causal: bool 
     if workspace is None or workspace.numel() * workspace.element_size() < need:
         workspace = torch.empty((need + 3) // 4, dtype=torch.float32, device=dev)
     status = L.status_word(dev)
-    L.check(L.lib().linattn_sparse_attention(
+    L.check(L.lib().linattn_sparse_attention_out(
         q.data_ptr(), L.dtype_code(q), b, hq, tq, L.strides4(q), kv, lists, int(causal), offset, scale,
-        out.data_ptr(), L.strides4(out), L.ptr(lse_out), n_splits, workspace.data_ptr(), need,
+        out.data_ptr(), L.dtype_code(out), L.strides4(out), L.ptr(lse_out), n_splits, workspace.data_ptr(), need,
         status.data_ptr(), L.stream_of(q)))
     if L.strict():
         L.check_status(dev)

@@ -52,7 +52,7 @@ int sm_count();
 template <typename T, int D>
 static cudaError_t launch_mma_d(const AttnParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv, int box_rows,
                                 int* counter, int64_t n_items, cudaStream_t stream) {
-  using S = MmaShape<D>;
+  using S = MmaShape<D, sizeof(T)>;
   static bool configured[64] = {};
   const int dev = device_index();
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
@@ -73,10 +73,15 @@ static cudaError_t launch_mma_d(const AttnParams& p, const CUtensorMap& tmk, con
 template <typename T>
 static cudaError_t launch_mma(const AttnParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv, int box_rows, int D,
                               int* counter, int64_t n_items, cudaStream_t stream) {
-  switch (D) {
-    case 64: return launch_mma_d<T, 64>(p, tmk, tmv, box_rows, counter, n_items, stream);
-    case 128: return launch_mma_d<T, 128>(p, tmk, tmv, box_rows, counter, n_items, stream);
-    default: return cudaErrorInvalidValue;
+  if constexpr (sizeof(T) == 1) {
+    if (D != 128) return cudaErrorInvalidValue;
+    return launch_mma_d<T, 128>(p, tmk, tmv, box_rows, counter, n_items, stream);
+  } else {
+    switch (D) {
+      case 64: return launch_mma_d<T, 64>(p, tmk, tmv, box_rows, counter, n_items, stream);
+      case 128: return launch_mma_d<T, 128>(p, tmk, tmv, box_rows, counter, n_items, stream);
+      default: return cudaErrorInvalidValue;
+    }
   }
 }
 

@@ -110,9 +110,12 @@ int check_kv(const linattn_kv_t* kv) {
   return LINATTN_OK;
 }
 
-// ---- TMA tensor maps over the [rows, D] view of a 16-bit K or V pool --------------
-// 2-D map {D, rows} with 64 x box_rows boxes and 128-byte swizzle.
+// ---- TMA tensor maps over the [rows, D] view of a K or V pool ----------------------
+// 2-D map {D, rows} with 128-byte x box_rows boxes and 128-byte swizzle (16-bit: 64
+// elements per box row; fp8 codes as bytes: 128).
 bool kv_tensor_map(CUtensorMap* out, const void* base, int64_t rows, int d, int dtype, int box_rows) {
+  if (dtype == LINATTN_FP8E4M3)
+    return tensor_map_2d(out, base, CU_TENSOR_MAP_DATA_TYPE_UINT8, d, rows, d, 128, box_rows);
   return tensor_map_2d(out, base, dtype == LINATTN_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                         : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                        d, rows, static_cast<int64_t>(d) * 2, 64, box_rows);
@@ -254,14 +257,21 @@ int linattn_sparse_attention_out(const void* q, int32_t q_dtype, int64_t B, int6
   p.scale_log2 = scale * 1.4426950408889634f;
   p.out = out; p.lse_out = lse_out; p.n_splits = n_splits; p.status = status;
   const int64_t g_total = Hq / lists->n_heads;
-  // tensor-core path: 16-bit KV, q of the same dtype, D in {64, 128}, at most 128 list
-  // entries per split (the producer's per-item table), and K/V describable as TMA
-  // tensor maps over their [rows, D] views: strides multiples of D, pages either at
-  // least one 2048/D-row tile or a power of two >= 8 rows (box starts stay 1024-byte
-  // aligned for the 128-byte swizzle), rows below 2^31 (32-bit coordinates).
-  bool mma_path = (kv->dtype == LINATTN_BF16 || kv->dtype == LINATTN_F16) && q_dtype == kv->dtype &&
-                  (D == 64 || D == 128) && (lists->max_len + n_splits - 1) / n_splits <= 128;
-  const int tile_rows_mma = 2048 / D;
+  // tensor-core path: 16-bit KV with q of the same dtype and D in {64, 128}, or fp8 KV
+  // with a 16-bit q (exact in f16 after a power-of-two factor; an fp32 q stays on the
+  // fp32 CUDA-core path), D = 128 and pages of at least one 32-row tile (so that a tile
+  // has one pair of scales); at most 128 list entries per split (the producer's
+  // per-item table), and K/V describable as TMA tensor maps over their [rows, D] views:
+  // strides multiples of D, pages either at least one tile (4096 bytes of rows) or a
+  // power of two >= 8 rows (box starts stay 1024-byte aligned for the 128-byte
+  // swizzle), rows below 2^31 (32-bit coordinates).
+  const bool f8_mma = kv->dtype == LINATTN_FP8E4M3 && (q_dtype == LINATTN_BF16 || q_dtype == LINATTN_F16) &&
+                      D == 128 && kv->page_size >= 32;
+  bool mma_path = (((kv->dtype == LINATTN_BF16 || kv->dtype == LINATTN_F16) && q_dtype == kv->dtype &&
+                    (D == 64 || D == 128)) ||
+                   f8_mma) &&
+                  (lists->max_len + n_splits - 1) / n_splits <= 128;
+  const int tile_rows_mma = f8_mma ? 32 : 2048 / D;
   const int64_t P = kv->page_size;
   const int box_rows = static_cast<int>(P >= tile_rows_mma ? tile_rows_mma : P);
   mma_path = mma_path && (P >= tile_rows_mma || (P >= 8 && (P & (P - 1)) == 0)) && kv->stride_b % D == 0 &&
@@ -302,9 +312,9 @@ int linattn_sparse_attention_out(const void* q, int32_t q_dtype, int64_t B, int6
   if (mma_path) {
     e = cudaMemsetAsync(counter, 0, sizeof(int), st);
     if (e == cudaSuccess)
-      e = kv->dtype == LINATTN_BF16
-              ? launch_sparse_attention_mma_bf16(p, tmk, tmv, box_rows, D, counter, blocks, st)
-              : launch_sparse_attention_mma_f16(p, tmk, tmv, box_rows, D, counter, blocks, st);
+      e = kv->dtype == LINATTN_BF16  ? launch_sparse_attention_mma_bf16(p, tmk, tmv, box_rows, D, counter, blocks, st)
+          : kv->dtype == LINATTN_F16 ? launch_sparse_attention_mma_f16(p, tmk, tmv, box_rows, D, counter, blocks, st)
+                                     : launch_sparse_attention_mma_fp8(p, tmk, tmv, box_rows, D, counter, blocks, st);
   } else {
     const unsigned grid = static_cast<unsigned>(blocks);
     switch (kv->dtype) {

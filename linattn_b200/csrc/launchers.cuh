@@ -50,6 +50,8 @@ cudaError_t launch_sparse_attention_mma_bf16(const AttnParams& p, const CUtensor
                                             int box_rows, int D, int* counter, int64_t n_items, cudaStream_t stream);
 cudaError_t launch_sparse_attention_mma_f16(const AttnParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv,
                                            int box_rows, int D, int* counter, int64_t n_items, cudaStream_t stream);
+cudaError_t launch_sparse_attention_mma_fp8(const AttnParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv,
+                                           int box_rows, int D, int* counter, int64_t n_items, cudaStream_t stream);
 int sm_count();
 // Tensor-core indexer scores (indexer_mma.cu); false when the call is not eligible
 // (nothing launched), else *err holds the launch status.

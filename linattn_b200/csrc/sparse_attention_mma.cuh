@@ -1,4 +1,4 @@
-// Sparse (paged, block-list) attention on the tensor cores, for 16-bit KV.
+// Sparse (paged, block-list) attention on the tensor cores, for 16-bit and fp8 KV.
 //
 // Work: the (batch, list head, query, head chunk) units of linattn_sparse_attention,
 // each cut into `n_splits` equal slices of its page list ("items").  A persistent
@@ -24,11 +24,24 @@
 //   online softmax runs per head (column) in the log2 domain; P is split into two
 //   16-bit parts (hi + lo) so its rounding stays near fp32 precision, and the running
 //   sum uses the unrounded fp32 P.
+// fp8 (e4m3, one scale per (page, kv head)) KV, D = 128, pages of >= 32 rows: tiles of
+// 32 one-byte rows (one 128-byte box row each, same 4 KiB per K or V tile), so a tile
+// never spans two pages and its two scales are per-tile constants.  The codes are
+// converted in registers (cvt e4m3x2 -> f16x2, exact) straight from the swizzled
+// tile, without ldmatrix: K rows feed the A fragments with the channels permuted
+// identically in q (one 16-byte load per row and half), V^T fragments pair tokens per
+// channel with byte permutes, the output channels being permuted instead (undone in
+// the epilogue).  q runs as f16 times a per-head power of two; the K scale folds into
+// the score scale; P is a single f16 part and o is kept in units of the V scale of the
+// last page read (a change of page multiplies o by old / new scale together with the
+// softmax rescale).
 // Every wait is bounded (a give-up reports LINATTN_DEV_TIMEOUT and unwinds after
 // waiting, bounded, for the copies in flight).
 #pragma once
 
 #include <cuda.h>
+
+#include <type_traits>
 
 #include "sparse_attention.cuh"
 
@@ -77,21 +90,26 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t&
                : "r"(addr));
 }
 
-template <int D>
+// Geometry for head_dim D and EB-byte KV elements: every K or V tile is 4 KiB
+// (D=128: 16 rows of bf16/f16 or 32 rows of fp8; D=64 16-bit: 32 rows).
+template <int D, int EB = 2>
 struct MmaShape {
-  static constexpr int TRW = 2048 / D;            // tile rows (D=128: 16, D=64: 32)
-  static constexpr int NHALF = D / 64;            // 64-channel (128-byte) column blocks
+  static constexpr int ROWB = D * EB;             // bytes per K/V row
+  static constexpr int TRW = 4096 / ROWB;         // tile rows
+  static constexpr int NHALF = ROWB / 128;        // 128-byte column blocks
   static constexpr int HALF_BYTES = TRW * 128;    // one column block of a tile
   static constexpr int TILE_BYTES = NHALF * HALF_BYTES;  // one of K or V (4 KiB)
   static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
   static constexpr int STG = 3;                   // stages per warp
   static constexpr int NW = 8;                    // warps per CTA
   static constexpr int ITEM_MAX = 128;            // list entries per item (host guarantees)
+  static constexpr int ENT_BYTES = EB == 1 ? 16 : 8;  // table entry: int2, or int4 with the fp8 scales
   static constexpr size_t RING_BYTES = static_cast<size_t>(NW) * STG * STAGE_BYTES;
-  static constexpr size_t TABLE_BYTES = static_cast<size_t>(NW) * 2 * ITEM_MAX * 8;
+  static constexpr size_t TABLE_BYTES = static_cast<size_t>(NW) * 2 * ITEM_MAX * ENT_BYTES;
   static constexpr size_t SMEM_BYTES = 1024 + RING_BYTES + TABLE_BYTES;  // + alignment slack
   static constexpr int MT = TRW / 16;             // token 16-blocks per tile
   static constexpr int KS = D / 16;               // channel 16-blocks
+  static_assert(NHALF >= 1 && TRW <= 32, "tile geometry");
 };
 
 // An item as resolved by its warp (one of two slots per warp).
@@ -104,12 +122,14 @@ struct MmaStage {
   uint32_t loaded;  // rows written by this tile's boxes
   int32_t b, t, h0, n_heads, split;
   int32_t first, last;
+  float ks, vs;     // fp8: the tile's page scales (a tile never spans two pages)
 };
 
-// Swizzled byte offset of 16-byte chunk `chunk` (0 .. D/8-1) of tile row `row`.
-template <int D>
+// Swizzled byte offset of 16-byte chunk `chunk` (0 .. ROWB/16-1) of tile row `row`.
+template <int D, int EB = 2>
 __device__ __forceinline__ uint32_t swz(int row, int chunk) {
-  return static_cast<uint32_t>((chunk >> 3) * MmaShape<D>::HALF_BYTES + row * 128 + (((chunk & 7) ^ (row & 7)) << 4));
+  return static_cast<uint32_t>((chunk >> 3) * MmaShape<D, EB>::HALF_BYTES + row * 128 +
+                               (((chunk & 7) ^ (row & 7)) << 4));
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, int y, uint64_t* bar) {
@@ -126,13 +146,29 @@ __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
   return y;
 }
 
+// The two e4m3 codes in the low 16 bits of v (low byte first) -> f16x2 (low half
+// first), exactly: every e4m3 value is an f16.
+__device__ __forceinline__ uint32_t e4m3x2_f16x2(uint32_t v) {
+  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(v & 0xffffu), __NV_E4M3);
+  return static_cast<uint32_t>(h.x) | (static_cast<uint32_t>(h.y) << 16);
+}
+
+__device__ __forceinline__ uint32_t word_of(const uint4& u, int i) {
+  return i == 0 ? u.x : i == 1 ? u.y : i == 2 ? u.z : u.w;
+}
+
+// T: the KV element type (bf16 / f16, or fp8e4m3 for the fp8 mode described at the
+// top of the file); D: head_dim.
 template <typename T, int D>
-__global__ void __launch_bounds__(32 * MmaShape<D>::NW, 1)
+__global__ void __launch_bounds__(32 * MmaShape<D, sizeof(T)>::NW, 1)
     sparse_attention_mma_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmk,
                                 const __grid_constant__ CUtensorMap tmv, int box_rows, int* __restrict__ counter,
                                 int64_t n_items) {
-  using S = MmaShape<D>;
-  using M = MmaOp<T>;
+  constexpr bool F8 = sizeof(T) == 1;
+  static_assert(!F8 || D == 128, "fp8 tiles hold one 128-byte row per token");
+  using S = MmaShape<D, sizeof(T)>;
+  using M = MmaOp<std::conditional_t<F8, __half, T>>;
+  using Ent = std::conditional_t<F8, int4, int2>;  // {row position, pool row[, k scale, v scale]}
   constexpr int TRW = S::TRW, STG = S::STG;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   // 128-byte swizzled TMA destinations want 1024-byte alignment
@@ -143,7 +179,7 @@ __global__ void __launch_bounds__(32 * MmaShape<D>::NW, 1)
 
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   uint8_t* ring = smem + static_cast<size_t>(w) * STG * S::STAGE_BYTES;
-  int2* tables = reinterpret_cast<int2*>(smem + S::RING_BYTES) + w * 2 * S::ITEM_MAX;
+  Ent* tables = reinterpret_cast<Ent*>(smem + S::RING_BYTES) + w * 2 * S::ITEM_MAX;
   if (lane == 0) {
     for (int s = 0; s < STG; ++s) mbar_init(&full_bar[w][s], 1);
     mbar_fence_init();
@@ -215,12 +251,13 @@ __global__ void __launch_bounds__(32 * MmaShape<D>::NW, 1)
       }
       const int64_t len_b = p.kv.seq_lens ? static_cast<int64_t>(p.kv.seq_lens[b]) : p.kv.seq_len;
       const int64_t kvh = h0 / heads_per_kv;
-      int2* table = tables + k * S::ITEM_MAX;
+      Ent* table = tables + k * S::ITEM_MAX;
       for (int64_t e = lane; e < n; e += 32) {
         const int64_t id = p.lists.ids_dtype == LINATTN_I64
                                ? static_cast<const int64_t*>(p.lists.ids)[lbase + j0 + e]
                                : static_cast<int64_t>(static_cast<const int32_t*>(p.lists.ids)[lbase + j0 + e]);
         int rowpos = -1, y0 = 0;
+        float ksc = 0.f, vsc = 0.f;
         if (id >= 0 && id * P < len_b) {
           int64_t ph = id;
           if (p.kv.page_table) {
@@ -234,9 +271,17 @@ __global__ void __launch_bounds__(32 * MmaShape<D>::NW, 1)
             rowpos = static_cast<int>(id * P);
             // first row of this (page, kv head) in the [rows, D] view of the pool
             y0 = static_cast<int>((b * p.kv.stride_b + ph * p.kv.stride_page + kvh * p.kv.stride_head) / D);
+            if constexpr (F8) {
+              const int64_t si = ph * p.kv.scale_stride_page + kvh * p.kv.scale_stride_head;
+              ksc = p.kv.k_scale[si];
+              vsc = p.kv.v_scale[si];
+            }
           }
         }
-        table[e] = make_int2(rowpos, y0);
+        if constexpr (F8)
+          table[e] = make_int4(rowpos, y0, __float_as_int(ksc), __float_as_int(vsc));
+        else
+          table[e] = make_int2(rowpos, y0);
       }
       if (lane == 0) {
         MmaItem& d = items[w][k];
@@ -266,7 +311,7 @@ __global__ void __launch_bounds__(32 * MmaShape<D>::NW, 1)
     }
     if (pi >= res_count) return false;
     const MmaItem& it = items[w][pi & 1];
-    const int2* table = tables + (pi & 1) * S::ITEM_MAX;
+    const Ent* table = tables + (pi & 1) * S::ITEM_MAX;
     const int s = static_cast<int>(produced % STG);
     uint8_t* kdst = ring + static_cast<size_t>(s) * S::STAGE_BYTES;
     uint8_t* vdst = kdst + S::TILE_BYTES;
@@ -284,10 +329,15 @@ __global__ void __launch_bounds__(32 * MmaShape<D>::NW, 1)
     }
     bool valid = false;
     int y = 0;
+    float tks = 0.f, tvs = 0.f;  // fp8: row 0's page scales are the tile's (pages >= TRW rows)
     if (r < TRW && slot < PPT32 && e < it.n && rp < P32) {
-      const int2 ent = table[e];
+      const Ent ent = table[e];
       valid = ent.x >= 0 && ent.x + rp < it.limit;
       y = ent.y + rp;
+      if constexpr (F8) {
+        tks = __int_as_float(ent.z);
+        tvs = __int_as_float(ent.w);
+      }
     }
     const uint32_t mask = __ballot_sync(0xffffffffu, valid);
     const uint32_t box_mask = box_rows >= 32 ? 0xffffffffu : ((1u << box_rows) - 1u);
@@ -309,14 +359,16 @@ __global__ void __launch_bounds__(32 * MmaShape<D>::NW, 1)
       m.split = it.split;
       m.first = k == 0;
       m.last = k + 1 == it.n_tiles;
+      m.ks = tks;
+      m.vs = tvs;
       mbar_arrive_expect_tx(&full_bar[w][s], static_cast<uint32_t>(n_boxes) * S::NHALF * box_rows * 128u * 2u);
     }
     __syncwarp();
     if (r < TRW && r % box_rows == 0 && ((mask >> r) & box_mask)) {
 #pragma unroll
       for (int h = 0; h < S::NHALF; ++h) {
-        tma_load_2d(kdst + h * S::HALF_BYTES + r * 128, &tmk, h * 64, y, &full_bar[w][s]);
-        tma_load_2d(vdst + h * S::HALF_BYTES + r * 128, &tmv, h * 64, y, &full_bar[w][s]);
+        tma_load_2d(kdst + h * S::HALF_BYTES + r * 128, &tmk, h * (128 * D / S::ROWB), y, &full_bar[w][s]);
+        tma_load_2d(vdst + h * S::HALF_BYTES + r * 128, &tmv, h * (128 * D / S::ROWB), y, &full_bar[w][s]);
       }
     }
     ++ptile;
@@ -328,11 +380,15 @@ __global__ void __launch_bounds__(32 * MmaShape<D>::NW, 1)
   const int mi = lane >> 3, ri = lane & 7;
   const int hA = (lane & 3) * 2;   // this thread's two heads (accumulator columns)
   const int tk = lane >> 2;        // its token / channel row within a 16-row block
+  const int lq = lane & 3;         // its quad position (k pairs 2lq, 2lq+1, 2lq+8, 2lq+9)
   uint32_t qb[S::KS][2];
   float o[S::KS][4];               // O^T: channel blocks x (row tk, tk+8) x heads (hA, hA+1)
   float mA = -INFINITY, mB = -INFINITY, lA = 0.f, lB = 0.f;
   int32_t cb = 0, ct = 0, ch0 = 0, cnh = 0, csplit = 0;
   const float sl2 = p.scale_log2;
+  // fp8: the q power-of-two factors undone on heads hA, hA+1, and the V scale that o is
+  // currently expressed in (o_true = o * cvs)
+  float qfA = 1.f, qfB = 1.f, cvs = 1.f;
   const uint32_t ring_s = smem_u32(ring);
 
   int64_t consumed = 0;
@@ -360,18 +416,50 @@ __global__ void __launch_bounds__(32 * MmaShape<D>::NW, 1)
       ch0 = sd.h0;
       cnh = sd.n_heads;
       csplit = sd.split;
-      const T* qrow = static_cast<const T*>(p.q) + static_cast<int64_t>(cb) * p.qs[0] +
-                      static_cast<int64_t>(ch0 + tk) * p.qs[1] + static_cast<int64_t>(ct) * p.qs[2];
+      const int64_t qoff = static_cast<int64_t>(cb) * p.qs[0] + static_cast<int64_t>(ch0 + tk) * p.qs[1] +
+                           static_cast<int64_t>(ct) * p.qs[2];
+      if constexpr (F8) {
+        // Channels are permuted identically in q and K (the sum over them is unchanged):
+        // in k-block kk = 4h + j, this lane's k pairs (2lq, 2lq+1) and (2lq+8, 2lq+9) are
+        // channels 32lq + 16h + 4j + {0,1} and {2,3}, so a lane reads 16 contiguous K
+        // bytes per (row, h) and 32 contiguous q channels.  q is f16 times a power of two
+        // that puts the head's largest |q| in [2^14, 2^15) (exact for every element down
+        // to 2^-24 of it); the factor is undone in the score scale.
+        float v[32];
+        float amax = 0.f;
 #pragma unroll
-      for (int kk = 0; kk < S::KS; ++kk) {
-        float v[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int col = kk * 16 + hA + (e >> 1) * 8 + (e & 1);  // B fragment: k = channels, n = head tk
-          v[e] = tk < cnh ? to_float(qrow[col * p.qs[3]]) : 0.f;
+        for (int i = 0; i < 32; ++i) {
+          v[i] = tk < cnh ? load_any(p.q, qoff + static_cast<int64_t>(32 * lq + i) * p.qs[3], p.q_dtype) : 0.f;
+          amax = fmaxf(amax, fabsf(v[i]));
         }
-        qb[kk][0] = M::pack(v[0], v[1]);
-        qb[kk][1] = M::pack(v[2], v[3]);
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        const int ex = amax > 0.f ? static_cast<int>((__float_as_uint(amax) >> 23) & 0xffu) - 127 : 0;
+        const int e2 = max(-126, min(126, 14 - ex));  // both 2^e2 and 2^-e2 stay normal floats
+        const float up = __uint_as_float(static_cast<uint32_t>(127 + e2) << 23);
+        const float down = __uint_as_float(static_cast<uint32_t>(127 - e2) << 23);
+#pragma unroll
+        for (int kk = 0; kk < S::KS; ++kk) {
+          const int c0 = 16 * (kk >> 2) + 4 * (kk & 3);
+          qb[kk][0] = M::pack(v[c0] * up, v[c0 + 1] * up);
+          qb[kk][1] = M::pack(v[c0 + 2] * up, v[c0 + 3] * up);
+        }
+        qfA = __shfl_sync(0xffffffffu, down, hA * 4);
+        qfB = __shfl_sync(0xffffffffu, down, hA * 4 + 4);
+        cvs = 1.f;
+      } else {
+        const T* qrow = static_cast<const T*>(p.q) + qoff;
+#pragma unroll
+        for (int kk = 0; kk < S::KS; ++kk) {
+          float v[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int col = kk * 16 + hA + (e >> 1) * 8 + (e & 1);  // B fragment: k = channels, n = head tk
+            v[e] = tk < cnh ? to_float(qrow[col * p.qs[3]]) : 0.f;
+          }
+          qb[kk][0] = M::pack(v[0], v[1]);
+          qb[kk][1] = M::pack(v[2], v[3]);
+        }
       }
 #pragma unroll
       for (int n = 0; n < S::KS; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
@@ -380,15 +468,18 @@ __global__ void __launch_bounds__(32 * MmaShape<D>::NW, 1)
     }
     const uint32_t kst = ring_s + static_cast<uint32_t>(s) * S::STAGE_BYTES;
     const uint32_t vst = kst + S::TILE_BYTES;
+    const uint8_t* kptr = ring + static_cast<size_t>(s) * S::STAGE_BYTES;
+    const uint8_t* vptr = kptr + S::TILE_BYTES;
     // rows a box brought in but the tile does not use: zero their V so that P = 0
     // meets finite values in P V
     const uint32_t holes = sd.loaded & ~sd.rows;
     if (holes) {
       uint8_t* vrows = ring + static_cast<size_t>(s) * S::STAGE_BYTES + S::TILE_BYTES;
-      for (int i = lane; i < TRW * (D / 8); i += 32) {
-        const int row = i / (D / 8), chunk = i % (D / 8);
+      constexpr int CPR = S::ROWB / 16;  // 16-byte chunks per row
+      for (int i = lane; i < TRW * CPR; i += 32) {
+        const int row = i / CPR, chunk = i % CPR;
         if ((holes >> row) & 1u)
-          *reinterpret_cast<uint4*>(vrows + swz<D>(row, chunk)) = make_uint4(0u, 0u, 0u, 0u);
+          *reinterpret_cast<uint4*>(vrows + swz<D, sizeof(T)>(row, chunk)) = make_uint4(0u, 0u, 0u, 0u);
       }
       __syncwarp();
     }
@@ -399,13 +490,33 @@ __global__ void __launch_bounds__(32 * MmaShape<D>::NW, 1)
       sc[mt][0] = sc[mt][1] = sc[mt][2] = sc[mt][3] = 0.f;
       sc2[mt][0] = sc2[mt][1] = sc2[mt][2] = sc2[mt][3] = 0.f;
     }
-#pragma unroll
-    for (int kk = 0; kk < S::KS; ++kk) {
+    if constexpr (F8) {
 #pragma unroll
       for (int mt = 0; mt < S::MT; ++mt) {
-        uint32_t a[4];
-        ldsm_x4(kst + swz<D>(mt * 16 + (mi & 1) * 8 + ri, kk * 2 + (mi >> 1)), a[0], a[1], a[2], a[3]);
-        M::mma((kk & 1) ? sc2[mt] : sc[mt], a, qb[kk][0], qb[kk][1]);
+        // rows tk and tk+8 of the block, chunks 2lq and 2lq+1 (lanes of a quarter warp
+        // hit 8 distinct chunks under the swizzle)
+        uint4 k0[2], k1[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          k0[h] = *reinterpret_cast<const uint4*>(kptr + swz<D, 1>(mt * 16 + tk, 2 * lq + h));
+          k1[h] = *reinterpret_cast<const uint4*>(kptr + swz<D, 1>(mt * 16 + tk + 8, 2 * lq + h));
+        }
+#pragma unroll
+        for (int kk = 0; kk < S::KS; ++kk) {
+          const uint32_t w0 = word_of(k0[kk >> 2], kk & 3), w1 = word_of(k1[kk >> 2], kk & 3);
+          const uint32_t a[4] = {e4m3x2_f16x2(w0), e4m3x2_f16x2(w1), e4m3x2_f16x2(w0 >> 16), e4m3x2_f16x2(w1 >> 16)};
+          M::mma((kk & 1) ? sc2[mt] : sc[mt], a, qb[kk][0], qb[kk][1]);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int kk = 0; kk < S::KS; ++kk) {
+#pragma unroll
+        for (int mt = 0; mt < S::MT; ++mt) {
+          uint32_t a[4];
+          ldsm_x4(kst + swz<D>(mt * 16 + (mi & 1) * 8 + ri, kk * 2 + (mi >> 1)), a[0], a[1], a[2], a[3]);
+          M::mma((kk & 1) ? sc2[mt] : sc[mt], a, qb[kk][0], qb[kk][1]);
+        }
       }
     }
 #pragma unroll
@@ -413,15 +524,16 @@ __global__ void __launch_bounds__(32 * MmaShape<D>::NW, 1)
 #pragma unroll
       for (int i = 0; i < 4; ++i) sc[mt][i] += sc2[mt][i];
     // ---- online softmax per head (column); unread rows -> -inf
+    const float fA = F8 ? sl2 * sd.ks * qfA : sl2, fB = F8 ? sl2 * sd.ks * qfB : sl2;
     float tA = -INFINITY, tB = -INFINITY;
 #pragma unroll
     for (int mt = 0; mt < S::MT; ++mt) {
       const bool v0 = (sd.rows >> (mt * 16 + tk)) & 1u;
       const bool v1 = (sd.rows >> (mt * 16 + tk + 8)) & 1u;
-      sc[mt][0] = v0 ? sc[mt][0] * sl2 : -INFINITY;
-      sc[mt][1] = v0 ? sc[mt][1] * sl2 : -INFINITY;
-      sc[mt][2] = v1 ? sc[mt][2] * sl2 : -INFINITY;
-      sc[mt][3] = v1 ? sc[mt][3] * sl2 : -INFINITY;
+      sc[mt][0] = v0 ? sc[mt][0] * fA : -INFINITY;
+      sc[mt][1] = v0 ? sc[mt][1] * fB : -INFINITY;
+      sc[mt][2] = v1 ? sc[mt][2] * fA : -INFINITY;
+      sc[mt][3] = v1 ? sc[mt][3] * fB : -INFINITY;
       tA = fmaxf(tA, fmaxf(sc[mt][0], sc[mt][2]));
       tB = fmaxf(tB, fmaxf(sc[mt][1], sc[mt][3]));
     }
@@ -431,8 +543,8 @@ __global__ void __launch_bounds__(32 * MmaShape<D>::NW, 1)
       tB = fmaxf(tB, __shfl_xor_sync(0xffffffffu, tB, off));
     }
     const float nA = fmaxf(mA, tA), nB = fmaxf(mB, tB);
-    const float aA = nA == -INFINITY ? 1.f : exp2f(mA - nA);
-    const float aB = nB == -INFINITY ? 1.f : exp2f(mB - nB);
+    float aA = nA == -INFINITY ? 1.f : exp2f(mA - nA);
+    float aB = nB == -INFINITY ? 1.f : exp2f(mB - nB);
     float sA = 0.f, sB = 0.f;
 #pragma unroll
     for (int mt = 0; mt < S::MT; ++mt) {
@@ -452,6 +564,19 @@ __global__ void __launch_bounds__(32 * MmaShape<D>::NW, 1)
     lB = lB * aB + sB;
     mA = nA;
     mB = nB;
+    // fp8: P V is taken on the codes of a page whose V scale is sd.vs; o moves to that
+    // scale (a tile whose scale is 0 adds nothing and leaves o's scale alone)
+    bool pv = true;
+    if constexpr (F8) {
+      if (sd.vs != 0.f) {
+        const float r = cvs / sd.vs;
+        aA *= r;
+        aB *= r;
+        cvs = sd.vs;
+      } else {
+        pv = false;
+      }
+    }
 #pragma unroll
     for (int n = 0; n < S::KS; ++n) {
       o[n][0] *= aA;
@@ -459,22 +584,50 @@ __global__ void __launch_bounds__(32 * MmaShape<D>::NW, 1)
       o[n][2] *= aA;
       o[n][3] *= aB;
     }
-    // ---- O^T += V^T P^T  (P = hi + lo in the 16-bit type)
+    if constexpr (F8) {
+      // ---- O^T += V^T P^T with one f16 P.  Output rows are permuted: in channel block
+      // dm, accumulator rows tk / tk+8 are channels 16tk + 2dm / 16tk + 2dm + 1, so a
+      // lane reads one 16-byte chunk (channels 16tk .. 16tk+15) of each of its four
+      // token rows (2lq, 2lq+1, 2lq+8, 2lq+9) and pairs tokens per channel with byte
+      // permutes.
+      if (pv) {
 #pragma unroll
-    for (int mt = 0; mt < S::MT; ++mt) {
-      const uint32_t h0 = M::pack(sc[mt][0], sc[mt][1]);  // tokens tk,   heads hA, hA+1
-      const uint32_t h1 = M::pack(sc[mt][2], sc[mt][3]);  // tokens tk+8
-      const float2 r0 = M::unpack(h0), r1 = M::unpack(h1);
-      const uint32_t l0 = M::pack(sc[mt][0] - r0.x, sc[mt][1] - r0.y);
-      const uint32_t l1 = M::pack(sc[mt][2] - r1.x, sc[mt][3] - r1.y);
-      const uint32_t bh0 = movmatrix_t(h0), bh1 = movmatrix_t(h1);
-      const uint32_t bl0 = movmatrix_t(l0), bl1 = movmatrix_t(l1);
+        for (int mt = 0; mt < S::MT; ++mt) {
+          const uint32_t bh0 = movmatrix_t(M::pack(sc[mt][0], sc[mt][1]));
+          const uint32_t bh1 = movmatrix_t(M::pack(sc[mt][2], sc[mt][3]));
+          uint4 vw[4];
 #pragma unroll
-      for (int dm = 0; dm < S::KS; ++dm) {
-        uint32_t a[4];
-        ldsm_x4_t(vst + swz<D>(mt * 16 + (mi >> 1) * 8 + ri, dm * 2 + (mi & 1)), a[0], a[1], a[2], a[3]);
-        M::mma(o[dm], a, bh0, bh1);
-        M::mma(o[dm], a, bl0, bl1);
+          for (int i = 0; i < 4; ++i)
+            vw[i] = *reinterpret_cast<const uint4*>(vptr + swz<D, 1>(mt * 16 + 2 * lq + (i & 1) + (i >> 1) * 8, tk));
+#pragma unroll
+          for (int dm = 0; dm < S::KS; ++dm) {
+            const uint32_t sel = (dm & 1) ? 0x7362u : 0x5140u;
+            const uint32_t p01 = __byte_perm(word_of(vw[0], dm >> 1), word_of(vw[1], dm >> 1), sel);
+            const uint32_t p89 = __byte_perm(word_of(vw[2], dm >> 1), word_of(vw[3], dm >> 1), sel);
+            const uint32_t a[4] = {e4m3x2_f16x2(p01), e4m3x2_f16x2(p01 >> 16), e4m3x2_f16x2(p89),
+                                   e4m3x2_f16x2(p89 >> 16)};
+            M::mma(o[dm], a, bh0, bh1);
+          }
+        }
+      }
+    } else {
+      // ---- O^T += V^T P^T  (P = hi + lo in the 16-bit type)
+#pragma unroll
+      for (int mt = 0; mt < S::MT; ++mt) {
+        const uint32_t h0 = M::pack(sc[mt][0], sc[mt][1]);  // tokens tk,   heads hA, hA+1
+        const uint32_t h1 = M::pack(sc[mt][2], sc[mt][3]);  // tokens tk+8
+        const float2 r0 = M::unpack(h0), r1 = M::unpack(h1);
+        const uint32_t l0 = M::pack(sc[mt][0] - r0.x, sc[mt][1] - r0.y);
+        const uint32_t l1 = M::pack(sc[mt][2] - r1.x, sc[mt][3] - r1.y);
+        const uint32_t bh0 = movmatrix_t(h0), bh1 = movmatrix_t(h1);
+        const uint32_t bl0 = movmatrix_t(l0), bl1 = movmatrix_t(l1);
+#pragma unroll
+        for (int dm = 0; dm < S::KS; ++dm) {
+          uint32_t a[4];
+          ldsm_x4_t(vst + swz<D>(mt * 16 + (mi >> 1) * 8 + ri, dm * 2 + (mi & 1)), a[0], a[1], a[2], a[3]);
+          M::mma(o[dm], a, bh0, bh1);
+          M::mma(o[dm], a, bl0, bl1);
+        }
       }
     }
     __syncwarp();
@@ -482,7 +635,7 @@ __global__ void __launch_bounds__(32 * MmaShape<D>::NW, 1)
     ++consumed;
     // ---- item finished: write (o, lse) for its heads
     if (sd.last) {
-      const float iA = lA > 0.f ? 1.f / lA : 0.f, iB = lB > 0.f ? 1.f / lB : 0.f;
+      const float iA = lA > 0.f ? cvs / lA : 0.f, iB = lB > 0.f ? cvs / lB : 0.f;
       const float lseA = lA > 0.f ? (mA + log2f(lA)) * 0.69314718055994531f : -INFINITY;
       const float lseB = lB > 0.f ? (mB + log2f(lB)) * 0.69314718055994531f : -INFINITY;
 #pragma unroll
@@ -492,22 +645,47 @@ __global__ void __launch_bounds__(32 * MmaShape<D>::NW, 1)
         const int64_t h = ch0 + g;
         const int64_t row = (static_cast<int64_t>(cb) * p.Hq + h) * p.Tq + ct;
         const float inv = j ? iB : iA;
+        // (channel, value) pairs of this lane for head g: 16-bit KV rows dm*16+tk and
+        // dm*16+tk+8; fp8 channels 16tk .. 16tk+15 in order
+        float* wo = nullptr;
         if (p.n_splits == 1) {
           const int64_t ob = static_cast<int64_t>(cb) * p.os[0] + h * p.os[1] + static_cast<int64_t>(ct) * p.os[2];
+          if (F8 && p.out_dtype == LINATTN_F32 && p.os[3] == 1) wo = static_cast<float*>(p.out) + ob;
+          if (!wo) {
 #pragma unroll
-          for (int dm = 0; dm < S::KS; ++dm) {
-            store_any(p.out, ob + (dm * 16 + tk) * p.os[3], p.out_dtype, o[dm][j] * inv);
-            store_any(p.out, ob + (dm * 16 + tk + 8) * p.os[3], p.out_dtype, o[dm][2 + j] * inv);
+            for (int dm = 0; dm < S::KS; ++dm) {
+              const int c0 = F8 ? 16 * tk + 2 * dm : dm * 16 + tk, c1 = F8 ? c0 + 1 : c0 + 8;
+              store_any(p.out, ob + c0 * p.os[3], p.out_dtype, o[dm][j] * inv);
+              store_any(p.out, ob + c1 * p.os[3], p.out_dtype, o[dm][2 + j] * inv);
+            }
           }
           if (p.lse_out && tk == 0) p.lse_out[row] = j ? lseB : lseA;
         } else {
-          float* wo = p.ws_o + (static_cast<int64_t>(csplit) * rows_total + row) * D;
-#pragma unroll
-          for (int dm = 0; dm < S::KS; ++dm) {
-            wo[dm * 16 + tk] = o[dm][j] * inv;
-            wo[dm * 16 + tk + 8] = o[dm][2 + j] * inv;
-          }
+          wo = p.ws_o + (static_cast<int64_t>(csplit) * rows_total + row) * D;
           if (tk == 0) p.ws_lse[static_cast<int64_t>(csplit) * rows_total + row] = j ? lseB : lseA;
+        }
+        if (wo) {
+          if constexpr (F8) {
+            float* w16 = wo + 16 * tk;
+            if ((reinterpret_cast<uintptr_t>(w16) & 15u) == 0) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                reinterpret_cast<float4*>(w16)[i] = make_float4(o[2 * i][j] * inv, o[2 * i][2 + j] * inv,
+                                                                o[2 * i + 1][j] * inv, o[2 * i + 1][2 + j] * inv);
+            } else {
+#pragma unroll
+              for (int dm = 0; dm < S::KS; ++dm) {
+                w16[2 * dm] = o[dm][j] * inv;
+                w16[2 * dm + 1] = o[dm][2 + j] * inv;
+              }
+            }
+          } else {
+#pragma unroll
+            for (int dm = 0; dm < S::KS; ++dm) {
+              wo[dm * 16 + tk] = o[dm][j] * inv;
+              wo[dm * 16 + tk + 8] = o[dm][2 + j] * inv;
+            }
+          }
         }
       }
     }

@@ -30,6 +30,7 @@ import torch
 import torch.distributed as dist
 
 from linattn_b200 import _lib as L
+from linattn_b200.block_sparse import plan_splits
 from linattn_b200.paged import PagedKVCache, plan_select_chunks
 
 __all__ = ["ShardedQuestDecoder", "exchange_candidates", "exchange_packed", "exchange_partials", "shard_page_ranges"]
@@ -132,7 +133,10 @@ class ShardedQuestDecoder:
         self.out = torch.empty(b, n_heads, 1, d, dtype=q_dtype, device=dev)
         self._lists = L.Lists(self.union_ids.data_ptr(), L.I32, hkv, *self.union_ids.stride()[:3], self.max_union,
                               self.union_count.data_ptr(), *self.union_count.stride())
-        self._ws_bytes = L.lib().linattn_sparse_attention_workspace(b, n_heads, 1, d, 1)
+        kv_code = L.FP8E4M3 if cache.fp8 else L.dtype_code(cache.k_pool)
+        q_code = {torch.float32: L.F32, torch.float16: L.F16, torch.bfloat16: L.BF16}[q_dtype]
+        self.n_splits = plan_splits(b, n_heads, 1, d, kv_code, q_code, hkv, self.max_union, cache.page_size, dev)
+        self._ws_bytes = L.lib().linattn_sparse_attention_workspace(b, n_heads, 1, d, self.n_splits)
         self._ws = torch.empty(max(1, (self._ws_bytes + 3) // 4), dtype=torch.float32, device=dev)
 
     def candidates(self, q: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
@@ -175,7 +179,8 @@ class ShardedQuestDecoder:
         L.check(L.lib().linattn_sparse_attention_out(
             q.data_ptr(), L.dtype_code(q), q.shape[0], self.n_heads, 1, L.strides4(q), self.cache.kv_desc(),
             self._lists, 0, 0, self.scale, self.o_part.data_ptr(), L.F32, L.strides4(self.o_part),
-            self.lse_part.data_ptr(), 1, self._ws.data_ptr(), self._ws_bytes, status.data_ptr(), L.stream_of(q)))
+            self.lse_part.data_ptr(), self.n_splits, self._ws.data_ptr(), self._ws_bytes, status.data_ptr(),
+            L.stream_of(q)))
         return self.o_part, self.lse_part
 
     def combine(self, all_o: torch.Tensor, all_lse: torch.Tensor) -> torch.Tensor:
