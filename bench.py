@@ -170,7 +170,7 @@ def build_c2(device, seed: int, n_q: int, batch: int = C2["B"]):
     return cache, qs
 
 
-def build_c5(device, rank: int, world: int, n_q: int, batch: int = C5["B"]):
+def build_c5(device, rank: int, world: int, n_q: int, batch: int = C5["B"], t: int = C5["T"]):
     """This rank's shard of the config-5 cache (pages [lo, hi) of every sequence, fp8
     e4m3 with per-(page, kv head) scales, seeded N(0,1) values before quantisation,
     0.5% needle pages at global positions shared by all ranks, a random page table over
@@ -179,7 +179,7 @@ def build_c5(device, rank: int, world: int, n_q: int, batch: int = C5["B"]):
     from linattn_b200.sharded import shard_page_ranges
 
     c = C5
-    b, hq, hkv, d, t, p = batch, c["Hq"], c["Hkv"], c["D"], c["T"], c["P"]
+    b, hq, hkv, d, p = batch, c["Hq"], c["Hkv"], c["D"], c["P"]
     n_glob = t // p
     lo, hi = shard_page_ranges(n_glob, world, rank)
     n_loc = hi - lo
@@ -634,10 +634,10 @@ def run_c5(args, rank, world, local_rank):
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     c = C5
-    b, hq, hkv, d, t, p = args.batch or c["B"], c["Hq"], c["Hkv"], c["D"], c["T"], c["P"]
+    b, hq, hkv, d, t, p = args.batch or c["B"], c["Hq"], c["Hkv"], c["D"], args.seq_len or c["T"], c["P"]
     n_q = args.warmup + args.steps
     t_build = time.perf_counter()
-    cache, qs, (lo, hi) = build_c5(device, rank, world, n_q, b)
+    cache, qs, (lo, hi) = build_c5(device, rank, world, n_q, b, t)
     torch.cuda.synchronize(device)
     build_s = time.perf_counter() - t_build
     n_glob = t // p
@@ -751,7 +751,8 @@ def run_c5(args, rank, world, local_rank):
         "dtype": "fp8e4m3 KV, bf16 q, f32 accumulate",
         "data": "synthetic (seeded N(0,1) values quantised to e4m3 per (page, kv head), 0.5% needle pages at "
                 "global positions shared by every rank, random page table per shard)",
-        "config": {"workload": "sharded_decode_c5" if b == C5["B"] else f"sharded_decode_c5_b{b}", "batch": b,
+        "config": {"workload": "sharded_decode_c5" if (b, t) == (C5["B"], C5["T"]) else f"sharded_decode_c5_b{b}_t{t}",
+                   "batch": b,
                    "seq_len": t, "page_size": p, "n_heads": hq, "n_kv_heads": hkv, "head_dim": d,
                    "budget_pages": c["topk"], "pages_per_gpu_per_seq": n_loc,
                    "parallelism": f"sequence-sharded x{world} (KV pages split, NCCL all-gathers)",
@@ -827,7 +828,7 @@ def main(argv=None) -> int:
                     help="c2: paged Quest decode (the headline); c3: DSA indexer + token attention; c4: block-sparse "
                          "prefill; c5: million-token sequence-sharded decode")
     ap.add_argument("--seq-len", type=int, default=None,
-                    help="c3 / c4 only: a shorter sequence (profiling captures)")
+                    help="c3 / c4 / c5 only: a shorter sequence (profiling captures)")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the config-3 / config-4 legs reported beside the config-2 line")
     args = ap.parse_args(argv)

@@ -47,11 +47,14 @@ def plan_splits(b: int, hq: int, tq: int, d: int, kv_dtype: int, q_dtype: int, l
                 page_size: int, device: torch.device) -> int:
     """Split-KV factor for a call.
 
-    Tensor-core path: at most one work item per resident warp (148 SMs x 8 warps), so
-    that every item starts in the first wave (a second partial wave of items costs more
-    than the longer items save), each item keeping at least 4 tiles (and at most 128
-    list entries).  CUDA-core path: about 4 CTAs per SM, each split keeping at least 2
-    tiles."""
+    Tensor-core path (a persistent grid of 148 SMs x 8 warps, one item at a time per
+    warp): the items run in waves of 1184, so the split count S minimises
+    ceil(units * S / 1184) * (tiles / S + 3), the waves times an item's time in tiles
+    (an item start costs about 3 tiles: the list resolution and the first copies),
+    with at least 4 tiles and at most 128 list entries per item.  Configuration 2
+    (128 units) takes S = 9 (one wave), configuration 5 (512 units) S = 9 (3.9 waves;
+    S = 4 leaves the last of its 1.7 waves mostly idle).  CUDA-core path: about 4 CTAs
+    per SM, each split keeping at least 2 tiles."""
     sms = torch.cuda.get_device_properties(device).multi_processor_count
     g_total = hq // list_heads
     tc = uses_tensor_cores(kv_dtype, q_dtype, d, page_size)
@@ -59,21 +62,26 @@ def plan_splits(b: int, hq: int, tq: int, d: int, kv_dtype: int, q_dtype: int, l
         tr = mma_tile_rows(kv_dtype, d)
         units = b * list_heads * tq * ((g_total + 7) // 8)
         tiles = max(1, (max_len * page_size + tr - 1) // tr) if page_size <= tr else max_len * -(-page_size // tr)
-        target, min_tiles = 8 * sms, 4
-    else:
-        eb = {L.F32: 4, L.F16: 2, L.BF16: 2, L.FP8E4M3: 1}[kv_dtype]
-        tr = tile_rows(eb, d)
-        g_t = 1
-        while g_t < g_total and g_t < 8:
-            g_t <<= 1
-        units = b * list_heads * tq * ((g_total + g_t - 1) // g_t)
-        tiles = max(1, (max_len * page_size + tr - 1) // tr)
-        target, min_tiles = 4 * sms, 2
-    floor = -(-max_len // 128) if tc else 1  # <= 128 entries per split
+        floor = max(1, -(-max_len // 128))  # <= 128 entries per split
+        cap = max(floor, min(64, tiles // 4))
+        warps = 8 * sms
+        best, best_cost = floor, None
+        for s in range(floor, cap + 1):
+            cost = math.ceil(units * s / warps) * (tiles / s + 3.0)
+            if best_cost is None or cost < best_cost - 1e-12:
+                best, best_cost = s, cost
+        return int(best)
+    eb = {L.F32: 4, L.F16: 2, L.BF16: 2, L.FP8E4M3: 1}[kv_dtype]
+    tr = tile_rows(eb, d)
+    g_t = 1
+    while g_t < g_total and g_t < 8:
+        g_t <<= 1
+    units = b * list_heads * tq * ((g_total + g_t - 1) // g_t)
+    tiles = max(1, (max_len * page_size + tr - 1) // tr)
+    target, min_tiles = 4 * sms, 2
     if units >= target or tiles < 2 * min_tiles:
-        return max(1, floor)
-    per = target // max(units, 1) if tc else math.ceil(target / max(units, 1))
-    return int(max(floor, min(per, tiles // min_tiles, 64)))
+        return 1
+    return int(max(1, min(math.ceil(target / max(units, 1)), tiles // min_tiles, 64)))
 
 
 def kv_contiguous(k: torch.Tensor, v: torch.Tensor, block_size: int) -> L.KV:

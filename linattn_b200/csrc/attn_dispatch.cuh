@@ -49,7 +49,7 @@ static cudaError_t launch_dg(const AttnParams& p, int D, int G, unsigned grid, c
 
 int sm_count();
 
-template <typename T, int D>
+template <typename T, int D, int NQT = 1>
 static cudaError_t launch_mma_d(const AttnParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv, int box_rows,
                                 int* counter, int64_t n_items, cudaStream_t stream) {
   using S = MmaShape<D, sizeof(T)>;
@@ -57,7 +57,7 @@ static cudaError_t launch_mma_d(const AttnParams& p, const CUtensorMap& tmk, con
   const int dev = device_index();
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(sparse_attention_mma_kernel<T, D>,
+    cudaError_t e = cudaFuncSetAttribute(sparse_attention_mma_kernel<T, D, NQT>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(S::SMEM_BYTES));
     if (e != cudaSuccess) return e;
@@ -65,8 +65,8 @@ static cudaError_t launch_mma_d(const AttnParams& p, const CUtensorMap& tmk, con
   }
   const int64_t want = (n_items + S::NW - 1) / S::NW;
   const int grid = static_cast<int>(lmax(1, lmin(sm_count(), want)));
-  sparse_attention_mma_kernel<T, D><<<grid, 32 * S::NW, S::SMEM_BYTES, stream>>>(p, tmk, tmv, box_rows, counter,
-                                                                             n_items);
+  sparse_attention_mma_kernel<T, D, NQT><<<grid, 32 * S::NW, S::SMEM_BYTES, stream>>>(p, tmk, tmv, box_rows,
+                                                                                  counter, n_items);
   return cudaGetLastError();
 }
 
@@ -74,8 +74,11 @@ template <typename T>
 static cudaError_t launch_mma(const AttnParams& p, const CUtensorMap& tmk, const CUtensorMap& tmv, int box_rows, int D,
                               int* counter, int64_t n_items, cudaStream_t stream) {
   if constexpr (sizeof(T) == 1) {
+    // q as e4m3 terms: two hold a bf16 q exactly, an f16 q takes three
     if (D != 128) return cudaErrorInvalidValue;
-    return launch_mma_d<T, 128>(p, tmk, tmv, box_rows, counter, n_items, stream);
+    if (p.q_dtype == LINATTN_BF16) return launch_mma_d<T, 128, 2>(p, tmk, tmv, box_rows, counter, n_items, stream);
+    if (p.q_dtype == LINATTN_F16) return launch_mma_d<T, 128, 3>(p, tmk, tmv, box_rows, counter, n_items, stream);
+    return cudaErrorInvalidValue;
   } else {
     switch (D) {
       case 64: return launch_mma_d<T, 64>(p, tmk, tmv, box_rows, counter, n_items, stream);

@@ -9,9 +9,10 @@
 
 namespace linattn {
 
-// One CTA per output row, one thread per channel: every thread reads all parts'
-// lse (broadcast loads), so the max, the weights and the o loads (coalesced across
-// threads, independent across parts) need no dependent round trips.
+// One CTA per output row, one thread per channel.  Every warp fetches the parts' lse
+// 32 at a time (lane s holds part s of the group, one round trip for all of them),
+// reduces the max and broadcasts each part's weight by shuffle, so the o loads
+// (coalesced across threads, independent across parts) follow in a second round trip.
 __global__ void __launch_bounds__(256) lse_combine_kernel(const float* __restrict__ o_parts,
                                                           const float* __restrict__ lse_parts, int64_t S,
                                                           int64_t rows, int64_t D, int64_t o_ps, int64_t l_ps,
@@ -19,18 +20,26 @@ __global__ void __launch_bounds__(256) lse_combine_kernel(const float* __restric
                                                           int64_t H, int64_t Tq, int64_t os0, int64_t os1,
                                                           int64_t os2, int64_t os3, float* lse_out) {
   const int64_t row = blockIdx.x;
-  const int c = threadIdx.x;
+  const int c = threadIdx.x, lane = c & 31;
   float L = -INFINITY;
-  for (int64_t s = 0; s < S; ++s) L = fmaxf(L, lse_parts[s * l_ps + row]);
+  for (int64_t s0 = 0; s0 < S; s0 += 32)
+    L = fmaxf(L, s0 + lane < S ? lse_parts[(s0 + lane) * l_ps + row] : -INFINITY);
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) L = fmaxf(L, __shfl_xor_sync(0xffffffffu, L, off));
   float acc = 0.f, W = 0.f;
   if (L != -INFINITY) {
+    for (int64_t s0 = 0; s0 < S; s0 += 32) {
+      const float ls = s0 + lane < S ? lse_parts[(s0 + lane) * l_ps + row] : -INFINITY;
+      const float wl = ls == -INFINITY ? 0.f : __expf(ls - L);
+      const int n = static_cast<int>(lmin(32, S - s0));
+      const float* op = o_parts + s0 * o_ps + row * D + c;
 #pragma unroll 8
-    for (int64_t s = 0; s < S; ++s) {
-      const float ls = lse_parts[s * l_ps + row];
-      if (ls == -INFINITY) continue;  // empty part: its o is not read (it may be unwritten)
-      const float w = __expf(ls - L);
-      W += w;
-      if (c < D) acc = fmaf(w, o_parts[s * o_ps + row * D + c], acc);
+      for (int j = 0; j < n; ++j) {
+        const float w = __shfl_sync(0xffffffffu, wl, j);
+        W += w;
+        // an empty part (lse = -inf) is not read: its o may be unwritten
+        if (w != 0.f && c < D) acc = fmaf(w, op[j * o_ps], acc);
+      }
     }
   }
   if (c < D) {

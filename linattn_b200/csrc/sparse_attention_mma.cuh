@@ -26,15 +26,19 @@
 //   sum uses the unrounded fp32 P.
 // fp8 (e4m3, one scale per (page, kv head)) KV, D = 128, pages of >= 32 rows: tiles of
 // 32 one-byte rows (one 128-byte box row each, same 4 KiB per K or V tile), so a tile
-// never spans two pages and its two scales are per-tile constants.  The codes are
-// converted in registers (cvt e4m3x2 -> f16x2, exact) straight from the swizzled
-// tile, without ldmatrix: K rows feed the A fragments with the channels permuted
-// identically in q (one 16-byte load per row and half), V^T fragments pair tokens per
-// channel with byte permutes, the output channels being permuted instead (undone in
-// the epilogue).  q runs as f16 times a per-head power of two; the K scale folds into
-// the score scale; P is a single f16 part and o is kept in units of the V scale of the
-// last page read (a change of page multiplies o by old / new scale together with the
-// softmax rescale).
+// never spans two pages and its two scales are per-tile constants.  Fragments come
+// straight from the swizzled tile (no ldmatrix):
+// * S^T = K Q^T runs on the e4m3 tensor-core mma (m16n8k32) with the K codes as they
+//   are: the channels are permuted identically in q and K so that a lane's A fragments
+//   are two 16-byte loads per row.  q (times a per-head power of two putting its
+//   largest |q| in [2^7, 2^8)) is split into NQT e4m3 terms q1 + q2/16 (+ q3/256),
+//   each an mma of its own: two terms hold a bf16 q exactly, three an f16 q (every
+//   element down to 2^-13 of the largest).  The K scale folds into the score scale.
+// * O^T += V^T P^T runs in f16: V^T fragments pair two tokens per channel with byte
+//   permutes and convert them exactly (cvt e4m3x2 -> f16x2); the output channels are
+//   permuted instead (undone in the epilogue).  P is a single f16 part carrying the
+//   ratio of the page's V scale to the one o is kept in (o is rebased when that ratio
+//   leaves [2^-4, 2^4]).
 // Every wait is bounded (a give-up reports LINATTN_DEV_TIMEOUT and unwinds after
 // waiting, bounded, for the copies in flight).
 #pragma once
@@ -117,12 +121,14 @@ struct MmaItem {
   int32_t b, t, h0, n_heads, split, n, n_tiles, limit;
 };
 
-struct MmaStage {
-  uint32_t rows;    // valid-row mask of the tile
-  uint32_t loaded;  // rows written by this tile's boxes
-  int32_t b, t, h0, n_heads, split;
-  int32_t first, last;
-  float ks, vs;     // fp8: the tile's page scales (a tile never spans two pages)
+// A filled ring stage as the consumer sees it (two 16-byte words).
+struct __align__(16) MmaStage {
+  uint32_t rows;   // valid-row mask of the tile
+  uint32_t holes;  // rows a box wrote that the tile does not use
+  int32_t b, t;
+  uint32_t h0nh;   // first head | n_heads << 24 | first tile << 30 | last tile << 31
+  int32_t split;
+  float ks, vs;    // fp8: the tile's page scales (a tile never spans two pages)
 };
 
 // Swizzled byte offset of 16-byte chunk `chunk` (0 .. ROWB/16-1) of tile row `row`.
@@ -153,19 +159,31 @@ __device__ __forceinline__ uint32_t e4m3x2_f16x2(uint32_t v) {
   return static_cast<uint32_t>(h.x) | (static_cast<uint32_t>(h.y) << 16);
 }
 
+// d += a * b over k = 32 e4m3 codes per row (fp32 accumulation).
+__device__ __forceinline__ void mma_e4m3(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 __device__ __forceinline__ uint32_t word_of(const uint4& u, int i) {
   return i == 0 ? u.x : i == 1 ? u.y : i == 2 ? u.z : u.w;
 }
 
 // T: the KV element type (bf16 / f16, or fp8e4m3 for the fp8 mode described at the
-// top of the file); D: head_dim.
-template <typename T, int D>
+// top of the file); D: head_dim; NQT: fp8 mode, e4m3 terms of q (2 for a bf16 q, 3 for
+// an f16 q).
+template <typename T, int D, int NQT = 1>
 __global__ void __launch_bounds__(32 * MmaShape<D, sizeof(T)>::NW, 1)
     sparse_attention_mma_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmk,
                                 const __grid_constant__ CUtensorMap tmv, int box_rows, int* __restrict__ counter,
                                 int64_t n_items) {
   constexpr bool F8 = sizeof(T) == 1;
   static_assert(!F8 || D == 128, "fp8 tiles hold one 128-byte row per token");
+  static_assert(!F8 || NQT == 2 || NQT == 3, "fp8 mode splits q into 2 or 3 terms");
   using S = MmaShape<D, sizeof(T)>;
   using M = MmaOp<std::conditional_t<F8, __half, T>>;
   using Ent = std::conditional_t<F8, int4, int2>;  // {row position, pool row[, k scale, v scale]}
@@ -183,6 +201,8 @@ __global__ void __launch_bounds__(32 * MmaShape<D, sizeof(T)>::NW, 1)
   if (lane == 0) {
     for (int s = 0; s < STG; ++s) mbar_init(&full_bar[w][s], 1);
     mbar_fence_init();
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmk)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmv)) : "memory");
   }
   // rows never copied must hold finite values
   for (int i = lane; i < STG * S::STAGE_BYTES / 16; i += 32)
@@ -300,19 +320,32 @@ __global__ void __launch_bounds__(32 * MmaShape<D, sizeof(T)>::NW, 1)
     }
   };
 
-  // ---- production: item pi of the resolved sequence, tile ptile of it.  Returns
+  // ---- production: item pi of the resolved sequence, tile ptile of it, into ring
+  // stage ps.  The item's fields live in registers from its first tile on.  Returns
   // false when the next tile needs an item that is not resolved yet (or none is left).
-  int pi = 0, ptile = 0;
-  int64_t produced = 0;
+  int pi = 0, ptile = 0, ps = 0, in_flight = 0;
+  int p_ntiles = -1, p_n = 0, p_limit = 0, p_b = 0, p_t = 0, p_split = 0;
+  uint32_t p_h0nh = 0u;
   auto issue = [&]() -> bool {
-    while (pi < res_count && ptile >= items[w][pi & 1].n_tiles) {
+    while (true) {
+      if (pi >= res_count) return false;
+      if (p_ntiles < 0) {
+        const MmaItem& it = items[w][pi & 1];
+        p_ntiles = it.n_tiles;
+        p_n = it.n;
+        p_limit = it.limit;
+        p_b = it.b;
+        p_t = it.t;
+        p_split = it.split;
+        p_h0nh = static_cast<uint32_t>(it.h0) | (static_cast<uint32_t>(it.n_heads) << 24);
+      }
+      if (ptile < p_ntiles) break;
       ++pi;  // the slot of item pi-1 is free again
       ptile = 0;
+      p_ntiles = -1;
     }
-    if (pi >= res_count) return false;
-    const MmaItem& it = items[w][pi & 1];
     const Ent* table = tables + (pi & 1) * S::ITEM_MAX;
-    const int s = static_cast<int>(produced % STG);
+    const int s = ps;
     uint8_t* kdst = ring + static_cast<size_t>(s) * S::STAGE_BYTES;
     uint8_t* vdst = kdst + S::TILE_BYTES;
     const int k = ptile;
@@ -330,9 +363,9 @@ __global__ void __launch_bounds__(32 * MmaShape<D, sizeof(T)>::NW, 1)
     bool valid = false;
     int y = 0;
     float tks = 0.f, tvs = 0.f;  // fp8: row 0's page scales are the tile's (pages >= TRW rows)
-    if (r < TRW && slot < PPT32 && e < it.n && rp < P32) {
+    if (r < TRW && slot < PPT32 && e < p_n && rp < P32) {
       const Ent ent = table[e];
-      valid = ent.x >= 0 && ent.x + rp < it.limit;
+      valid = ent.x >= 0 && ent.x + rp < p_limit;
       y = ent.y + rp;
       if constexpr (F8) {
         tks = __int_as_float(ent.z);
@@ -349,22 +382,20 @@ __global__ void __launch_bounds__(32 * MmaShape<D, sizeof(T)>::NW, 1)
         loaded |= box_mask << r0b;
       }
     if (lane == 0) {
-      MmaStage& m = st[w][s];
+      MmaStage m;
       m.rows = mask;
-      m.loaded = loaded;
-      m.b = it.b;
-      m.t = it.t;
-      m.h0 = it.h0;
-      m.n_heads = it.n_heads;
-      m.split = it.split;
-      m.first = k == 0;
-      m.last = k + 1 == it.n_tiles;
+      m.holes = loaded & ~mask;
+      m.b = p_b;
+      m.t = p_t;
+      m.h0nh = p_h0nh | (k == 0 ? 1u << 30 : 0u) | (k + 1 == p_ntiles ? 1u << 31 : 0u);
+      m.split = p_split;
       m.ks = tks;
       m.vs = tvs;
+      st[w][s] = m;
       mbar_arrive_expect_tx(&full_bar[w][s], static_cast<uint32_t>(n_boxes) * S::NHALF * box_rows * 128u * 2u);
     }
     __syncwarp();
-    if (r < TRW && r % box_rows == 0 && ((mask >> r) & box_mask)) {
+    if (r < TRW && (r & (box_rows - 1)) == 0 && ((mask >> r) & box_mask)) {
 #pragma unroll
       for (int h = 0; h < S::NHALF; ++h) {
         tma_load_2d(kdst + h * S::HALF_BYTES + r * 128, &tmk, h * (128 * D / S::ROWB), y, &full_bar[w][s]);
@@ -372,7 +403,8 @@ __global__ void __launch_bounds__(32 * MmaShape<D, sizeof(T)>::NW, 1)
       }
     }
     ++ptile;
-    ++produced;
+    ps = ps + 1 == STG ? 0 : ps + 1;
+    ++in_flight;
     return true;
   };
 
@@ -381,50 +413,51 @@ __global__ void __launch_bounds__(32 * MmaShape<D, sizeof(T)>::NW, 1)
   const int hA = (lane & 3) * 2;   // this thread's two heads (accumulator columns)
   const int tk = lane >> 2;        // its token / channel row within a 16-row block
   const int lq = lane & 3;         // its quad position (k pairs 2lq, 2lq+1, 2lq+8, 2lq+9)
-  uint32_t qb[S::KS][2];
+  // q B fragments: 16-bit KV, per channel block; fp8, term t / k-step j at [4t + j]
+  uint32_t qb[F8 ? 4 * NQT : S::KS][2];
   float o[S::KS][4];               // O^T: channel blocks x (row tk, tk+8) x heads (hA, hA+1)
   float mA = -INFINITY, mB = -INFINITY, lA = 0.f, lB = 0.f;
   int32_t cb = 0, ct = 0, ch0 = 0, cnh = 0, csplit = 0;
   const float sl2 = p.scale_log2;
   // fp8: the q power-of-two factors undone on heads hA, hA+1, and the V scale that o is
-  // currently expressed in (o_true = o * cvs)
+  // currently expressed in (o_true = o * cvs; 0 until a page with a nonzero V scale)
   float qfA = 1.f, qfB = 1.f, cvs = 1.f;
   const uint32_t ring_s = smem_u32(ring);
 
-  int64_t consumed = 0;
+  int cs = 0;          // ring stage consumed next
+  uint32_t cph = 0u;   // its fill phase parity
   bool abort = false;
   while (true) {
     // keep one item resolved ahead of production (the loads overlap the copies in
     // flight), then top the ring up; both have exactly one call site
     if (!exhausted && res_count <= pi + 1) resolve();
-    while (produced - consumed < STG && issue()) {
+    while (in_flight < STG && issue()) {
     }
-    if (consumed == produced) {
+    if (in_flight == 0) {
       if (exhausted && pi >= res_count) break;
       continue;
     }
-    const int s = static_cast<int>(consumed % STG);
-    if (!mbar_wait_bounded(&full_bar[w][s], static_cast<uint32_t>((consumed / STG) & 1))) {
+    const int s = cs;
+    if (!mbar_wait_bounded(&full_bar[w][s], cph)) {
       report(p.status, LINATTN_DEV_TIMEOUT);
       abort = true;
       break;
     }
     const MmaStage sd = st[w][s];
-    if (sd.first) {
+    const bool first = (sd.h0nh >> 30) & 1u, last = sd.h0nh >> 31;
+    if (first) {
       cb = sd.b;
       ct = sd.t;
-      ch0 = sd.h0;
-      cnh = sd.n_heads;
+      ch0 = static_cast<int32_t>(sd.h0nh & 0xffffffu);
+      cnh = static_cast<int32_t>((sd.h0nh >> 24) & 0x3fu);
       csplit = sd.split;
       const int64_t qoff = static_cast<int64_t>(cb) * p.qs[0] + static_cast<int64_t>(ch0 + tk) * p.qs[1] +
                            static_cast<int64_t>(ct) * p.qs[2];
       if constexpr (F8) {
         // Channels are permuted identically in q and K (the sum over them is unchanged):
-        // in k-block kk = 4h + j, this lane's k pairs (2lq, 2lq+1) and (2lq+8, 2lq+9) are
-        // channels 32lq + 16h + 4j + {0,1} and {2,3}, so a lane reads 16 contiguous K
-        // bytes per (row, h) and 32 contiguous q channels.  q is f16 times a power of two
-        // that puts the head's largest |q| in [2^14, 2^15) (exact for every element down
-        // to 2^-24 of it); the factor is undone in the score scale.
+        // in k-step j, this lane's A / B k-quads (4lq .. 4lq+3) and (16+4lq .. 16+4lq+3)
+        // are channels 32lq + 8j + {0..3} and {4..7}, so a lane reads 32 contiguous K
+        // bytes per row (chunks 2lq, 2lq+1) and 32 contiguous q channels.
         float v[32];
         float amax = 0.f;
 #pragma unroll
@@ -435,18 +468,33 @@ __global__ void __launch_bounds__(32 * MmaShape<D, sizeof(T)>::NW, 1)
         amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
         amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
         const int ex = amax > 0.f ? static_cast<int>((__float_as_uint(amax) >> 23) & 0xffu) - 127 : 0;
-        const int e2 = max(-126, min(126, 14 - ex));  // both 2^e2 and 2^-e2 stay normal floats
+        const int e2 = max(-126, min(126, 7 - ex));  // both 2^e2 and 2^-e2 stay normal floats
         const float up = __uint_as_float(static_cast<uint32_t>(127 + e2) << 23);
         const float down = __uint_as_float(static_cast<uint32_t>(127 - e2) << 23);
 #pragma unroll
-        for (int kk = 0; kk < S::KS; ++kk) {
-          const int c0 = 16 * (kk >> 2) + 4 * (kk & 3);
-          qb[kk][0] = M::pack(v[c0] * up, v[c0 + 1] * up);
-          qb[kk][1] = M::pack(v[c0 + 2] * up, v[c0 + 3] * up);
+        for (int i = 0; i < 32; ++i) v[i] *= up;
+        // term t: e4m3 (round to nearest even) of 16^t times what the earlier terms left
+#pragma unroll
+        for (int t = 0; t < NQT; ++t) {
+#pragma unroll
+          for (int r = 0; r < 8; ++r) {
+            uint32_t word = 0u;
+#pragma unroll
+            for (int hp = 0; hp < 2; ++hp) {
+              const int i = 4 * r + 2 * hp;
+              const uint32_t c2 = __nv_cvt_float2_to_fp8x2(make_float2(v[i], v[i + 1]), __NV_SATFINITE, __NV_E4M3);
+              word |= c2 << (16 * hp);
+              const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(c2), __NV_E4M3);
+              const float2 back = __half22float2(*reinterpret_cast<const __half2*>(&h));
+              v[i] = (v[i] - back.x) * 16.f;
+              v[i + 1] = (v[i + 1] - back.y) * 16.f;
+            }
+            qb[4 * t + (r >> 1)][r & 1] = word;
+          }
         }
         qfA = __shfl_sync(0xffffffffu, down, hA * 4);
         qfB = __shfl_sync(0xffffffffu, down, hA * 4 + 4);
-        cvs = 1.f;
+        cvs = 0.f;
       } else {
         const T* qrow = static_cast<const T*>(p.q) + qoff;
 #pragma unroll
@@ -472,7 +520,7 @@ __global__ void __launch_bounds__(32 * MmaShape<D, sizeof(T)>::NW, 1)
     const uint8_t* vptr = kptr + S::TILE_BYTES;
     // rows a box brought in but the tile does not use: zero their V so that P = 0
     // meets finite values in P V
-    const uint32_t holes = sd.loaded & ~sd.rows;
+    const uint32_t holes = sd.holes;
     if (holes) {
       uint8_t* vrows = ring + static_cast<size_t>(s) * S::STAGE_BYTES + S::TILE_BYTES;
       constexpr int CPR = S::ROWB / 16;  // 16-byte chunks per row
@@ -501,11 +549,22 @@ __global__ void __launch_bounds__(32 * MmaShape<D, sizeof(T)>::NW, 1)
           k0[h] = *reinterpret_cast<const uint4*>(kptr + swz<D, 1>(mt * 16 + tk, 2 * lq + h));
           k1[h] = *reinterpret_cast<const uint4*>(kptr + swz<D, 1>(mt * 16 + tk + 8, 2 * lq + h));
         }
+        float acc[NQT][4];
 #pragma unroll
-        for (int kk = 0; kk < S::KS; ++kk) {
-          const uint32_t w0 = word_of(k0[kk >> 2], kk & 3), w1 = word_of(k1[kk >> 2], kk & 3);
-          const uint32_t a[4] = {e4m3x2_f16x2(w0), e4m3x2_f16x2(w1), e4m3x2_f16x2(w0 >> 16), e4m3x2_f16x2(w1 >> 16)};
-          M::mma((kk & 1) ? sc2[mt] : sc[mt], a, qb[kk][0], qb[kk][1]);
+        for (int t = 0; t < NQT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int h = j >> 1, wd = 2 * (j & 1);
+          const uint32_t a0 = word_of(k0[h], wd), a1 = word_of(k1[h], wd);
+          const uint32_t a2 = word_of(k0[h], wd + 1), a3 = word_of(k1[h], wd + 1);
+#pragma unroll
+          for (int t = 0; t < NQT; ++t) mma_e4m3(acc[t], a0, a1, a2, a3, qb[4 * t + j][0], qb[4 * t + j][1]);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float x = fmaf(acc[1][i], 0.0625f, acc[0][i]);
+          if constexpr (NQT == 3) x = fmaf(acc[2][i], 0.00390625f, x);
+          sc[mt][i] = x;
         }
       }
     } else {
@@ -523,9 +582,14 @@ __global__ void __launch_bounds__(32 * MmaShape<D, sizeof(T)>::NW, 1)
     for (int mt = 0; mt < S::MT; ++mt)
 #pragma unroll
       for (int i = 0; i < 4; ++i) sc[mt][i] += sc2[mt][i];
-    // ---- online softmax per head (column); unread rows -> -inf
+    // ---- online softmax per head (column); unread rows -> -inf.  The running maxima
+    // mA / mB are lazy: they move only when a score exceeds them by more than 8 (log2
+    // domain; one warp vote per tile), so P <= 2^8, and o is rescaled only then.  The
+    // row sums lA / lB are per-lane partials (this lane's rows), summed over the lanes
+    // of a head column once, at the end of the item.  fp8: P also carries vs / cvs
+    // (exp2 offset lr) and the row sums take it back out (ir).
     const float fA = F8 ? sl2 * sd.ks * qfA : sl2, fB = F8 ? sl2 * sd.ks * qfB : sl2;
-    float tA = -INFINITY, tB = -INFINITY;
+    bool over = false;
 #pragma unroll
     for (int mt = 0; mt < S::MT; ++mt) {
       const bool v0 = (sd.rows >> (mt * 16 + tk)) & 1u;
@@ -534,56 +598,72 @@ __global__ void __launch_bounds__(32 * MmaShape<D, sizeof(T)>::NW, 1)
       sc[mt][1] = v0 ? sc[mt][1] * fB : -INFINITY;
       sc[mt][2] = v1 ? sc[mt][2] * fA : -INFINITY;
       sc[mt][3] = v1 ? sc[mt][3] * fB : -INFINITY;
-      tA = fmaxf(tA, fmaxf(sc[mt][0], sc[mt][2]));
-      tB = fmaxf(tB, fmaxf(sc[mt][1], sc[mt][3]));
+      over |= fmaxf(sc[mt][0], sc[mt][2]) > mA + 8.f || fmaxf(sc[mt][1], sc[mt][3]) > mB + 8.f;
     }
+    float lr = 0.f, ir = 1.f;
+    bool pv = true, rebase = false;
+    if constexpr (F8) {
+      if (sd.vs == 0.f) {
+        pv = false;  // the page's V is 0: it adds nothing to o
+      } else if (cvs == 0.f) {
+        cvs = sd.vs;  // first page with a V scale: o is still 0
+      } else if (sd.vs != cvs) {
+        lr = log2f(sd.vs / cvs);
+        if (fabsf(lr) > 4.f) {
+          rebase = true;
+          lr = 0.f;
+        } else {
+          ir = cvs / sd.vs;
+        }
+      }
+    }
+    if (rebase || __any_sync(0xffffffffu, over)) {
+      float tA = -INFINITY, tB = -INFINITY;
 #pragma unroll
-    for (int off = 4; off <= 16; off <<= 1) {
-      tA = fmaxf(tA, __shfl_xor_sync(0xffffffffu, tA, off));
-      tB = fmaxf(tB, __shfl_xor_sync(0xffffffffu, tB, off));
+      for (int mt = 0; mt < S::MT; ++mt) {
+        tA = fmaxf(tA, fmaxf(sc[mt][0], sc[mt][2]));
+        tB = fmaxf(tB, fmaxf(sc[mt][1], sc[mt][3]));
+      }
+#pragma unroll
+      for (int off = 4; off <= 16; off <<= 1) {
+        tA = fmaxf(tA, __shfl_xor_sync(0xffffffffu, tA, off));
+        tB = fmaxf(tB, __shfl_xor_sync(0xffffffffu, tB, off));
+      }
+      const float nA = fmaxf(mA, tA), nB = fmaxf(mB, tB);
+      const float aA = nA == -INFINITY ? 1.f : exp2f(mA - nA);
+      const float aB = nB == -INFINITY ? 1.f : exp2f(mB - nB);
+      lA *= aA;
+      lB *= aB;
+      mA = nA;
+      mB = nB;
+      float oA = aA, oB = aB;
+      if (rebase) {
+        const float r = cvs / sd.vs;
+        oA *= r;
+        oB *= r;
+        cvs = sd.vs;
+      }
+#pragma unroll
+      for (int n = 0; n < S::KS; ++n) {
+        o[n][0] *= oA;
+        o[n][1] *= oB;
+        o[n][2] *= oA;
+        o[n][3] *= oB;
+      }
     }
-    const float nA = fmaxf(mA, tA), nB = fmaxf(mB, tB);
-    float aA = nA == -INFINITY ? 1.f : exp2f(mA - nA);
-    float aB = nB == -INFINITY ? 1.f : exp2f(mB - nB);
+    const float oA_ = mA - lr, oB_ = mB - lr;  // exp2 offsets
     float sA = 0.f, sB = 0.f;
 #pragma unroll
     for (int mt = 0; mt < S::MT; ++mt) {
-      sc[mt][0] = nA == -INFINITY ? 0.f : exp2f(sc[mt][0] - nA);
-      sc[mt][2] = nA == -INFINITY ? 0.f : exp2f(sc[mt][2] - nA);
-      sc[mt][1] = nB == -INFINITY ? 0.f : exp2f(sc[mt][1] - nB);
-      sc[mt][3] = nB == -INFINITY ? 0.f : exp2f(sc[mt][3] - nB);
+      sc[mt][0] = mA == -INFINITY ? 0.f : exp2f(sc[mt][0] - oA_);
+      sc[mt][2] = mA == -INFINITY ? 0.f : exp2f(sc[mt][2] - oA_);
+      sc[mt][1] = mB == -INFINITY ? 0.f : exp2f(sc[mt][1] - oB_);
+      sc[mt][3] = mB == -INFINITY ? 0.f : exp2f(sc[mt][3] - oB_);
       sA += sc[mt][0] + sc[mt][2];
       sB += sc[mt][1] + sc[mt][3];
     }
-#pragma unroll
-    for (int off = 4; off <= 16; off <<= 1) {
-      sA += __shfl_xor_sync(0xffffffffu, sA, off);
-      sB += __shfl_xor_sync(0xffffffffu, sB, off);
-    }
-    lA = lA * aA + sA;
-    lB = lB * aB + sB;
-    mA = nA;
-    mB = nB;
-    // fp8: P V is taken on the codes of a page whose V scale is sd.vs; o moves to that
-    // scale (a tile whose scale is 0 adds nothing and leaves o's scale alone)
-    bool pv = true;
-    if constexpr (F8) {
-      if (sd.vs != 0.f) {
-        const float r = cvs / sd.vs;
-        aA *= r;
-        aB *= r;
-        cvs = sd.vs;
-      } else {
-        pv = false;
-      }
-    }
-#pragma unroll
-    for (int n = 0; n < S::KS; ++n) {
-      o[n][0] *= aA;
-      o[n][1] *= aB;
-      o[n][2] *= aA;
-      o[n][3] *= aB;
-    }
+    lA = fmaf(sA, ir, lA);
+    lB = fmaf(sB, ir, lB);
     if constexpr (F8) {
       // ---- O^T += V^T P^T with one f16 P.  Output rows are permuted: in channel block
       // dm, accumulator rows tk / tk+8 are channels 16tk + 2dm / 16tk + 2dm + 1, so a
@@ -632,9 +712,16 @@ __global__ void __launch_bounds__(32 * MmaShape<D, sizeof(T)>::NW, 1)
     }
     __syncwarp();
     if (holes) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // before the next TMA fill
-    ++consumed;
+    --in_flight;
+    cs = cs + 1 == STG ? 0 : cs + 1;
+    if (cs == 0) cph ^= 1u;
     // ---- item finished: write (o, lse) for its heads
-    if (sd.last) {
+    if (last) {
+#pragma unroll
+      for (int off = 4; off <= 16; off <<= 1) {
+        lA += __shfl_xor_sync(0xffffffffu, lA, off);
+        lB += __shfl_xor_sync(0xffffffffu, lB, off);
+      }
       const float iA = lA > 0.f ? cvs / lA : 0.f, iB = lB > 0.f ? cvs / lB : 0.f;
       const float lseA = lA > 0.f ? (mA + log2f(lA)) * 0.69314718055994531f : -INFINITY;
       const float lseB = lB > 0.f ? (mB + log2f(lB)) * 0.69314718055994531f : -INFINITY;
@@ -691,8 +778,11 @@ __global__ void __launch_bounds__(32 * MmaShape<D, sizeof(T)>::NW, 1)
     }
   }
   if (abort) {
-    for (int64_t c2 = consumed; c2 < produced; ++c2)
-      (void)mbar_wait_bounded(&full_bar[w][c2 % STG], static_cast<uint32_t>((c2 / STG) & 1));
+    for (; in_flight > 0; --in_flight) {
+      (void)mbar_wait_bounded(&full_bar[w][cs], cph);
+      cs = cs + 1 == STG ? 0 : cs + 1;
+      if (cs == 0) cph ^= 1u;
+    }
   }
 }
 
