@@ -159,38 +159,75 @@ __device__ __forceinline__ void select_head_reg(const DecodeSelectParams& p, con
     }
   }
   uint32_t lo = __reduce_min_sync(0xffffffffu, kmin), hi = __reduce_max_sync(0xffffffffu, kmax);
-  // largest t with count(key >= t) >= kb: the kb-th largest key
+  // count(key >= t) over the warp, with 8 independent partial sums (short add chains)
+  auto count_ge = [&](uint32_t t) -> uint32_t {
+    uint32_t cc[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int j = 0; j < ITEMS; ++j) cc[j & 7] += key[j] >= t ? 1u : 0u;
+    return __reduce_add_sync(0xffffffffu, ((cc[0] + cc[1]) + (cc[2] + cc[3])) + ((cc[4] + cc[5]) + (cc[6] + cc[7])));
+  };
+  // largest t with count(key >= t) >= kb (the kb-th largest key), or any t with
+  // count(key >= t) == kb exactly (then the keys >= t are the selection, ties included)
+  bool exact = false;
   while (lo < hi && kb > 0) {
     const uint32_t mid = lo + ((hi - lo + 1u) >> 1);
-    uint32_t c = 0u;
-#pragma unroll
-    for (int j = 0; j < ITEMS; ++j) c += key[j] >= mid ? 1u : 0u;
-    if (__reduce_add_sync(0xffffffffu, c) >= static_cast<uint32_t>(kb)) lo = mid;
+    const uint32_t c = count_ge(mid);
+    if (c == static_cast<uint32_t>(kb)) {
+      lo = mid;
+      exact = true;
+      break;
+    }
+    if (c > static_cast<uint32_t>(kb)) lo = mid;
     else hi = mid - 1u;
   }
   const uint32_t kstar = lo;
-  uint32_t cgt = 0u;
-#pragma unroll
-  for (int j = 0; j < ITEMS; ++j) cgt += key[j] > kstar ? 1u : 0u;
-  const uint32_t remaining = static_cast<uint32_t>(kb) - __reduce_add_sync(0xffffffffu, cgt);
-  // gather: every key > kstar, and the first `remaining` keys == kstar (index order)
-  uint32_t n_sel = 0u, eq_taken = 0u;
+  uint32_t n_ge = 0u, n_eq = 0u;
 #pragma unroll
   for (int j = 0; j < ITEMS; ++j) {
-    const int64_t i = j * 32 + lane;
-    const bool gt = kb > 0 && key[j] > kstar;
-    const bool eq = kb > 0 && i < nb && key[j] == kstar;
-    const unsigned eq_mask = __ballot_sync(0xffffffffu, eq);
-    const uint32_t eq_rank = eq_taken + __popc(eq_mask & ((1u << lane) - 1u));
-    const bool take = gt || (eq && eq_rank < remaining);
-    const unsigned take_mask = __ballot_sync(0xffffffffu, take);
-    if (take) {
-      const uint32_t pos = n_sel + __popc(take_mask & ((1u << lane) - 1u));
-      sel_idx[pos] = static_cast<uint32_t>(i);
-      sel_key[pos] = key[j];
+    n_ge += key[j] >= kstar ? 1u : 0u;
+    n_eq += key[j] == kstar ? 1u : 0u;
+  }
+  const uint32_t tot_ge = __reduce_add_sync(0xffffffffu, n_ge);
+  if (kb > 0 && (exact || tot_ge == static_cast<uint32_t>(kb))) {
+    // every key >= kstar is selected: place each lane's keys after an exclusive scan of
+    // the lanes' counts (the order inside sel does not matter, the ranking sorts)
+    uint32_t pos = n_ge;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, pos, o);
+      if (lane >= o) pos += y;
     }
-    n_sel += __popc(take_mask);
-    eq_taken += __popc(eq_mask);
+    pos -= n_ge;
+#pragma unroll
+    for (int j = 0; j < ITEMS; ++j) {
+      if (key[j] >= kstar && j * 32 + lane < nb) {
+        sel_idx[pos] = static_cast<uint32_t>(j * 32 + lane);
+        sel_key[pos] = key[j];
+        ++pos;
+      }
+    }
+  } else {
+    // ties at the k-th key: every key > kstar and the first `remaining` keys == kstar
+    // (index order)
+    const uint32_t remaining = static_cast<uint32_t>(kb) - (tot_ge - __reduce_add_sync(0xffffffffu, n_eq));
+    uint32_t n_sel = 0u, eq_taken = 0u;
+#pragma unroll
+    for (int j = 0; j < ITEMS; ++j) {
+      const int64_t i = j * 32 + lane;
+      const bool gt = kb > 0 && key[j] > kstar;
+      const bool eq = kb > 0 && i < nb && key[j] == kstar;
+      const unsigned eq_mask = __ballot_sync(0xffffffffu, eq);
+      const uint32_t eq_rank = eq_taken + __popc(eq_mask & ((1u << lane) - 1u));
+      const bool take = gt || (eq && eq_rank < remaining);
+      const unsigned take_mask = __ballot_sync(0xffffffffu, take);
+      if (take) {
+        const uint32_t pos = n_sel + __popc(take_mask & ((1u << lane) - 1u));
+        sel_idx[pos] = static_cast<uint32_t>(i);
+        sel_key[pos] = key[j];
+      }
+      n_sel += __popc(take_mask);
+      eq_taken += __popc(eq_mask);
+    }
   }
   __syncwarp();
   write_selection(p, srow, sel_idx, sel_key, kb, bitmap, pg0, b, h, lane);
