@@ -138,6 +138,25 @@ int linattn_paged_page_bounds(const linattn_kv_t* kv, int64_t B, const int32_t* 
                               const linattn_meta_t* meta, int32_t* status, void* stream);
 
 /*
+ * Decode / chunk append in one launch: rows t of k_new, v_new (B, H_kv, T_new, D),
+ * any strides with unit stride on D, go to position start_pos[b] + t of sequence b
+ * (logical page pos / page_size through kv->page_table, row pos % page_size), converted
+ * to the pool's dtype, and the Quest bounds of every page the new rows touch become
+ * min / max over the page's earlier rows (taken from the stored bounds) and the new
+ * rows (outward-rounded to the metadata dtype), equal to a recomputation over all of
+ * the page's rows.  start_pos: device int32 [B], the sequence lengths before the
+ * append (e.g. kv->seq_lens, updated by the caller afterwards).  The page table must
+ * already map the touched pages.  16/32-bit pools only (fp8 pools are quantised a
+ * whole page at a time).
+ * Replaces the KV write of QuestAttention.push_kv followed by _refresh_pages
+ * (src/linattn/variants/selection.py:176-201; page_update_triton,
+ * src/linattn/kernels/triton/quest_pages.py:84-100, 134-142).
+ */
+int linattn_paged_append(const linattn_kv_t* kv, const linattn_meta_t* meta, int64_t B, const void* k_new,
+                         const void* v_new, int32_t new_dtype, const int64_t* new_strides /*[4] elements*/,
+                         int64_t T_new, const int32_t* start_pos, int32_t* status, void* stream);
+
+/*
  * Quest upper-bound scores s[b,h,t,p] = sum_d max(q_d*min_d, q_d*max_d) in fp32,
  * written to scores (B, H_q, T_q, n_pages) contiguous, with the selection masks of
  * the reference applied: pages starting after the query position (offset + t), or

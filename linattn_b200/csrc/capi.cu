@@ -155,6 +155,26 @@ int linattn_paged_page_bounds(const linattn_kv_t* kv, int64_t B, const int32_t* 
                      "paged_page_bounds");
 }
 
+int linattn_paged_append(const linattn_kv_t* kv, const linattn_meta_t* meta, int64_t B, const void* k_new,
+                         const void* v_new, int32_t new_dtype, const int64_t* new_strides, int64_t T_new,
+                         const int32_t* start_pos, int32_t* status, void* stream) {
+  int rc = check_kv(kv);
+  if (rc) return rc;
+  if (kv->dtype != LINATTN_F32 && kv->dtype != LINATTN_F16 && kv->dtype != LINATTN_BF16)
+    return fail(LINATTN_EUNSUPPORTED, "paged_append: 16/32-bit pools only (fp8 pools are quantised per page)");
+  if (!meta || !meta->mins || !meta->maxs) return fail(LINATTN_EINVAL, "paged_append: metadata pointers NULL");
+  if (!is_float16_32(meta->dtype)) return fail(LINATTN_EUNSUPPORTED, "metadata dtype %d not supported", meta->dtype);
+  if (meta->page_table && (meta->page_table_stride <= 0 || meta->num_phys_pages <= 0))
+    return fail(LINATTN_EINVAL, "metadata page table needs a stride and num_phys_pages");
+  if (!is_float16_32(new_dtype)) return fail(LINATTN_EUNSUPPORTED, "paged_append: new rows dtype %d", new_dtype);
+  if (!k_new || !v_new || !new_strides || !start_pos) return fail(LINATTN_EINVAL, "paged_append: NULL pointer");
+  if (B < 0 || T_new < 0) return fail(LINATTN_EINVAL, "paged_append: B and T_new must be >= 0");
+  if (new_strides[3] != 1) return fail(LINATTN_EINVAL, "paged_append: new rows need unit stride on D");
+  return cuda_status(launch_paged_append(*kv, *meta, B, k_new, v_new, new_dtype, new_strides, T_new, start_pos,
+                                         status, static_cast<cudaStream_t>(stream)),
+                     "paged_append");
+}
+
 int linattn_quest_scores(const void* q, int32_t q_dtype, int64_t B, int64_t Hq, int64_t Tq, int64_t D,
                          const int64_t* q_strides, const linattn_meta_t* meta, int64_t page_size, int64_t n_pages,
                          int64_t offset, int32_t sink_pages, const int32_t* n_pages_b, float* scores,

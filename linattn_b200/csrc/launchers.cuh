@@ -30,6 +30,9 @@ int set_error(int code, const char* msg);
 
 cudaError_t launch_page_bounds(const void* k, int dtype, int64_t B, int64_t H, int64_t T_, int64_t D,
                                const int64_t* s, int64_t P, void* mins, void* maxs, cudaStream_t stream);
+cudaError_t launch_paged_append(const linattn_kv_t& kv, const linattn_meta_t& meta, int64_t B, const void* k_new,
+                                const void* v_new, int new_dtype, const int64_t* s, int64_t T_new,
+                                const int32_t* start_pos, int32_t* status, cudaStream_t stream);
 cudaError_t launch_paged_page_bounds(const linattn_kv_t& kv, int64_t B, const int32_t* first_page,
                                      int64_t max_pages, const linattn_meta_t& meta, int32_t* status,
                                      cudaStream_t stream);

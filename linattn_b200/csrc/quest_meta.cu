@@ -127,6 +127,75 @@ __global__ void __launch_bounds__(256) paged_page_bounds_kernel(linattn_kv_t kv,
   }
 }
 
+// Append: new rows of every sequence into the paged pool, and their pages' bounds.
+// One CTA per (batch, kv head, page touched by the new rows), one thread per channel:
+// the thread writes its channel of every new row of the page (K and V, converted to
+// the pool's dtype; rows are coalesced across the threads) and folds the stored keys
+// into the page's bounds, starting from the stored bounds when the page already held
+// rows.  Min / max are exact and the outward rounding of narrower metadata commutes
+// with them, so the result equals a recomputation over all of the page's rows.
+template <typename T>
+__device__ __forceinline__ T from_float(float v);
+template <> __device__ __forceinline__ float from_float<float>(float v) { return v; }
+template <> __device__ __forceinline__ __half from_float<__half>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_float<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) paged_append_kernel(linattn_kv_t kv, linattn_meta_t meta,
+                                                           const void* __restrict__ k_new,
+                                                           const void* __restrict__ v_new, int new_dtype,
+                                                           int64_t sb, int64_t sh, int64_t st, int64_t T_new,
+                                                           const int32_t* __restrict__ start_pos, int32_t* status) {
+  const int64_t H = kv.n_kv_heads, P = kv.page_size, D = kv.head_dim;
+  const int64_t h = blockIdx.x % H, b = blockIdx.x / H;
+  const int64_t start = start_pos[b];
+  const int64_t lp = start / P + blockIdx.y;  // logical page
+  const int64_t r0 = lmax(start, lp * P), r1 = lmin(start + T_new, (lp + 1) * P);
+  if (r0 >= r1 || start < 0) return;
+  int64_t phys = lp;
+  if (kv.page_table) {
+    phys = lp < kv.page_table_stride ? kv.page_table[b * kv.page_table_stride + lp] : -1;
+    if (phys < 0 || phys >= kv.num_phys_pages) {
+      if (threadIdx.x == 0) report(status, LINATTN_DEV_BAD_ID);
+      return;
+    }
+  }
+  int64_t mphys = lp;
+  if (meta.page_table) {
+    mphys = lp < meta.page_table_stride ? meta.page_table[b * meta.page_table_stride + lp] : -1;
+    if (mphys < 0 || mphys >= meta.num_phys_pages) {
+      if (threadIdx.x == 0) report(status, LINATTN_DEV_BAD_ID);
+      return;
+    }
+  }
+  const int64_t pool0 = b * kv.stride_b + phys * kv.stride_page + h * kv.stride_head;
+  T* kp = static_cast<T*>(const_cast<void*>(kv.k)) + pool0;
+  T* vp = static_cast<T*>(const_cast<void*>(kv.v)) + pool0;
+  const int64_t mo = b * meta.stride_b + mphys * meta.stride_page + h * meta.stride_head;
+  const bool had_rows = lp * P < start;
+  for (int64_t c = threadIdx.x; c < D; c += blockDim.x) {
+    float mn = INFINITY, mx = -INFINITY;
+    if (had_rows) {
+      mn = load_any(meta.mins, mo + c, meta.dtype);
+      mx = load_any(meta.maxs, mo + c, meta.dtype);
+    }
+    for (int64_t r = r0; r < r1; ++r) {
+      const int64_t src = b * sb + h * sh + (r - start) * st + c;
+      const T kv_k = from_float<T>(load_any(k_new, src, new_dtype));
+      const T kv_v = from_float<T>(load_any(v_new, src, new_dtype));
+      kp[(r - lp * P) * D + c] = kv_k;
+      vp[(r - lp * P) * D + c] = kv_v;
+      const float stored = elem_to_float<T>(&kv_k, 0);
+      mn = fminf(mn, stored);
+      mx = fmaxf(mx, stored);
+    }
+    store_bound(const_cast<void*>(meta.mins), mo + c, meta.dtype, mn, true);
+    store_bound(const_cast<void*>(meta.maxs), mo + c, meta.dtype, mx, false);
+  }
+}
+
 // ---------------------------------------------------------------------------------
 // launchers (called from capi.cu)
 // ---------------------------------------------------------------------------------
@@ -176,6 +245,31 @@ cudaError_t launch_paged_page_bounds(const linattn_kv_t& kv, int64_t B, const in
       break;
     case LINATTN_FP8E4M3:
       paged_page_bounds_kernel<fp8e4m3><<<grid, 256, 0, stream>>>(kv, B, first_page, max_pages, meta, status);
+      break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_paged_append(const linattn_kv_t& kv, const linattn_meta_t& meta, int64_t B, const void* k_new,
+                                const void* v_new, int new_dtype, const int64_t* s, int64_t T_new,
+                                const int32_t* start_pos, int32_t* status, cudaStream_t stream) {
+  if (B == 0 || T_new == 0) return cudaSuccess;
+  const int64_t P = kv.page_size;
+  const dim3 grid(static_cast<unsigned>(B * kv.n_kv_heads), static_cast<unsigned>((T_new + P - 1 + P - 1) / P));
+  const unsigned threads = static_cast<unsigned>(lmin(256, (kv.head_dim + 31) / 32 * 32));
+  switch (kv.dtype) {
+    case LINATTN_F32:
+      paged_append_kernel<float><<<grid, threads, 0, stream>>>(kv, meta, k_new, v_new, new_dtype, s[0], s[1], s[2],
+                                                               T_new, start_pos, status);
+      break;
+    case LINATTN_F16:
+      paged_append_kernel<__half><<<grid, threads, 0, stream>>>(kv, meta, k_new, v_new, new_dtype, s[0], s[1], s[2],
+                                                                T_new, start_pos, status);
+      break;
+    case LINATTN_BF16:
+      paged_append_kernel<__nv_bfloat16><<<grid, threads, 0, stream>>>(kv, meta, k_new, v_new, new_dtype, s[0],
+                                                                       s[1], s[2], T_new, start_pos, status);
       break;
     default: return cudaErrorInvalidValue;
   }

@@ -119,29 +119,37 @@ class PagedKVCache:
 
     # -- writes ----------------------------------------------------------------------
     def append(self, k: torch.Tensor, v: torch.Tensor) -> None:
-        """Append ``(B, H_kv, T_new, D)`` keys/values to every sequence and refresh the
-        metadata of the touched pages (``QuestAttention._refresh_pages``,
-        ``src/linattn/variants/selection.py:181-201``).  16/32-bit pools only."""
+        """Append ``(B, H_kv, T_new, D)`` keys/values to every sequence and fold them into
+        the bounds of the pages they touch (``QuestAttention.push_kv`` +
+        ``_refresh_pages``, ``src/linattn/variants/selection.py:176-201``): one
+        ``linattn_paged_append`` launch after the host allocator has mapped any new
+        pages.  16/32-bit pools only."""
         if self.fp8:
-            raise NotImplementedError("fp8 pools are written a page at a time (write_pages)")
+            raise NotImplementedError("fp8 pools are quantised a whole page at a time (fill)")
         L.require_cuda(k, v)
         b_, hk, tn, d = k.shape
-        if (b_, hk, d) != (self.batch, self.n_kv_heads, self.head_dim):
+        if (b_, hk, d) != (self.batch, self.n_kv_heads, self.head_dim) or v.shape != k.shape:
             raise ValueError("append shape mismatch")
-        first = []
+        if tn == 0:
+            return
+        if k.stride(3) != 1:
+            k = k.contiguous()
+        if v.stride() != k.stride():
+            v = v.contiguous()
+            k = k.contiguous()
         for b in range(self.batch):
-            start = self._host_lens[b]
-            end = start + tn
-            self._ensure_pages(b, math.ceil(end / self.page_size))
-            first.append(start // self.page_size)
-            pos = torch.arange(start, end, device=self.device)
-            phys = self.page_table[b].long()[pos // self.page_size]
-            rows = pos % self.page_size
-            self.k_pool[phys, :, rows] = k[b].transpose(0, 1).to(self.k_pool.dtype)
-            self.v_pool[phys, :, rows] = v[b].transpose(0, 1).to(self.v_pool.dtype)
-            self._host_lens[b] = end
+            self._ensure_pages(b, math.ceil((self._host_lens[b] + tn) / self.page_size))
+        status = L.status_word(self.device)
+        # start positions: the device lengths before the append (updated below, in
+        # stream order after the kernel)
+        L.check(L.lib().linattn_paged_append(
+            self.kv_desc(), self.meta_desc(), self.batch, k.data_ptr(), v.data_ptr(), L.dtype_code(k),
+            L.strides4(k), tn, self.seq_lens.data_ptr(), status.data_ptr(),
+            torch.cuda.current_stream(self.device).cuda_stream))
+        self._host_lens = [x + tn for x in self._host_lens]
         self._sync_lens()
-        self.refresh_meta(torch.tensor(first, dtype=torch.int32, device=self.device))
+        if L.strict():
+            L.check_status(self.device)
 
     def fill(self, k: torch.Tensor, v: torch.Tensor, seq_lens, page_table: Optional[torch.Tensor] = None) -> None:
         """Write whole sequences: ``k, v (B, H_kv, T, D)`` (any float dtype) with
