@@ -14,7 +14,7 @@ from linattn_b200.block_sparse import block_sparse_attention, sparse_attention  
 from linattn_b200.core import AttnConfig, AttentionVariant  # noqa: F401
 from linattn_b200.indexer import indexer_scores, indexer_topk, quantize_keys_fp8, row_topk  # noqa: F401
 from linattn_b200.merge import lse_combine  # noqa: F401
-from linattn_b200.paged import PagedKVCache, QuestDecoder  # noqa: F401
+from linattn_b200.paged import PagedKVCache, QuestDecodeGraph, QuestDecoder  # noqa: F401
 from linattn_b200.quest_pages import page_bounds, page_select, quest_select  # noqa: F401
 from linattn_b200.registry import KERNEL_VARIANTS, build, build_cuda, describe_kernel, list_kernel_variants  # noqa: F401
 

@@ -29,7 +29,7 @@ from linattn_b200 import _lib as L
 from linattn_b200.block_sparse import plan_splits, sparse_attention
 from linattn_b200.quest_pages import DECODE_OFFSET, QuestSelection
 
-__all__ = ["PagedKVCache", "QuestDecoder", "fused_select_smem", "plan_select_chunks"]
+__all__ = ["PagedKVCache", "QuestDecodeGraph", "QuestDecoder", "fused_select_smem", "plan_select_chunks"]
 
 
 class PagedKVCache:
@@ -347,3 +347,46 @@ class QuestDecoder:
         if L.strict():
             L.check_status(self.cache.device)
         return out
+
+    def graph(self) -> "QuestDecodeGraph":
+        """The decode step as one CUDA graph with pinned host input and output."""
+        return QuestDecodeGraph(self)
+
+
+class QuestDecodeGraph:
+    """A :class:`QuestDecoder` step captured once as a CUDA graph: the copy of q from a
+    pinned host buffer, the selection and attention launches, and the copy of o back
+    to a pinned host buffer.  ``run(q_host)`` copies ``q_host`` (B, H_q, 1, D) into the
+    staging buffer, replays the graph on the current stream and returns the pinned
+    output, valid once the stream is synchronised (stage the next q only after that).
+    The graph holds the cache's buffer addresses, not their contents, so appends
+    between replays are seen (the cache must not be re-allocated)."""
+
+    def __init__(self, dec: QuestDecoder):
+        c = dec.cache
+        if L.strict():
+            raise RuntimeError("QuestDecodeGraph: strict mode synchronises inside the step and cannot be captured")
+        self.dec = dec
+        shape = (c.batch, dec.n_heads, 1, c.head_dim)
+        self.q_host = torch.empty(shape, dtype=dec.out.dtype, pin_memory=True)
+        self.o_host = torch.empty(shape, dtype=dec.out.dtype, pin_memory=True)
+        self.q_dev = torch.zeros(shape, dtype=dec.out.dtype, device=c.device)
+        # one eager step on a side stream first: status word, tensor maps and kernel
+        # attributes are set up outside the capture
+        side = torch.cuda.Stream(c.device)
+        side.wait_stream(torch.cuda.current_stream(c.device))
+        with torch.cuda.stream(side):
+            dec.step(self.q_dev)
+        torch.cuda.current_stream(c.device).wait_stream(side)
+        torch.cuda.synchronize(c.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.q_dev.copy_(self.q_host, non_blocking=True)
+            out = dec.step(self.q_dev)
+            self.o_host.copy_(out, non_blocking=True)
+
+    def run(self, q_host: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if q_host is not None:
+            self.q_host.copy_(q_host)
+        self.graph.replay()
+        return self.o_host
