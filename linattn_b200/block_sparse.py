@@ -48,12 +48,15 @@ def plan_splits(b: int, hq: int, tq: int, d: int, kv_dtype: int, q_dtype: int, l
     """Split-KV factor for a call.
 
     Tensor-core path (a persistent grid of 148 SMs x 8 warps, one item at a time per
-    warp): the items run in waves of 1184, so the split count S minimises
-    ceil(units * S / 1184) * (tiles / S + 3), the waves times an item's time in tiles
-    (an item start costs about 3 tiles: the list resolution and the first copies),
-    with at least 4 tiles and at most 128 list entries per item.  Configuration 2
-    (128 units) takes S = 9 (one wave), configuration 5 (512 units) S = 9 (3.9 waves;
-    S = 4 leaves the last of its 1.7 waves mostly idle).  CUDA-core path: about 4 CTAs
+    warp; items = units x S).  When one wave fits (units x S within 90% of the 1184
+    warps, with at most 128 list entries per item), S is the largest such count: a
+    single wave finishes with its last item, and a wave that fills the last ~10% of the
+    warps ends late (configuration 2, 128 units: 8 splits = 1024 items 98 us, 9 = 1152
+    items 102-106 us, 10 = a second wave 137 us).  Otherwise the items run in waves and
+    S minimises ceil(units x S / 1184) x (tiles / S + 3), the waves times an item's time
+    in tiles (an item start costs about 3 tiles), each item keeping at least 4 tiles:
+    configuration 5 (512 units) takes 9 splits (3.9 waves, 753 us; 8 splits 806 us,
+    4 splits leave the last of 1.7 waves mostly idle).  CUDA-core path: about 4 CTAs
     per SM, each split keeping at least 2 tiles."""
     sms = torch.cuda.get_device_properties(device).multi_processor_count
     g_total = hq // list_heads
@@ -65,6 +68,9 @@ def plan_splits(b: int, hq: int, tq: int, d: int, kv_dtype: int, q_dtype: int, l
         floor = max(1, -(-max_len // 128))  # <= 128 entries per split
         cap = max(floor, min(64, tiles // 4))
         warps = 8 * sms
+        one_wave = int(0.9 * warps) // max(units, 1)
+        if one_wave >= floor:
+            return int(max(floor, min(one_wave, cap)))
         best, best_cost = floor, None
         for s in range(floor, cap + 1):
             cost = math.ceil(units * s / warps) * (tiles / s + 3.0)
