@@ -44,11 +44,13 @@ def pooled_block_scores(q: torch.Tensor, k: torch.Tensor, block: int) -> torch.T
     """``(B,H_q,n_qb,n_kb)`` fp32 pooled block scores with the GQA repeat of ``k``."""
     b, hq, _, d = q.shape
     hkv = k.shape[1]
-    qp = block_mean(q, block)
+    # the 1/sqrt(D) factor goes on the pooled queries (n_qb x D per head) rather than
+    # on the n_qb x n_kb scores: one small pass instead of one over the score matrix
+    qp = block_mean(q, block).mul_(1.0 / math.sqrt(d))
     kp = block_mean(k, block)
     g = hq // hkv
     s = torch.matmul(qp.view(b, hkv, g, qp.shape[2], d), kp.view(b, hkv, 1, kp.shape[2], d).transpose(-1, -2))
-    return s.view(b, hq, qp.shape[2], kp.shape[2]).mul_(1.0 / math.sqrt(d))
+    return s.view(b, hq, qp.shape[2], kp.shape[2])
 
 
 def merge_block_lists(topk_ids: torch.Tensor, *, period: int, first_pos: int, own_div: int, n_blocks: int,

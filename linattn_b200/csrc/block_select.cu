@@ -43,6 +43,53 @@ __global__ void block_mean_kernel(const BlockMeanParams p) {
   }
 }
 
+// 16-bit rows with unit channel stride and 16-byte aligned rows: each thread sums 8
+// channels of one block with 16-byte loads, eight rows in flight, in the same row
+// order as block_mean_kernel (bit-identical means); D / 8 threads per block.
+template <bool BF16>
+__global__ void __launch_bounds__(128) block_mean_vec_kernel(const BlockMeanParams p, int64_t units) {
+  const int tpu = static_cast<int>(p.D / 8);  // threads per (b, h, block); divides 128
+  const int64_t unit = static_cast<int64_t>(blockIdx.x) * (128 / tpu) + threadIdx.x / tpu;
+  if (unit >= units) return;
+  const int c0 = (threadIdx.x % tpu) * 8;
+  const int64_t blk = unit % p.nb, bh = unit / p.nb;
+  const int64_t h = bh % p.H, b = bh / p.H;
+  const int64_t t0 = blk * p.block;
+  const uint16_t* base = static_cast<const uint16_t*>(p.x) + b * p.s[0] + h * p.s[1] + c0;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int64_t i0 = 0; i0 < p.block; i0 += 8) {
+    uint4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int64_t t = lmin(t0 + lmin(i0 + u, p.block - 1), p.T - 1);  // the tail repeats the last row
+      v[u] = *reinterpret_cast<const uint4*>(base + t * p.s[2]);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      if (i0 + u >= p.block) break;
+      const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float lo, hi;
+        if constexpr (BF16) {
+          lo = __uint_as_float(w[q] << 16);
+          hi = __uint_as_float(w[q] & 0xffff0000u);
+        } else {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[q]));
+          lo = f.x;
+          hi = f.y;
+        }
+        acc[2 * q] += lo;
+        acc[2 * q + 1] += hi;
+      }
+    }
+  }
+  const float inv = 1.f / static_cast<float>(p.block);
+  float* o = p.out + unit * p.D + c0;
+  reinterpret_cast<float4*>(o)[0] = make_float4(acc[0] * inv, acc[1] * inv, acc[2] * inv, acc[3] * inv);
+  reinterpret_cast<float4*>(o)[1] = make_float4(acc[4] * inv, acc[5] * inv, acc[6] * inv, acc[7] * inv);
+}
+
 struct MergeParams {
   const int32_t* topk;
   int64_t rows, k;
@@ -110,7 +157,19 @@ extern "C" int linattn_block_mean(const void* x, int32_t dtype, int64_t B, int64
   p.block = block; p.nb = (T + block - 1) / block; p.out = out;
   const int64_t units = B * H * p.nb;
   if (units > 0x7fffffff) return set_error(LINATTN_EUNSUPPORTED, "block_mean: too many blocks");
-  block_mean_kernel<<<static_cast<unsigned>(units), D >= 128 ? 128 : 64, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  const bool vec = dtype != LINATTN_F32 && D % 8 == 0 && 128 % (D / 8) == 0 && p.s[3] == 1 &&
+                   (reinterpret_cast<uintptr_t>(x) & 15) == 0 && p.s[0] % 8 == 0 && p.s[1] % 8 == 0 &&
+                   p.s[2] % 8 == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+  if (vec) {
+    const int64_t per_cta = 128 / (D / 8);
+    const unsigned grid = static_cast<unsigned>((units + per_cta - 1) / per_cta);
+    if (dtype == LINATTN_BF16)
+      block_mean_vec_kernel<true><<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(p, units);
+    else
+      block_mean_vec_kernel<false><<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(p, units);
+  } else {
+    block_mean_kernel<<<static_cast<unsigned>(units), D >= 128 ? 128 : 64, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  }
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     char msg[256];

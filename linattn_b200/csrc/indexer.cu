@@ -612,6 +612,88 @@ extern "C" int linattn_indexer_scores(const void* q_idx, int32_t q_dtype, const 
   return LINATTN_OK;
 }
 
+// Short rows (n <= 32 * ITEMS <= 2048) in index order: one warp per row, eight rows
+// per CTA.  Lane l holds entries i = it * 32 + l (coalesced loads) as order-preserving
+// keys; the k-th largest key is found by a binary search over the key range with warp
+// counts (eight independent partial sums per lane, and an early exit once exactly k
+// keys reach the probe); the keys above it and the lowest-index copies of it are then
+// written in ascending index order by ballots over the entry blocks.  Same selection
+// and output as row_topk_reg_kernel's index-order path.
+template <int ITEMS>
+__global__ void __launch_bounds__(256) row_topk_warp_kernel(const RowTopkParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (r >= p.rows) return;  // warp-uniform
+  const int64_t seg = r / p.period, j = r % p.period;
+  const int nv_all = static_cast<int>(p.causal ? visible_keys(p.n, p.first_pos + j, p.kb) : p.n);
+  const int skip = static_cast<int>(lmin(p.skip, nv_all));
+  const int nv = nv_all - skip;  // candidates: entries skip .. nv_all - 1, indexed from 0 here
+  const int64_t ob = seg * p.out_bstride + j * p.out_stride;
+  const int kb = static_cast<int>(lmin(p.k, nv));
+  const float* row = p.scores + r * p.row_stride + skip;
+  uint32_t key[ITEMS];
+  uint32_t kmin = 0xffffffffu, kmax = 0u;
+#pragma unroll
+  for (int it = 0; it < ITEMS; ++it) {
+    const int i = it * 32 + lane;
+    key[it] = i < nv ? float_key(__ldg(row + i)) : 0u;  // candidate keys are > 0 (even -inf's)
+    if (i < nv) {
+      kmin = min(kmin, key[it]);
+      kmax = max(kmax, key[it]);
+    }
+  }
+  auto count_ge = [&](uint32_t t) -> uint32_t {
+    uint32_t cc[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int it = 0; it < ITEMS; ++it) cc[it & 7] += key[it] >= t ? 1u : 0u;
+    return __reduce_add_sync(0xffffffffu, ((cc[0] + cc[1]) + (cc[2] + cc[3])) + ((cc[4] + cc[5]) + (cc[6] + cc[7])));
+  };
+  uint32_t lo = __reduce_min_sync(0xffffffffu, kmin), hi = __reduce_max_sync(0xffffffffu, kmax);
+  // largest t with count(key >= t) >= kb (the kb-th largest key), or any t that exactly
+  // kb keys reach (then the keys >= t are the selection, ties included)
+  while (lo < hi && kb > 0) {
+    const uint32_t mid = lo + ((hi - lo + 1u) >> 1);
+    const uint32_t c = count_ge(mid);
+    if (c == static_cast<uint32_t>(kb)) {
+      lo = mid;
+      break;
+    }
+    if (c > static_cast<uint32_t>(kb)) lo = mid;
+    else hi = mid - 1u;
+  }
+  const uint32_t kstar = lo;
+  uint32_t n_gt = 0u;
+#pragma unroll
+  for (int it = 0; it < ITEMS; ++it) n_gt += key[it] > kstar ? 1u : 0u;
+  // copies of kstar to take, lowest index first
+  const uint32_t remaining = kb > 0 ? static_cast<uint32_t>(kb) - __reduce_add_sync(0xffffffffu, n_gt) : 0u;
+  const unsigned lt = (1u << lane) - 1u;
+  uint32_t n_sel = 0u, eq_taken = 0u;
+#pragma unroll
+  for (int it = 0; it < ITEMS; ++it) {
+    if (kb == 0) break;
+    const int i = it * 32 + lane;
+    const bool gt = key[it] > kstar;
+    const bool eq = i < nv && key[it] == kstar;
+    const unsigned eq_mask = __ballot_sync(0xffffffffu, eq);
+    const bool take = gt || (eq && eq_taken + __popc(eq_mask & lt) < remaining);
+    const unsigned take_mask = __ballot_sync(0xffffffffu, take);
+    if (take) {
+      const int64_t pos = ob + n_sel + __popc(take_mask & lt);
+      if (p.values) p.values[pos] = key_float(key[it]);
+      if (p.idx64) p.idx64[pos] = i + skip;
+      if (p.idx32) p.idx32[pos] = i + skip;
+    }
+    n_sel += __popc(take_mask);
+    eq_taken += __popc(eq_mask);
+  }
+  for (int64_t i = kb + lane; i < p.k; i += 32) {
+    if (p.values) p.values[ob + i] = -INFINITY;
+    if (p.idx64) p.idx64[ob + i] = -1;
+    if (p.idx32) p.idx32[ob + i] = -1;
+  }
+}
+
 extern "C" int linattn_row_topk(const float* scores, int64_t rows, int64_t n, int64_t row_stride, int64_t k,
                                 int32_t causal, int64_t first_pos, int64_t key_block, int64_t period, int64_t skip,
                                 int32_t sorted, float* values,
@@ -633,7 +715,13 @@ extern "C" int linattn_row_topk(const float* scores, int64_t rows, int64_t n, in
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const unsigned grid = static_cast<unsigned>(rows);
   cudaError_t e = cudaSuccess;
-  if (n <= 32768) {
+  if (!sorted && n <= 2048) {
+    const unsigned wgrid = static_cast<unsigned>((rows + 7) / 8);
+    if (n <= 512) row_topk_warp_kernel<16><<<wgrid, 256, 0, st>>>(p);
+    else if (n <= 1024) row_topk_warp_kernel<32><<<wgrid, 256, 0, st>>>(p);
+    else row_topk_warp_kernel<64><<<wgrid, 256, 0, st>>>(p);
+    e = cudaGetLastError();
+  } else if (n <= 32768) {
     const size_t smem = sorted ? static_cast<size_t>(2 * kp) * sizeof(uint32_t)
                                : static_cast<size_t>((n + 31) / 32) * sizeof(uint32_t);
     auto go = [&](auto kernel, int nt) {
