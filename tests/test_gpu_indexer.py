@@ -262,3 +262,25 @@ def test_indexer_tensor_core_shapes(cuda, h, d, kdt, tk):
     _, idx_u = indexer_topk(qd, kd, wd, k, k_scale=sc, causal=True, offset=off, sorted=False)
     srt = np.sort(np.where(idx.cpu().numpy() < 0, 1 << 40, idx.cpu().numpy()), -1)
     assert np.array_equal(np.where(srt == 1 << 40, -1, srt), idx_u.cpu().numpy())
+
+
+@pytest.mark.parametrize("n", [1500, 6000])
+def test_row_topk_causal_skip_period(cuda, n):
+    """Index-order top-k with `skip` leading non-candidates, causal visibility by row
+    position modulo `period`, ties among small integers: the warp-per-row path
+    (n <= 2048) and the block path (longer rows) against the oracle."""
+    from linattn_b200 import row_topk
+
+    g = torch.Generator().manual_seed(n)
+    rows, k, skip, period, first_pos = 30, 40, 3, 10, 7
+    s = torch.randint(0, 5, (rows, n), generator=g).float()
+    v, i = row_topk(s.to(cuda), k, sorted=False, causal=True, first_pos=first_pos, period=period, skip=skip,
+                    index_dtype=torch.int32)
+    for r in range(rows):
+        nv_all = min(n, first_pos + r % period + 1)
+        cand = s[r, skip:nv_all].numpy().astype(np.float64)
+        exp = np.full(k, -1)
+        if cand.size:
+            sel = topk_lowest_index(cand[None], min(k, cand.size))[0] + skip
+            exp[: sel.size] = np.sort(sel)
+        assert np.array_equal(i[r].cpu().numpy(), exp)
