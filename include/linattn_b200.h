@@ -389,6 +389,21 @@ int linattn_block_mean(const void* x, int32_t dtype, int64_t B, int64_t H, int64
                        const int64_t* strides /*[4]*/, int64_t block, float* out, void* stream);
 
 /*
+ * CSA2 compressed KV: the mean of each `ratio` consecutive tokens of x (B, H, T, D)
+ * (element strides, tail padded by repeating the last token) rounded to x's dtype, then,
+ * for bits 4 or 8, stored through the group-wise codec (FP4 E2M1 with absmax / 6 scales,
+ * or FP8 e4m3 with absmax / 448 scales, one scale per `group` = 32 channels, tail groups
+ * zero-padded) and dequantised back to x's dtype; bits 16 is the rounded mean alone.
+ * out (B, H, ceil(T / ratio), D) contiguous, x's dtype (bf16, f16 or f32), D <= 256.
+ * Replaces CSA2Attention.compressed_kv (src/linattn/variants/csa2.py:73-81), i.e.
+ * block_reduce (src/linattn/core.py:103-120) followed by quantize / dequantize
+ * (src/linattn/kv/quant.py:76-109).
+ */
+int linattn_csa2_pool_quant(const void* x, int32_t dtype, int64_t B, int64_t H, int64_t T, int64_t D,
+                            const int64_t* strides /*[4]*/, int64_t ratio, int32_t bits, int32_t group, void* out,
+                            void* stream);
+
+/*
  * Block lists from a top-k selection: for each of `rows` rows, the ascending union
  * (duplicates removed) of its top-k ids (int32, -1 padded, rows of k) with the forced
  * blocks [0, sink) and [own - window + 1, own], plus `own` itself with force_own, all

@@ -274,13 +274,71 @@ def make_paged_decode(out):
     np.savez_compressed(out / "paged_decode.npz", **rec)
 
 
+def make_csa2_variant(out):
+    import torch
+    from linattn.core import AttnConfig
+    from linattn.harness import structured_inputs
+    from linattn.registry import build
+
+    rec = {"fn": "CSA2Attention"}
+    # codec: compressed_kv of one tensor in bf16 / f16 / f32, ragged tail (T = 50), a
+    # partial quantisation group (D = 48), channel scales spread over 60x, and one
+    # all-zero (token group, channel group) to reach the 1e-8 scale clamp
+    gen = torch.Generator().manual_seed(11)
+    dtypes = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}
+    for d in (48, 128):
+        x = torch.randn(1, 2, 50, d, generator=gen) * torch.linspace(0.05, 3.0, d)
+        x[0, 1, :12, :32] = 0.0
+        rec[f"codec_x_d{d}"] = _np(x)
+        for name, dt in dtypes.items():
+            for ratio in (3, 4):
+                for bits in (4, 8, 16):
+                    cfg = AttnConfig(n_heads=2, n_kv_heads=2, head_dim=d,
+                                     extras={"compress_ratio": ratio, "bits": bits})
+                    kc, _ = build("csa2", cfg).compressed_kv(x.to(dt), x.to(dt))
+                    rec[f"codec_{name}_d{d}_m{ratio}_b{bits}"] = _np(kc.float())
+    # the variant in float32: chunked prefill (64 / 192) and one decode step
+    q, k, v = structured_inputs(1, 4, 192, 32, kv_heads=2, seed=7)
+    q, k, v = q.float(), k.float(), v.float()
+    rec.update(q=_np(q), k=_np(k), v=_np(v))
+    for bits in (4, 8):
+        cfg = AttnConfig(n_heads=4, n_kv_heads=2, head_dim=32, window_size=24, topk_blocks=3, compress_ratio=8,
+                         seed=5, extras={"bits": bits})
+        var = build("csa2", cfg)
+        with torch.no_grad():
+            kc, _ = var.compressed_kv(k, v)
+            rec[f"scores_b{bits}"] = _np(var.indexer_scores(q, kc))
+            rec[f"q_proj_b{bits}"] = _np(var.q_proj.detach())
+            for chunk in (64, 192):
+                v2 = build("csa2", cfg)
+                o, _ = v2.forward(q, k, v, chunk=chunk)
+                rec[f"out{chunk}_b{bits}"] = _np(o)
+                for key, val in v2.stats().items():
+                    rec[f"stats{chunk}_b{bits}_{key}"] = float(val)
+            v3 = build("csa2", cfg)
+            _, st = v3.forward(q[:, :, :191], k[:, :, :191], v[:, :, :191], chunk=191)
+            od, _ = v3.forward(q[:, :, 191:], k[:, :, 191:], v[:, :, 191:], state=st)
+            rec[f"out_decode_b{bits}"] = _np(od)
+            rec[f"reads_decode_b{bits}"] = float(v3.stats()["reads_per_query"])
+    # accounting (read_budget / memory_bytes / selection_flops) for a few settings
+    acct = []
+    for extras in ({}, {"bits": 8, "cross_layer_group": 2}, {"bits": 16, "compress_ratio": 4, "topk_groups": 9}):
+        var = build("csa2", AttnConfig(n_heads=8, n_kv_heads=2, head_dim=64, extras=dict(extras)))
+        for n in (5, 100, 4096):
+            acct.append([var.read_budget(n), var.memory_bytes(n), var.selection_flops(n), var.read_budget(n, 3),
+                         var.memory_bytes(n, 3)])
+    rec["accounting"] = np.array(acct, dtype=np.float64)
+    np.savez_compressed(out / "csa2_variant.npz", **rec)
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("LINATTN_REF", "/root/reference"))
     args = ap.parse_args()
     _import_reference(Path(args.ref))
     for fn in (make_page_bounds, make_page_select, make_topk_ties, make_quest_variant, make_block_sparse,
-               make_indexer, make_dense, make_block_selectors, make_quant, make_paged_decode, make_dsa_variant):
+               make_indexer, make_dense, make_block_selectors, make_quant, make_paged_decode, make_dsa_variant,
+               make_csa2_variant):
         fn(HERE)
         print("wrote", fn.__name__)
     return 0
