@@ -162,8 +162,8 @@ class CudaCSA2Attention(AttentionVariant):
     def stats(self) -> Dict[str, float]:
         if self._groups is None:
             return {}
-        groups = float(self._groups.float().mean())
-        window_reads = float(self._window_reads.float().mean())
+        groups = float(self._groups.double().mean())
+        window_reads = float(self._window_reads.double().mean())
         return {"reads_per_query": groups + window_reads, "groups_per_query": groups,
                 "tokens_equivalent": groups * self.compress_ratio + window_reads, "bits": float(self.bits)}
 
