@@ -99,7 +99,7 @@ def moba_select(q: torch.Tensor, k: torch.Tensor, block: int, topk: int, *,
     kp = block_mean(k, block)
     nkb = kp.shape[2]
     g = hq // hkv
-    gates = torch.matmul(q.float().view(b, hkv, g * tq, d), kp.transpose(-1, -2)).view(b, hq, tq, nkb)
+    gates = torch.matmul(q.float().reshape(b, hkv, g * tq, d), kp.transpose(-1, -2)).view(b, hq, tq, nkb)
     gates.mul_(1.0 / math.sqrt(d))
     kk = max(1, min(topk, nkb))
     # a query never routes to a block that starts after it: block j visible iff j * block <= pos

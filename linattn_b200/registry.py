@@ -13,11 +13,12 @@ from typing import Any, Dict, List
 
 from linattn_b200.core import AttentionVariant
 from linattn_b200.csa2 import CudaCSA2Attention
+from linattn_b200.nsa import CudaNSAAttention
 from linattn_b200.variants import CUDA_SUPPORTED, CudaDSAAttention, CudaQuestAttention
 
 __all__ = ["KERNEL_VARIANTS", "build", "build_cuda", "list_kernel_variants", "describe_kernel"]
 
-_CLASSES = {"quest": CudaQuestAttention, "dsa": CudaDSAAttention, "csa2": CudaCSA2Attention}
+_CLASSES = {"quest": CudaQuestAttention, "dsa": CudaDSAAttention, "csa2": CudaCSA2Attention, "nsa": CudaNSAAttention}
 
 KERNEL_VARIANTS: Dict[str, str] = {f"cuda_{name}": name for name in CUDA_SUPPORTED}
 

@@ -29,7 +29,7 @@ from linattn_b200.quest_pages import page_bounds, quest_select
 
 __all__ = ["CudaQuestAttention", "CudaDSAAttention", "CUDA_SUPPORTED"]
 
-CUDA_SUPPORTED = ("quest", "dsa", "csa2")
+CUDA_SUPPORTED = ("quest", "dsa", "csa2", "nsa")
 
 
 class CudaQuestAttention(AttentionVariant):

@@ -331,6 +331,61 @@ def make_csa2_variant(out):
     np.savez_compressed(out / "csa2_variant.npz", **rec)
 
 
+def make_nsa_variant(out):
+    import torch
+    from linattn.core import AttnConfig, block_reduce, repeat_kv
+    from linattn.harness import structured_inputs
+    from linattn.registry import build
+
+    q, k, v = structured_inputs(1, 4, 192, 32, kv_heads=2, seed=9)
+    q, k, v = q.float(), k.float(), v.float()
+    cfg = AttnConfig(n_heads=4, n_kv_heads=2, head_dim=32, block_size=16, window_size=24, topk_blocks=3,
+                     compress_ratio=8, seed=5)
+    rec = {"fn": "NSAAttention", "q": _np(q), "k": _np(k), "v": _np(v)}
+    with torch.no_grad():
+        var = build("nsa", cfg)
+        rec["gates_init"] = _np(var.gates.detach())
+        rec["o_cmp"] = _np(var.branch_compression(q, k, v, 0))
+        rec["o_slc"] = _np(var.branch_selection(q, k, v, 0))
+        rec["o_win"] = _np(var.branch_window(q, k, v, 0))
+        rec["sel_mask"] = _np(var.selection_mask(q, k, 0))
+        kr = block_reduce(repeat_kv(k, 2), 16, -2)
+        rec["block_scores"] = _np(torch.matmul(q, kr.transpose(-1, -2)) / (32 ** 0.5))
+        for chunk in (64, 192):
+            v2 = build("nsa", cfg)
+            o, _ = v2.forward(q, k, v, chunk=chunk)
+            rec[f"out{chunk}"] = _np(o)
+            for key, val in v2.stats().items():
+                rec[f"stats{chunk}_{key}"] = float(val)
+        v3 = build("nsa", cfg)
+        _, st = v3.forward(q[:, :, :191], k[:, :, :191], v[:, :, :191], chunk=191)
+        od, _ = v3.forward(q[:, :, 191:], k[:, :, 191:], v[:, :, 191:], state=st)
+        rec["out_decode"] = _np(od)
+    # with one selected block every row's selection is defined (the own block is always
+    # allowed, so the reference's top-k never reaches a later block): the full forward
+    # and the learned gates (fit, then one forward in the learned mode)
+    cfg1 = cfg.with_(topk_blocks=1)
+    with torch.no_grad():
+        v5 = build("nsa", cfg1)
+        o, _ = v5.forward(q, k, v, chunk=192)
+        rec["out192_k1"] = _np(o)
+        rec["stats192_k1_selected_blocks_per_query"] = float(v5.stats()["selected_blocks_per_query"])
+    v4 = build("nsa", cfg1)
+    rec["fit_loss"] = float(v4.fit_gates(q, k, v, steps=25, lr=0.05))
+    rec["gates_fit"] = _np(v4.gates.detach())
+    with torch.no_grad():
+        o, _ = v4.forward(q, k, v, chunk=192)
+    rec["out_learned"] = _np(o)
+    acct = []
+    for extras in ({}, {"compress_ratio": 4, "selected_blocks": 6}):
+        var = build("nsa", AttnConfig(n_heads=8, n_kv_heads=2, head_dim=64, extras=dict(extras)))
+        for n in (5, 100, 4096):
+            acct.append([var.read_budget(n), var.memory_bytes(n), var.flops(n), var.read_budget(n, 3),
+                         var.memory_bytes(n, 3), var.flops(n, 3)])
+    rec["accounting"] = np.array(acct, dtype=np.float64)
+    np.savez_compressed(out / "nsa_variant.npz", **rec)
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("LINATTN_REF", "/root/reference"))
@@ -338,7 +393,7 @@ def main() -> int:
     _import_reference(Path(args.ref))
     for fn in (make_page_bounds, make_page_select, make_topk_ties, make_quest_variant, make_block_sparse,
                make_indexer, make_dense, make_block_selectors, make_quant, make_paged_decode, make_dsa_variant,
-               make_csa2_variant):
+               make_csa2_variant, make_nsa_variant):
         fn(HERE)
         print("wrote", fn.__name__)
     return 0

@@ -1,0 +1,163 @@
+"""GPU parity of the ``cuda_nsa`` plugin: the three branches, the chunked / decode
+outputs and the fitted gates against the reference's outputs (float32, general sparse
+kernel), and the bf16 token-sparse / tcgen05 prefill paths against the oracle."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.attention import dense_attention
+from oracle.nsa import nsa_block_scores, nsa_branches, nsa_fill_rows, nsa_select
+from tests.conftest import golden
+
+pytestmark = pytest.mark.gpu
+
+TOL_32 = 2e-5
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy()
+
+
+def _cfg(selected=3, **kw):
+    from linattn_b200.core import AttnConfig
+
+    base = dict(n_heads=4, n_kv_heads=2, head_dim=32, block_size=16, window_size=24, topk_blocks=selected,
+                compress_ratio=8, seed=5)
+    base.update(kw)
+    return AttnConfig(**base)
+
+
+def _defined_rows(g, selected=3):
+    sc = g["block_scores"][0]
+    h, t, n_kb = sc.shape
+    ok = np.ones((h, t), dtype=bool)
+    ok[:, nsa_fill_rows(t, 16, selected, n_kb)] = False
+    for hh in range(h):
+        for tt in range(t):
+            s = np.sort(sc[hh, tt][np.arange(n_kb) * 16 <= tt])[::-1]
+            if s.size > selected and abs(s[selected - 1] - s[selected]) <= 1e-6 * max(1.0, abs(s[selected])):
+                ok[hh, tt] = False
+    return ok
+
+
+def _qkv(g, cuda):
+    return (torch.from_numpy(g[x]).to(cuda) for x in "qkv")
+
+
+def test_cuda_nsa_branches_golden(cuda):
+    from linattn_b200 import build
+
+    g = golden("nsa_variant")
+    q, k, v = _qkv(g, cuda)
+    var = build("cuda_nsa", _cfg())
+    ok = _defined_rows(g)
+    assert np.abs(_np(var.branch_compression(q, k, v, 0)) - g["o_cmp"]).max() < TOL_32
+    assert np.abs(_np(var.branch_window(q, k, v, 0)) - g["o_win"]).max() < TOL_32
+    err = np.abs(_np(var.branch_selection(q, k, v, 0)) - g["o_slc"])[0].max(-1)
+    assert err[ok].max() < TOL_32
+    # the selected blocks, as a token mask, on the rows the reference defines
+    ids, counts = var.selection_lists(q, k, 0)
+    ids, counts = ids.cpu().numpy()[0], counts.cpu().numpy()[0]
+    sel = np.zeros((4, 192, 12), dtype=bool)
+    for hh in range(4):
+        for tt in range(192):
+            sel[hh, tt, ids[hh, tt, :counts[hh, tt]]] = True
+    tok = np.repeat(sel, 16, axis=-1)
+    assert np.array_equal(tok[ok], g["sel_mask"][0][ok])
+
+
+@pytest.mark.parametrize("chunk", [64, 192])
+def test_cuda_nsa_variant_golden(cuda, chunk):
+    from linattn_b200 import build
+
+    g = golden("nsa_variant")
+    q, k, v = _qkv(g, cuda)
+    var = build("cuda_nsa", _cfg())
+    out, _ = var.forward(q, k, v, chunk=chunk)
+    ok = _defined_rows(g)
+    assert np.abs(_np(out) - g[f"out{chunk}"])[0].max(-1)[ok].max() < TOL_32
+    st = var.stats()
+    assert st["reads_per_query"] == pytest.approx(float(g[f"stats{chunk}_reads_per_query"]))
+    if chunk == 64:
+        assert st["selected_blocks_per_query"] == pytest.approx(float(g["stats64_selected_blocks_per_query"]),
+                                                                rel=1e-6)
+
+
+def test_cuda_nsa_single_block_and_decode_golden(cuda):
+    from linattn_b200 import build
+
+    g = golden("nsa_variant")
+    q, k, v = _qkv(g, cuda)
+    var = build("cuda_nsa", _cfg(selected=1))
+    out, _ = var.forward(q, k, v, chunk=192)
+    assert np.abs(_np(out) - g["out192_k1"]).max() < TOL_32
+    assert var.stats()["selected_blocks_per_query"] == pytest.approx(
+        float(g["stats192_k1_selected_blocks_per_query"]), rel=1e-6)
+    var = build("cuda_nsa", _cfg())
+    _, st = var.forward(q[:, :, :191], k[:, :, :191], v[:, :, :191], chunk=191)
+    od, _ = var.forward(q[:, :, 191:], k[:, :, 191:], v[:, :, 191:], state=st)
+    assert np.abs(_np(od) - g["out_decode"]).max() < TOL_32
+
+
+def test_cuda_nsa_fit_gates_golden(cuda):
+    from linattn_b200 import build
+
+    g = golden("nsa_variant")
+    q, k, v = _qkv(g, cuda)
+    var = build("cuda_nsa", _cfg(selected=1))
+    loss = var.fit_gates(q, k, v, steps=25, lr=0.05)
+    assert loss == pytest.approx(float(g["fit_loss"]), rel=1e-4)
+    assert np.abs(_np(var.gates) - g["gates_fit"]).max() < 1e-4
+    assert var.gate_mode == "learned"
+    out, _ = var.forward(q, k, v, chunk=192)
+    assert np.abs(_np(out) - g["out_learned"]).max() < 1e-4
+
+
+@pytest.mark.parametrize("d,block,selected", [(128, 64, 2), (64, 16, 3)])
+def test_cuda_nsa_bf16_paths(cuda, d, block, selected):
+    """bf16: compression and window branches on the token-sparse kernel, selection on the
+    tcgen05 prefill kernel (64-token blocks, D = 128) or the general kernel; each branch
+    against float64 attention (pooled rows rounded to bf16 as the reference pools), the
+    lists against the oracle's selection on rows without a near-tie."""
+    from linattn_b200 import build
+
+    gen = torch.Generator().manual_seed(d + block)
+    b, hq, hkv, t = 1, 4, 2, 300
+    q, k, v = (torch.randn(b, h, t, d, generator=gen).bfloat16() for h in (hq, hkv, hkv))
+    cfg = _cfg(selected, head_dim=d, block_size=block, window_size=40)
+    var = build("cuda_nsa", cfg)
+    qc, kc, vc = q.to(cuda), k.to(cuda), v.to(cuda)
+    qn, kn, vn = (x.float().numpy() for x in (q, k, v))
+    o_cmp, o_slc_oracle, o_win, sel_oracle = nsa_branches(qn, kn, vn, compress=8, block=block, selected=selected,
+                                                          window=40, dtype="bf16")
+    tol = 2e-3 + 2.0 ** -8 * np.abs(o_cmp)
+    assert np.all(np.abs(_np(var.branch_compression(qc, kc, vc, 0)) - o_cmp) <= tol)
+    assert np.all(np.abs(_np(var.branch_window(qc, kc, vc, 0)) - o_win) <= 2e-3 + 2.0 ** -8 * np.abs(o_win))
+    # selection: the plugin's lists against the oracle's on rows without a near-tie
+    ids, counts = var.selection_lists(qc, kc, 0)
+    ids, counts = ids.cpu().numpy(), counts.cpu().numpy()
+    n_kb = -(-t // block)
+    sel = np.zeros((b, hq, t, n_kb), dtype=bool)
+    for idx in np.ndindex(b, hq, t):
+        sel[idx][ids[idx][:counts[idx]]] = True
+    sc = nsa_block_scores(qn, kn, block, "bf16")
+    near = np.zeros((b, hq, t), dtype=bool)
+    for idx in np.ndindex(b, hq, t):
+        s = np.sort(sc[idx][np.arange(n_kb) * block <= idx[2]])[::-1]
+        if s.size > selected:
+            near[idx] = abs(s[selected - 1] - s[selected]) <= 1e-4 * max(1.0, abs(s[selected]))
+    assert near.mean() < 0.05
+    assert np.array_equal(sel[~near], sel_oracle[~near])
+    # the selection branch against float64 attention over the plugin's own blocks
+    tok = np.repeat(sel, block, axis=-1)[..., :t]
+    ref = dense_attention(qn, kn, vn, causal=False, mask=tok)
+    got = _np(var.branch_selection(qc, kc, vc, 0))
+    assert np.all(np.abs(got - ref) <= 2e-3 + 2.0 ** -8 * np.abs(ref))
+    # the combination: uniform gates over the three branch outputs
+    out, _ = var.forward(qc, kc, vc, chunk=t)
+    mixed = (o_cmp + ref + o_win) / 3.0
+    assert np.all(np.abs(_np(out) - mixed) <= 4e-3 + 2.0 ** -8 * np.abs(mixed))
+    del o_slc_oracle
