@@ -133,12 +133,18 @@ class CudaCSA2Attention(AttentionVariant):
 
     # -- attention -------------------------------------------------------------------
     def attend(self, q: torch.Tensor, state: Dict[str, Any], offset: int = 0) -> torch.Tensor:
+        return self.attend_kv(q, state["k"], state["v"], offset=offset)
+
+    def attend_kv(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, offset: int = 0,
+                  compressed: Optional[Tuple[torch.Tensor, torch.Tensor]] = None) -> torch.Tensor:
+        """``attend`` over explicit ``k, v``; ``compressed = (kc, vc)`` is this k, v's
+        ``compressed_kv`` when the caller already holds it (cross-layer reuse: every layer
+        of a group reads the representative layer's copy)."""
         L.require_cuda(q)
-        k, v = state["k"], state["v"]
         b, h, t_q, d = q.shape
         t_k = k.shape[-2]
         win = max(1, min(self.window, t_k))
-        kc, vc = self.compressed_kv(k, v)
+        kc, vc = self.compressed_kv(k, v) if compressed is None else compressed
         gids = self.select_groups(q, kc, t_k, offset)
         gids = torch.where(gids >= 0, gids + t_k, gids)  # pooled rows follow the raw keys
         k_all = torch.cat([k, kc], dim=-2)
@@ -159,11 +165,13 @@ class CudaCSA2Attention(AttentionVariant):
         self._groups = reads - self._window_reads
         return out
 
-    def stats(self) -> Dict[str, float]:
+    def stats(self, rows: Optional[slice] = None) -> Dict[str, float]:
+        """The last ``attend``'s means; ``rows`` restricts them to a range of its queries."""
         if self._groups is None:
             return {}
-        groups = float(self._groups.double().mean())
-        window_reads = float(self._window_reads.double().mean())
+        sel = slice(None) if rows is None else rows
+        groups = float(self._groups[..., sel].double().mean())
+        window_reads = float(self._window_reads[sel].double().mean())
         return {"reads_per_query": groups + window_reads, "groups_per_query": groups,
                 "tokens_equivalent": groups * self.compress_ratio + window_reads, "bits": float(self.bits)}
 
