@@ -8,7 +8,8 @@ pages scattered by a seeded random permutation over a pool of 16x1024 pages; bud
 32 pages + sink page 0 + the last page per query head (top-34 with both forced),
 GQA union per kv head.  A step = page scoring + top-k/union + sparse attention
 (split-KV + merge) for all 16 sequences; inputs resident in HBM, L2 flushed (a
-256 MiB write) before every step, outside the timed events.
+256 MiB write, then a read of it, so no dirty line is left to write back) before
+every step, outside the timed events.
 
 ``python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]``
 prints one JSON line.  For N > 1 (torchrun) every rank runs its own 16 sequences
@@ -51,6 +52,15 @@ C3 = dict(B=1, T=32768, Hq=32, Hkv=8, D=128, HI=4, DI=64, topk=2048, scale_group
 C4 = dict(B=2, T=131072, Hq=32, Hkv=8, D=128, block=64, sink_blocks=1, window_blocks=16, topk=16, rank=8, amp=0.5)
 C5 = dict(B=64, Hq=64, Hkv=8, D=128, T=1 << 20, P=64, topk=64, needle_frac=0.005)
 L2_FLUSH_BYTES = 256 << 20
+L2_NOTE = ("flushed before every step, outside the timed events: a 256 MiB write, then a read of the same "
+           "256 MiB so that the flush's dirty lines are written back before the step, not inside it")
+
+
+def l2_flush(buf: torch.Tensor) -> None:
+    """Write a buffer twice the L2 size, then read it back: L2 then holds only clean lines of
+    the flush buffer (none of the step's data, and no write-back left for the step)."""
+    buf.zero_()
+    buf.view(torch.int64).amax()
 
 
 # ---------------------------------------------------------------------------------
@@ -255,13 +265,13 @@ def _time_events(fn_parts, steps: int, warmup: int, flush, stream):
     """Runs the phases of one step (callables) `warmup` + `steps` times with an L2 flush
     before every step; returns the mean ms of each phase over the timed steps."""
     for _ in range(warmup):
-        flush.zero_()
+        l2_flush(flush)
         for f in fn_parts:
             f()
     torch.cuda.synchronize()
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(fn_parts) + 1)] for _ in range(steps)]
     for i in range(steps):
-        flush.zero_()
+        l2_flush(flush)
         ev[i][0].record(stream)
         for j, f in enumerate(fn_parts):
             f()
@@ -349,7 +359,7 @@ def run_prefill_workload(args):
             line = dict(base, metric="block-sparse causal prefill TFLOP/s", value=r["prefill_tflops"], unit="TFLOP/s",
                         ms_per_step=r["prefill_ms"],
                         config={"workload": "block_sparse_prefill_c4" if t == C4["T"] else f"block_sparse_prefill_c4_t{t}",
-                                "l2": "flushed (256 MiB write) before every step, outside the timed events", **C4,
+                                "l2": L2_NOTE, **C4,
                                 "T": t},
                         roofline={"bound": "tensor", "kernel": "prefill_umma_kernel", "achieved": r["prefill_tflops"],
                                   "peak": peak, "unit": "TFLOP/s", "frac": r["frac_of_bf16_peak"], "peak_kind": kind,
@@ -362,7 +372,7 @@ def run_prefill_workload(args):
             line = dict(base, metric="DSA prefill tok/s", value=round(t / (r["total_ms"] * 1e-3), 1), unit="tok/s",
                         ms_per_step=r["total_ms"],
                         config={"workload": "dsa_indexer_attention_c3" if t == C3["T"] else f"dsa_c3_t{t}",
-                                "l2": "flushed (256 MiB write) before every step, outside the timed events", **C3,
+                                "l2": L2_NOTE, **C3,
                                 "T": t},
                         roofline={"bound": "hbm", "kernel": "token_attention_kernel (gathered rows; L2 hits)",
                                   "achieved": r["attention_gathered_gbs"], "peak": hbm, "unit": "GB/s",
@@ -498,7 +508,7 @@ def run_ours(args, rank, world, local_rank):
     stream = torch.cuda.current_stream(device)
 
     for i in range(args.warmup):
-        flush.zero_()
+        l2_flush(flush)
         dec.step(qs[i])
     torch.cuda.synchronize(device)
     if world > 1:
@@ -514,7 +524,7 @@ def run_ours(args, rank, world, local_rank):
         t_wall = time.perf_counter()
         for i in range(args.steps):
             q = qs[args.warmup + i]
-            flush.zero_()
+            l2_flush(flush)
             ev[i][0].record(stream)
             dec.select(q)
             ev[i][1].record(stream)
@@ -546,7 +556,7 @@ def run_ours(args, rank, world, local_rank):
         o_host.copy_(dec.step(q_dev), non_blocking=True)
     torch.cuda.synchronize(device)
     for i in range(args.steps):
-        flush.zero_()
+        l2_flush(flush)
         e2e_ev[i][0].record(stream)
         q_dev.copy_(q_host[args.warmup + i], non_blocking=True)
         out = dec.step(q_dev)
@@ -562,7 +572,7 @@ def run_ours(args, rank, world, local_rank):
         torch.cuda.synchronize(device)
     g_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
     for i in range(args.steps):
-        flush.zero_()
+        l2_flush(flush)
         g_ev[i][0].record(stream)
         g.run(q_host[args.warmup + i])
         g_ev[i][1].record(stream)
@@ -607,7 +617,7 @@ def run_ours(args, rank, world, local_rank):
         "config": {"workload": "quest_decode_c2" if b == C2["B"] else f"quest_decode_c2_b{b}", "batch_per_gpu": b, "global_batch": b * world, "seq_len": t,
                    "page_size": p, "n_heads": hq, "n_kv_heads": hkv, "head_dim": d,
                    "budget_pages": c["topk"], "sink_pages": c["sink_pages"], "parallelism": f"dp{world} (batch)",
-                   "l2": "flushed (256 MiB write) before every step, outside the timed events",
+                   "l2": L2_NOTE,
                    "n_splits": dec.n_splits, "select_chunks": dec.chunks},
         "hbm_gbs": round(step_bytes / (mean_step * 1e-3) / 1e9, 1),
         "step_breakdown_ms": {"select": round(mean_sel, 4), "attend": round(mean_att, 4)},
@@ -680,7 +690,7 @@ def run_c5(args, rank, world, local_rank):
     phases = [phase_select, phase_merge, phase_attend, phase_combine]
     for i in range(args.warmup):
         box["q"] = qs[i]
-        flush.zero_()
+        l2_flush(flush)
         for f in phases:
             f()
     torch.cuda.synchronize(device)
@@ -695,7 +705,7 @@ def run_c5(args, rank, world, local_rank):
         t_wall = time.perf_counter()
         for i in range(args.steps):
             box["q"] = qs[args.warmup + i]
-            flush.zero_()
+            l2_flush(flush)
             ev[i][0].record(stream)
             for j, f in enumerate(phases):
                 f()
@@ -722,7 +732,7 @@ def run_c5(args, rank, world, local_rank):
         torch.distributed.barrier()
     e2e_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
     for i in range(args.steps):
-        flush.zero_()
+        l2_flush(flush)
         e2e_ev[i][0].record(stream)
         q_dev.copy_(q_host[args.warmup + i], non_blocking=True)
         o_host.copy_(dec.step(q_dev, exchange=exchange), non_blocking=True)
@@ -773,8 +783,7 @@ def run_c5(args, rank, world, local_rank):
                    "seq_len": t, "page_size": p, "n_heads": hq, "n_kv_heads": hkv, "head_dim": d,
                    "budget_pages": c["topk"], "pages_per_gpu_per_seq": n_loc,
                    "parallelism": f"sequence-sharded x{world} (KV pages split, NCCL all-gathers)",
-                   "l2": "flushed (256 MiB write) before every step, outside the timed events; per-step inputs "
-                         "(page metadata + selected pages) exceed L2 anyway"},
+                   "l2": L2_NOTE + "; per-step inputs (page metadata + selected pages) exceed L2 anyway"},
         "step_breakdown_ms": {"select": round(ph_max[0], 4), "exchange_candidates+merge": round(ph_max[1], 4),
                               "attend": round(ph_max[2], 4), "exchange_partials+combine": round(ph_max[3], 4)},
         "bytes_per_step_per_gpu": {"meta": int(meta_bytes), "scores": int(score_bytes), "kv_selected": int(kv_bytes)},
