@@ -202,3 +202,22 @@ def test_csa2_stack_against_reference(cuda):
     # the divergences move only through the few rows decided by a tie
     for key in ("divergence_shared_vs_ref", "divergence_unshared_vs_ref", "sharing_delta"):
         assert cmp[key] == pytest.approx(float(g[f"cmp_{key}"]), rel=0.1, abs=2e-3), key
+
+
+@pytest.mark.parametrize("name", ["bf16", "f32"])
+@pytest.mark.parametrize("bits", [4, 8])
+def test_pool_quant_vector_and_scalar_forms(cuda, name, bits):
+    """D = 96 (12 threads per pooled row: a CTA's last threads idle) on the vector form,
+    and the same values through a view one element off 16-byte alignment (the scalar
+    form): both bit-exact with the oracle."""
+    from linattn_b200 import csa2_pool_quant
+
+    gen = torch.Generator().manual_seed(bits + len(name))
+    b, h, t, d, ratio = 2, 3, 1001, 96, 7
+    x = (torch.randn(b, h, t, d + 1, generator=gen) * torch.linspace(0.02, 3.0, d + 1)).to(DTYPES[name])
+    ref = compressed_kv(x[..., 1:].float().numpy(), ratio, bits, 32, name)
+    xg = x.to(cuda)
+    aligned = csa2_pool_quant(xg[..., 1:].contiguous(), ratio, bits)
+    shifted = csa2_pool_quant(xg[..., 1:], ratio, bits)  # base one element past alignment
+    assert np.array_equal(_np(aligned), ref)
+    assert np.array_equal(_np(shifted), ref)
