@@ -383,6 +383,102 @@ def run_prefill_workload(args):
     return line
 
 
+CV = dict(B=1, T=16384, Hq=32, Hkv=8, D=128, csa2_ratio=16, csa2_topk_groups=64, csa2_window=256, csa2_bits=4,
+          nsa_block=64, nsa_selected=16, nsa_window=512, nsa_compress=16)
+
+
+def run_variants_workload(args):
+    """The CSA2 and NSA plugins' prefill forward on one GPU (``--workload variants``):
+    per-phase CUDA-event times, the pool + codec kernel's HBM bandwidth, the CSA2
+    attention's gathered bandwidth and the NSA selection branch's TFLOP/s.  Not part of
+    the default run."""
+    from linattn_b200.core import AttnConfig
+    from linattn_b200.registry import build
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    hbm, peak, kind = measured_peaks()
+    c = CV
+    b, hq, hkv, t, d = c["B"], c["Hq"], c["Hkv"], args.seq_len or c["T"], c["D"]
+    g = torch.Generator(device=device).manual_seed(77)
+    q, k, v = (torch.randn(b, h, t, d, device=device, generator=g, dtype=torch.float32).to(torch.bfloat16)
+               for h in (hq, hkv, hkv))
+    with ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[0])) as clocks:
+        # ---- CSA2
+        csa = build("cuda_csa2", AttnConfig(n_heads=hq, n_kv_heads=hkv, head_dim=d, seed=1,
+                                            extras={"compress_ratio": c["csa2_ratio"], "bits": c["csa2_bits"],
+                                                    "topk_groups": c["csa2_topk_groups"], "window": c["csa2_window"]}))
+        st = {}
+
+        def pool():
+            st["kv"] = csa.compressed_kv(k, v)
+
+        def select():
+            st["ids"] = csa.select_groups(q, st["kv"][0], t, 0)
+
+        def attend():
+            st["o"] = csa.attend_kv(q, k, v, compressed=st["kv"])
+        pool()
+        select()
+        ms_pool, ms_sel, ms_att = _time_events([pool, select, attend], args.steps, args.warmup, flush, stream)
+        reads = csa.stats()["reads_per_query"]
+        n_groups = st["kv"][0].shape[2]
+        pool_bytes = 2 * (b * hkv * t * d * 2 + b * hkv * n_groups * d * 2)
+        gathered = reads * b * hkv * t * 2 * d * 2  # K and V rows per (query, kv head)
+        ms_attention = max(ms_att - ms_sel, 1e-9)
+        csa2 = {"pool_quant_ms": round(ms_pool, 4), "select_ms": round(ms_sel, 4),
+                "attend_ms (selection + attention)": round(ms_att, 4), "total_ms": round(ms_pool + ms_att, 4),
+                "tok_per_s": round(b * t / ((ms_pool + ms_att) * 1e-3), 1),
+                "pool_quant_gbs": round(pool_bytes / (ms_pool * 1e-3) / 1e9, 1),
+                "pool_quant_frac_of_hbm": round(pool_bytes / (ms_pool * 1e-3) / 1e9 / hbm, 4),
+                "reads_per_query": round(reads, 2), "groups_per_query": round(csa.stats()["groups_per_query"], 2),
+                "attention_gathered_gbs": round(gathered / (ms_attention * 1e-3) / 1e9, 1)}
+        # ---- NSA
+        nsa = build("cuda_nsa", AttnConfig(n_heads=hq, n_kv_heads=hkv, head_dim=d, seed=1, block_size=c["nsa_block"],
+                                           window_size=c["nsa_window"], topk_blocks=c["nsa_selected"],
+                                           compress_ratio=c["nsa_compress"]))
+        outs = torch.empty(3, *q.shape, dtype=torch.float32, device=device)
+        ns = {}
+
+        def cmp_():
+            nsa.branch_compression(q, k, v, 0, out=outs[0])
+
+        def sel_lists():
+            ns["lists"] = nsa.selection_lists(q, k, 0)
+
+        def slc():
+            nsa.branch_selection(q, k, v, 0, out=outs[1])
+
+        def win():
+            nsa.branch_window(q, k, v, 0, out=outs[2])
+
+        def full():
+            nsa.attend(q, {"k": k, "v": v}, 0)
+        sel_lists()
+        ms_c, ms_l, ms_s, ms_w, ms_f = _time_events([cmp_, sel_lists, slc, win, full], args.steps, args.warmup, flush,
+                                                    stream)
+        counts = ns["lists"][1].long()
+        pairs = counts.sum().item() * c["nsa_block"]  # whole blocks are read
+        slc_tfl = 4 * d * pairs / (max(ms_s - ms_l, 1e-9) * 1e-3) / 1e12
+        nsa_r = {"compression_branch_ms": round(ms_c, 4), "selection_lists_ms": round(ms_l, 4),
+                 "selection_branch_ms (lists + attention)": round(ms_s, 4), "window_branch_ms": round(ms_w, 4),
+                 "attend_ms": round(ms_f, 4), "tok_per_s": round(b * t / (ms_f * 1e-3), 1),
+                 "selected_blocks_per_query": round(counts.float().mean().item(), 2),
+                 "selection_attention_tflops": round(slc_tfl, 1), "selection_attention_frac_of_bf16_peak":
+                     round(slc_tfl / peak, 4)}
+    line = {"metric": "CSA2 / NSA prefill tok/s", "value": csa2["tok_per_s"], "unit": "tok/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": csa2["total_ms"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1))",
+            "config": {"workload": "csa2_nsa_prefill", "l2": L2_NOTE, **c, "T": t},
+            "roofline": {"bound": "hbm", "kernel": "csa2_pool_quant_vec_kernel", "achieved": csa2["pool_quant_gbs"],
+                         "peak": hbm, "unit": "GB/s", "frac": csa2["pool_quant_frac_of_hbm"], "peak_kind": kind,
+                         "traffic": None},
+            "detail": {"csa2": csa2, "nsa": nsa_r}, "gpu_launches": None, "clocks": clocks.summary()}
+    return line
+
+
 # ---------------------------------------------------------------------------------
 # CPU baselines (rank 0, N == 1 / reference arm): bounded samples of the workload
 # ---------------------------------------------------------------------------------
@@ -850,9 +946,10 @@ def main(argv=None) -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences per GPU (default: the config's; smaller only for profiling captures)")
-    ap.add_argument("--workload", default="c2", choices=["c2", "c3", "c4", "c5"],
+    ap.add_argument("--workload", default="c2", choices=["c2", "c3", "c4", "c5", "variants"],
                     help="c2: paged Quest decode (the headline); c3: DSA indexer + token attention; c4: block-sparse "
-                         "prefill; c5: million-token sequence-sharded decode")
+                         "prefill; c5: million-token sequence-sharded decode; variants: the CSA2 and NSA plugins' "
+                         "prefill forward")
     ap.add_argument("--seq-len", type=int, default=None,
                     help="c3 / c4 / c5 only: a shorter sequence (profiling captures)")
     ap.add_argument("--no-secondary", action="store_true",
@@ -886,6 +983,10 @@ def main(argv=None) -> int:
             if world > 1:
                 raise SystemExit("--workload c3 / c4 run on one GPU")
             line = run_prefill_workload(args)
+        elif args.workload == "variants":
+            if world > 1:
+                raise SystemExit("--workload variants runs on one GPU")
+            line = run_variants_workload(args)
         else:
             if args.batch is None:
                 args.batch = C2["B"]
