@@ -421,8 +421,12 @@ int linattn_merge_block_lists(const int32_t* topk, int64_t rows, int64_t k, int6
  * Block-sparse causal prefill on the tcgen05 tensor cores.  Query t of head h reads the
  * 64-token key blocks of list ids[b, h, t / rows_per_list, :] (ascending, -1 padded,
  * counts optional; id_strides / count_strides = {batch, head, list row} in elements),
- * plus the tokens below `sink`, restricted to keys < Tk and, with `causal`, to keys
- * <= offset + t.  q (B, H_q, T_q, 128), K / V (B, H_kv, Tk, 128): contiguous rows,
+ * plus the tokens below `sink`, restricted to keys < Tk and, with `causal` = c >= 1, to
+ * keys j with j * c <= offset + t + c - 1 (c = 1: j <= offset + t; c > 1: the keys are
+ * pooled groups of c tokens, read once their group has started, the compression branch
+ * of NSAAttention, src/linattn/variants/native_sparse.py:67-76); with `window` > 0
+ * (no sink) also to keys >= offset + t - window + 1 (the window branch,
+ * native_sparse.py:100-105).  q (B, H_q, T_q, 128), K / V (B, H_kv, Tk, 128): contiguous rows,
  * bf16 or f16 (one type); out with element strides, lse_out (B, H_q, T_q) optional.
  * Lists of at most 64 blocks, Tk <= 2^18.  A row that reads nothing gets o = 0,
  * lse = -inf.  Replaces the token mask + masked dense attention of
@@ -437,7 +441,7 @@ int linattn_block_sparse_prefill(const void* q, int32_t dtype, int64_t B, int64_
                                  const void* v, int64_t Hkv, int64_t Tk, int64_t D, const int32_t* ids,
                                  const int32_t* counts, const int64_t* id_strides /*[3]*/, int64_t n_max,
                                  int64_t rows_per_list, const int64_t* count_strides /*[3]*/, int64_t sink,
-                                 int32_t causal, int64_t offset, float scale, void* out,
+                                 int32_t causal, int64_t window, int64_t offset, float scale, void* out,
                                  const int64_t* out_strides /*[4]*/, float* lse_out, const void* v_f16,
                                  const float* v_scale, int32_t* status, void* stream);
 

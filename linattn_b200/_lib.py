@@ -122,7 +122,7 @@ def _declare(lib: ctypes.CDLL) -> None:
                                               c_vp, c_i64, c_vp, c_vp]
     lib.linattn_block_sparse_prefill.argtypes = [c_vp, c_i32, c_i64, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64,
                                                  c_vp, c_vp, P(c_i64), c_i64, c_i64, P(c_i64), c_i64, c_i32, c_i64,
-                                                 ctypes.c_float, c_vp, P(c_i64), c_vp, c_vp, c_vp, c_vp, c_vp]
+                                                 c_i64, ctypes.c_float, c_vp, P(c_i64), c_vp, c_vp, c_vp, c_vp, c_vp]
     lib.linattn_prefill_v_to_f16.argtypes = [c_vp, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp]
     lib.linattn_shard_merge.argtypes = [c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_i64,
                                         c_vp, c_vp, c_vp, c_i64, c_vp, c_i64, c_vp, c_vp]

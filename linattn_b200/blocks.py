@@ -18,7 +18,7 @@
 from __future__ import annotations
 
 import math
-from typing import Optional, Tuple
+from typing import Optional, Tuple, Union
 
 import torch
 
@@ -111,12 +111,17 @@ def moba_select(q: torch.Tensor, k: torch.Tensor, block: int, topk: int, *,
 
 def block_sparse_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ids: torch.Tensor, *,
                          counts: Optional[torch.Tensor] = None, rows_per_list: int = 64, sink: int = 0,
-                         causal: bool = True, offset: int = 0, scale: Optional[float] = None,
+                         causal: Union[bool, int] = True, window: int = 0, offset: int = 0,
+                         scale: Optional[float] = None,
                          lse_out: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
                          v_f16: Optional[bool] = None) -> torch.Tensor:
     """Block-sparse causal prefill on the tcgen05 tensor cores: query ``t`` reads the
     64-token key blocks of ``ids[b, h, t // rows_per_list]`` (ascending, -1 padded) plus
     the tokens below ``sink``.  ``q (B,H_q,T_q,128)``, ``k, v (B,H_kv,T_k,128)``, bf16 or f16.
+    ``causal``: ``True`` / 1 reads keys ``<= offset + t``; an integer ``c > 1`` treats the
+    keys as pooled groups of ``c`` tokens and reads key ``j`` once ``j * c <= offset + t
+    + c - 1`` (NSA's compression branch).  ``window > 0`` (no sink): a query also skips the
+    keys below ``offset + t - window + 1`` (a token-exact sliding window).
 
     For bf16 inputs, ``v_f16`` (default on) first copies V to f16 (exact up to a
     per-(b, kv head) power-of-two scale) so that the P V product takes one f16 P part
@@ -148,7 +153,8 @@ def block_sparse_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ids:
                                                  amax.data_ptr(), L.stream_of(q)))
     L.check(L.lib().linattn_block_sparse_prefill(
         q.data_ptr(), L.dtype_code(q), b, hq, tq, k.data_ptr(), v.data_ptr(), hkv, tk, d, ids.data_ptr(),
-        L.ptr(counts), (L.c_i64 * 3)(*ids.stride()[:3]), ids.shape[-1], rows_per_list, cs, sink, int(causal), offset,
+        L.ptr(counts), (L.c_i64 * 3)(*ids.stride()[:3]), ids.shape[-1], rows_per_list, cs, sink, int(causal),
+        int(window), offset,
         scale, out.data_ptr(), L.strides4(out), L.ptr(lse_out), L.ptr(v16), L.ptr(vsc), status.data_ptr(),
         L.stream_of(q)))
     if L.strict():

@@ -3,7 +3,10 @@
 // Every query row reads the 64-token key blocks of its own ascending block list (one
 // list per `rows_per_list` consecutive queries: 64 for per-q-block lists such as
 // MInference's block-sparse pattern or sink + window + top-k, 1 for MoBA's per-token
-// routing), plus the tokens below `sink`, causally (key <= offset + t) and below T_k.
+// routing), plus the tokens below `sink`, causally (key <= offset + t; with causal = c > 1
+// the keys are pooled groups of c tokens and key j is read once its group has started,
+// j * c <= offset + t + c - 1, NSA's compression-branch rule), with `window` > 0 only keys
+// >= offset + t - window + 1 (a token-exact sliding window), and below T_k.
 // (MInferenceAttention._block_sparse / MoBAAttention.select + the masked attention of
 // BlockSelectionAttention.attend, src/linattn/variants/selection.py:86-116, 339-353,
 // 635-649.)
@@ -54,6 +57,7 @@ struct PrefillParams {
   int64_t ls_b, ls_h, ls_r, n_max, rows_per_list, cs_b, cs_h, cs_r;
   int64_t sink;           // tokens [0, sink) are read by every row
   int causal;
+  int window;             // > 0: a row also skips keys below its position - window + 1
   int64_t offset;
   float scale_log2;
   void* out;
@@ -244,7 +248,9 @@ __global__ void __launch_bounds__(320, 1)
     const int32_t* ids = p.ids + b * p.ls_b + h * p.ls_h + lr * p.ls_r;
     int64_t cnt = p.n_max;
     if (p.counts) cnt = lmin(cnt, static_cast<int64_t>(p.counts[b * p.cs_b + h * p.cs_h + lr * p.cs_r]));
-    const int64_t vis = p.causal ? (pos < 0 ? -1 : pos / PK) : p.n_kb - 1;  // last visible block
+    // last visible block: key j is visible iff j * c <= pos + c - 1 (c = p.causal; c = 1 is
+    // j <= pos)
+    const int64_t vis = p.causal ? (pos < 0 ? -1 : ((pos + p.causal - 1) / p.causal) / PK) : p.n_kb - 1;
     for (int64_t i0 = 0; i0 < cnt && my_n < PLMAX; i0 += 8) {
       int32_t blk8[8];  // eight independent loads in flight
 #pragma unroll
@@ -412,6 +418,10 @@ __global__ void __launch_bounds__(320, 1)
     bool ok = true;
     const int sink32 = static_cast<int>(lmin(p.sink, int64_t(1) << 30)), tk32 = static_cast<int>(p.Tk);
     const int pos32 = static_cast<int>(lmax(lmin(pos, int64_t(1) << 30), -(int64_t(1) << 30)));
+    // keys visible from this row under the causal rule (the first lim32 of them), and
+    // with a window the first key it reads
+    const int lim32 = pos32 < 0 ? 0 : (pos32 + (p.causal > 0 ? p.causal : 1) - 1) / (p.causal > 0 ? p.causal : 1) + 1;
+    const int wlo32 = p.window > 0 ? pos32 - p.window + 1 : 0;
     for (int j = 0; j < n_steps; ++j) {
       const int sb = j & 1;
       if (!__all_sync(0xffffffffu, mbar_wait_bounded(&s_full[sb], static_cast<uint32_t>((j >> 1) & 1)))) {
@@ -424,7 +434,7 @@ __global__ void __launch_bounds__(320, 1)
       tmem_ld32(lane_addr + sb * 128 + hb * 64 + 32, sv[1]);
       tmem_wait_ld();
       // which keys of this thread's block the row reads
-      int ke = 0;
+      int ke = 0, ks = 0;
       {
         const int e = 2 * j + hb;
         const int blk = ulist[e];
@@ -438,8 +448,12 @@ __global__ void __launch_bounds__(320, 1)
         int kend = member ? PK : (e < n ? min(PK, sink32 - key0) : 0);
         if (!row_ok) kend = 0;
         kend = min(kend, tk32 - key0);
-        if (p.causal) kend = min(kend, pos32 - key0 + 1);
+        if (p.causal) kend = min(kend, lim32 - key0);
         ke = max(0, kend);
+        if (p.window > 0) {
+          ks = max(0, wlo32 - key0);  // keys [ks, ke) of the block
+          if (ks >= ke) ke = ks = 0;
+        }
       }
       // raw scores; masks only where needed (scale > 0: max of raw = max / scale).  A
       // block that no row of the warp reads is skipped: P = 0 without exponentials.
@@ -448,13 +462,13 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
       for (int i = 0; i < 8; ++i) mx8[i] = -INFINITY;
       if (none_in) {
-      } else if (ke >= PK) {
+      } else if (ke >= PK && ks == 0) {
 #pragma unroll
         for (int c = 0; c < 64; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], __uint_as_float(sv[c >> 5][c & 31]));
       } else {
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
-          const float v = c < ke ? __uint_as_float(sv[c >> 5][c & 31]) : -INFINITY;
+          const float v = c >= ks && c < ke ? __uint_as_float(sv[c >> 5][c & 31]) : -INFINITY;
           sv[c >> 5][c & 31] = __float_as_uint(v);
           mx8[c & 7] = fmaxf(mx8[c & 7], v);
         }
@@ -713,7 +727,8 @@ extern "C" int linattn_block_sparse_prefill(const void* q, int32_t dtype, int64_
                                             const void* k, const void* v, int64_t Hkv, int64_t Tk, int64_t D,
                                             const int32_t* ids, const int32_t* counts, const int64_t* id_strides,
                                             int64_t n_max, int64_t rows_per_list, const int64_t* count_strides,
-                                            int64_t sink, int32_t causal, int64_t offset, float scale, void* out,
+                                            int64_t sink, int32_t causal, int64_t window, int64_t offset,
+                                            float scale, void* out,
                                             const int64_t* out_strides, float* lse_out, const void* v_f16,
                                             const float* v_scale, int32_t* status, void* stream) {
   if (!q || !k || !v || !ids || !out || !id_strides || !out_strides)
@@ -736,6 +751,9 @@ extern "C" int linattn_block_sparse_prefill(const void* q, int32_t dtype, int64_
     return set_error(LINATTN_EUNSUPPORTED, "block_sparse_prefill: too many rows for 32-bit TMA coordinates");
   if (offset < -(int64_t(1) << 30) || offset + Tq >= (int64_t(1) << 30))
     return set_error(LINATTN_EUNSUPPORTED, "block_sparse_prefill: query positions must lie in (-2^30, 2^30)");
+  if (causal < 0 || causal > (1 << 20)) return set_error(LINATTN_EINVAL, "block_sparse_prefill: causal must be 0 .. 2^20");
+  if (window < 0 || window > (int64_t(1) << 30) || (window > 0 && sink > 0))
+    return set_error(LINATTN_EINVAL, "block_sparse_prefill: window must be 0 .. 2^30 and goes without a sink");
   if (B == 0 || Hq == 0 || Tq == 0) return LINATTN_OK;
   // q / K / V: contiguous (B, H, T, 128) rows, viewed as 2-D [rows, 128]
   const CUtensorMapDataType cu = dtype == LINATTN_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -750,7 +768,7 @@ extern "C" int linattn_block_sparse_prefill(const void* q, int32_t dtype, int64_
   p.ls_b = id_strides[0]; p.ls_h = id_strides[1]; p.ls_r = id_strides[2]; p.n_max = n_max;
   p.rows_per_list = rows_per_list;
   p.cs_b = counts ? count_strides[0] : 0; p.cs_h = counts ? count_strides[1] : 0; p.cs_r = counts ? count_strides[2] : 0;
-  p.sink = sink < 0 ? 0 : sink; p.causal = causal; p.offset = offset;
+  p.sink = sink < 0 ? 0 : sink; p.causal = causal; p.window = static_cast<int>(window); p.offset = offset;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.out = out; p.out_dtype = dtype; p.lse = lse_out; p.status = status;
   p.v_scale = v_f16 ? v_scale : nullptr;

@@ -8,16 +8,19 @@ keys (``extras["compress_ratio"]``, ``["selected_blocks"]``, ``["gate_mode"]``,
 
 * compression (``native_sparse.py:67-76``): keys / values pooled by ``csa2_pool_quant``
   at 16 bits (the mean in the cache dtype, as ``block_reduce``); the groups a query
-  reads are a prefix (those starting at or before ``p + c - 1``), so the lists are the
-  shared ids ``0 .. G-1`` with a per-query count;
+  reads are a prefix (those starting at or before ``p + c - 1``): the tcgen05 prefill
+  kernel with its pooled causal rule (``causal = c``) at head size 128 in bf16 / f16,
+  otherwise the shared ids ``0 .. G-1`` with a per-query count;
 * selection (``:78-98``): block means of k (cache dtype), fp32 scores of every query
   against them (a cuBLAS GEMM), the row top-k kernel over the blocks starting at or
   before the query, the own block merged in by ``merge_block_lists``; the selected
   blocks are read whole (no causal cut, as the reference's mask): the tcgen05 prefill
   kernel for 64-token blocks at head size 128 in bf16 / f16, the general sparse kernel
   otherwise;
-* window (``:100-105``): the token-sparse kernel's window range (bf16 / f16, head sizes
-  64 / 128) or explicit window lists for the general kernel.
+* window (``:100-105``): the tcgen05 prefill with a token-exact window bound (head size
+  128 in bf16 / f16: each 64-query block lists the key blocks its windows touch), the
+  token-sparse kernel's window range (head size 64), or explicit window lists for the
+  general kernel.
 
 Each branch writes fp32; the gates combine them and round once to the output dtype.
 A query with fewer allowed blocks than ``selected_blocks`` reads its allowed blocks
@@ -98,6 +101,14 @@ class CudaNSAAttention(AttentionVariant):
         counts = torch.clamp((pos + c - 1).div(c, rounding_mode="floor") + 1, min=1, max=n_groups)
         counts = counts.to(torch.int32).view(1, 1, tq).expand(b, hkv, tq)
         ids = torch.arange(n_groups, dtype=torch.int32, device=q.device).view(1, 1, n_groups).expand(b, hkv, n_groups)
+        n_blk = -(-n_groups // 64)
+        if d == 128 and q.dtype in (torch.bfloat16, torch.float16) and kc.dtype == q.dtype and n_blk <= 64:
+            # tensor cores: every 128-query tile reads the pooled blocks once; the prefill
+            # kernel's causal rule with c = compress_ratio is exactly this prefix
+            blocks = torch.arange(n_blk, dtype=torch.int32, device=q.device).view(1, 1, 1, n_blk)
+            res = block_sparse_prefill(q, kc, vc, blocks.expand(b, hq, 1, n_blk), rows_per_list=max(tq, 1),
+                                       causal=c, offset=offset)
+            return res if out is None else out.copy_(res)
         if _token_kernel_ok(q, kc):
             res = token_sparse_attention(q, kc, vc, ids, counts=counts, block=1, causal=False, diag_fallback=False)
             return res if out is None else out.copy_(res)
@@ -124,6 +135,21 @@ class CudaNSAAttention(AttentionVariant):
         b, hq, tq, _ = q.shape
         hkv, tk = k.shape[1], k.shape[2]
         w = self.cfg.window_size
+        n_span = -(-max(w, 1) // 64) + 2  # key blocks a 64-query block's windows can touch
+        if (w > 0 and q.shape[-1] == 128 and q.dtype in (torch.bfloat16, torch.float16) and k.dtype == q.dtype
+                and n_span <= 64):
+            # tensor cores: per 64-query block the key blocks of [first - w + 1, last], each
+            # row cut to its own window by the kernel
+            n_qb, n_kb = -(-tq // 64), -(-tk // 64)
+            first = offset + torch.arange(n_qb, device=q.device) * 64
+            last = torch.clamp(first + 63, max=offset + tq - 1)
+            lo = torch.clamp((first - w + 1).div(64, rounding_mode="floor"), min=0)
+            hi = torch.clamp(last.div(64, rounding_mode="floor"), max=n_kb - 1)
+            ids = lo[:, None] + torch.arange(n_span, device=q.device)
+            ids = torch.where(ids <= hi[:, None], ids, torch.full_like(ids, -1)).to(torch.int32)
+            res = block_sparse_prefill(q, k, v, ids.view(1, 1, n_qb, n_span).expand(b, hq, n_qb, n_span),
+                                       rows_per_list=64, causal=True, window=w, offset=offset)
+            return res if out is None else out.copy_(res)
         if _token_kernel_ok(q, k):
             none = torch.full((b, hkv, 1), -1, dtype=torch.int32, device=q.device)
             res = token_sparse_attention(q, k, v, none, block=1, window=w, causal=True, offset=offset,

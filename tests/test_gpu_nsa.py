@@ -118,8 +118,10 @@ def test_cuda_nsa_fit_gates_golden(cuda):
 
 @pytest.mark.parametrize("d,block,selected", [(128, 64, 2), (64, 16, 3)])
 def test_cuda_nsa_bf16_paths(cuda, d, block, selected):
-    """bf16: compression and window branches on the token-sparse kernel, selection on the
-    tcgen05 prefill kernel (64-token blocks, D = 128) or the general kernel; each branch
+    """bf16: the compression branch on the tcgen05 prefill with its pooled causal rule
+    (D = 128) or the token-sparse kernel (D = 64), the window branch on the token-sparse
+    kernel, selection on the tcgen05 prefill (64-token blocks, D = 128) or the general
+    kernel; each branch
     against float64 attention (pooled rows rounded to bf16 as the reference pools), the
     lists against the oracle's selection on rows without a near-tie."""
     from linattn_b200 import build
@@ -161,3 +163,45 @@ def test_cuda_nsa_bf16_paths(cuda, d, block, selected):
     mixed = (o_cmp + ref + o_win) / 3.0
     assert np.all(np.abs(_np(out) - mixed) <= 4e-3 + 2.0 ** -8 * np.abs(mixed))
     del o_slc_oracle
+
+
+@pytest.mark.parametrize("c,offset", [(3, 5), (16, 0), (1, 7)])
+def test_prefill_pooled_causal_rule(cuda, c, offset):
+    """``block_sparse_prefill(causal=c)``: key j read by the query at p iff
+    j * c <= p + c - 1 (c = 1: the usual causal rule), with a partial last block."""
+    from linattn_b200.blocks import block_sparse_prefill
+
+    gen = torch.Generator().manual_seed(c + offset)
+    b, hq, hkv, tq, tk, d = 1, 4, 2, 200, 100, 128
+    q = torch.randn(b, hq, tq, d, generator=gen).bfloat16()
+    k, v = (torch.randn(b, hkv, tk, d, generator=gen).bfloat16() for _ in range(2))
+    n_blk = -(-tk // 64)
+    ids = torch.arange(n_blk, dtype=torch.int32).view(1, 1, 1, n_blk).expand(b, hq, 1, n_blk)
+    out = block_sparse_prefill(q.to(cuda), k.to(cuda), v.to(cuda), ids.to(cuda), rows_per_list=tq, causal=c,
+                               offset=offset)
+    pos = (np.arange(tq) + offset)[:, None]
+    allow = np.broadcast_to(np.arange(tk)[None, :] * c <= pos + c - 1, (b, hq, tq, tk))
+    ref = dense_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), causal=False, mask=allow)
+    assert np.all(np.abs(_np(out) - ref) <= 2e-3 + 2.0 ** -8 * np.abs(ref)), np.abs(_np(out) - ref).max()
+
+
+@pytest.mark.parametrize("w,offset,tq", [(40, 7, 200), (100, 0, 257), (1, 3, 70)])
+def test_prefill_window_rule(cuda, w, offset, tq):
+    """``block_sparse_prefill(window=w)``: the query at p reads keys [p - w + 1, p] of its
+    listed blocks (the NSA window branch's read set), per-64-row block lists."""
+    from linattn_b200.blocks import block_sparse_prefill
+
+    gen = torch.Generator().manual_seed(w + offset)
+    b, hq, hkv, d = 1, 4, 2, 128
+    tk = offset + tq
+    q = torch.randn(b, hq, tq, d, generator=gen).bfloat16()
+    k, v = (torch.randn(b, hkv, tk, d, generator=gen).bfloat16() for _ in range(2))
+    n_kb, n_qb = -(-tk // 64), -(-tq // 64)
+    ids = torch.arange(n_kb, dtype=torch.int32).view(1, 1, 1, n_kb).expand(b, hq, n_qb, n_kb)  # every block
+    out = block_sparse_prefill(q.to(cuda), k.to(cuda), v.to(cuda), ids.contiguous().to(cuda), rows_per_list=64,
+                               causal=True, window=w, offset=offset)
+    pos = (np.arange(tq) + offset)[:, None]
+    kj = np.arange(tk)[None, :]
+    allow = np.broadcast_to((kj <= pos) & (pos - kj < w), (b, hq, tq, tk))
+    ref = dense_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), causal=False, mask=allow)
+    assert np.all(np.abs(_np(out) - ref) <= 2e-3 + 2.0 ** -8 * np.abs(ref)), np.abs(_np(out) - ref).max()
