@@ -309,6 +309,8 @@ cudaError_t launch_hd(int H, int D, const IndexerMmaParams& p, const CUtensorMap
   LINATTN_IDX_CASE(2, 128)
   LINATTN_IDX_CASE(4, 32)
   LINATTN_IDX_CASE(8, 32)
+  LINATTN_IDX_CASE(4, 16)
+  LINATTN_IDX_CASE(8, 16)
 #undef LINATTN_IDX_CASE
   return cudaErrorInvalidValue;
 }
@@ -328,7 +330,8 @@ bool indexer_scores_mma(const void* q, int q_dtype, const int64_t* qs, const voi
   if (!fp8 && k_dtype != q_dtype) return false;
   const int keb = fp8 ? 1 : 2;
   const bool shape_ok = (H == 1 && D == 64) || (H == 2 && D == 64) || (H == 4 && D == 64) || (H == 1 && D == 128) ||
-                        (H == 2 && D == 128) || (H == 4 && D == 32) || (H == 8 && D == 32);
+                        (H == 2 && D == 128) || (H == 4 && D == 32) || (H == 8 && D == 32) ||
+                        (H == 4 && D == 16) || (H == 8 && D == 16);  // CSA2 / DSA plugin indexer shapes
   if (!shape_ok || (H * D * keb) % 128 != 0) return false;
   if (ks[3] != 1 || ks[2] != D || ks[1] != H * D || (B > 1 && ks[0] != Tk * H * D)) return false;
   if (reinterpret_cast<uintptr_t>(k) % 16 != 0 || B * Tk >= (int64_t(1) << 31) - XK) return false;
