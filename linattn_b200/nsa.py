@@ -12,7 +12,7 @@ keys (``extras["compress_ratio"]``, ``["selected_blocks"]``, ``["gate_mode"]``,
   kernel with its pooled causal rule (``causal = c``) at head size 128 in bf16 / f16,
   otherwise the shared ids ``0 .. G-1`` with a per-query count;
 * selection (``:78-98``): block means of k (cache dtype), fp32 scores of every query
-  against them (a cuBLAS GEMM), the row top-k kernel over the blocks starting at or
+  against them (a cuBLAS GEMM: 16-bit operands with fp32 accumulation and output), the row top-k kernel over the blocks starting at or
   before the query, the own block merged in by ``merge_block_lists``; the selected
   blocks are read whole (no causal cut, as the reference's mask): the tcgen05 prefill
   kernel for 64-token blocks at head size 128 in bf16 / f16, the general sparse kernel
@@ -60,7 +60,15 @@ def nsa_select(q: torch.Tensor, k: torch.Tensor, block: int, selected: int, *,
     kp = csa2_pool_quant(k, block, 16)  # block_reduce in the cache dtype
     nkb = kp.shape[2]
     g = hq // hkv
-    scores = torch.matmul(q.float().reshape(b, hkv, g * tq, d), kp.float().transpose(-1, -2)).view(b, hq, tq, nkb)
+    if q.dtype in (torch.bfloat16, torch.float16) and kp.dtype == q.dtype:
+        # 16-bit operands, fp32 accumulation and output on the tensor cores: the products
+        # of two 16-bit values are exact in fp32, so the scores are the fp32 GEMM's up to
+        # the order of the sums
+        scores = torch.bmm(q.reshape(b * hkv, g * tq, d), kp.reshape(b * hkv, nkb, d).transpose(1, 2),
+                           out_dtype=torch.float32).view(b, hq, tq, nkb)
+    else:
+        scores = torch.matmul(q.float().reshape(b, hkv, g * tq, d),
+                              kp.float().transpose(-1, -2)).view(b, hq, tq, nkb)
     scores.mul_(1.0 / math.sqrt(d))
     kk = max(1, min(selected, nkb))
     # block j is allowed for the query at p iff j * block <= p
