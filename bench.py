@@ -480,99 +480,150 @@ def run_variants_workload(args):
 
 
 # ---------------------------------------------------------------------------------
-# CPU baselines (rank 0, N == 1 / reference arm): bounded samples of the workload
+# CPU baselines: the reference's own torch operators on the host cores
 # ---------------------------------------------------------------------------------
-def _cpu_sample(cache, q, n_seq: int):
-    """Host copies of sequences [0, n_seq): contiguous logical pages, bf16 bits."""
-    tab = cache.page_table[:n_seq].long()
-    kp = cache.k_pool[tab.flatten()].view(torch.int16).cpu().numpy()  # (n_seq*n_pages, Hkv, P, D)
-    vp = cache.v_pool[tab.flatten()].view(torch.int16).cpu().numpy()
-    # metadata is stored per sequence in logical page order: (n_seq, H_kv, pages, D)
-    mn = cache.meta_min[:n_seq].transpose(1, 2).contiguous().view(torch.int16).cpu().numpy()
-    mx = cache.meta_max[:n_seq].transpose(1, 2).contiguous().view(torch.int16).cpu().numpy()
-    qh = q[:n_seq, :, 0].contiguous().view(torch.int16).cpu().numpy()
-    return kp, vp, mn, mx, qh
+REF_DIR = ROOT / "baseline" / "_ref"
+
+
+def reference_ops():
+    """The reference's CPU torch operators for the Quest decode path, imported from
+    its unmodified install in ``baseline/_ref`` (never this library):
+    ``page_bounds_torch`` / ``page_select_torch`` (``kernels/triton/quest_pages.py:38-78``)
+    and ``block_sparse_attention_torch`` (``kernels/triton/block_sparse.py:40-75``)."""
+    if not (REF_DIR / "linattn" / "__init__.py").exists():
+        return None
+    if str(REF_DIR) not in sys.path:
+        sys.path.insert(0, str(REF_DIR))
+    from linattn.kernels.triton.block_sparse import block_sparse_attention_torch
+    from linattn.kernels.triton.quest_pages import page_bounds_torch, page_select_torch
+
+    return page_bounds_torch, page_select_torch, block_sparse_attention_torch
+
+
+def reference_quest_step(ops, q, k, v, mins, maxs, page: int, topk: int, sink_pages: int, group: int):
+    """One config-2 decode step through the reference's operators, fp32 on the CPU:
+    the per-page bounds are repeated over each kv group's query heads (as
+    ``QuestAttention.page_scores`` does with ``repeat_kv``, ``variants/selection.py:203-212``),
+    ``page_select_torch`` takes the top-``topk`` pages with the query's own (last) page
+    forced, the sink page is forced the same way (it replaces the lowest-ranked pick
+    when it is not already chosen), the heads of a group read the union of their
+    pages (``selection.py:232-235``), and ``block_sparse_attention_torch`` attends over
+    the union (padding ids point past the end and are masked by the operator)."""
+    _, page_select_torch, block_sparse_attention_torch = ops
+    b, hq, _, d = q.shape
+    hkv, t = k.shape[1], k.shape[2]
+    n_pages = mins.shape[2]
+    ids, _ = page_select_torch(q, mins.repeat_interleave(group, dim=1), maxs.repeat_interleave(group, dim=1), page,
+                               topk, offset=t - 1)
+    ids = ids[:, :, 0]                                                   # (B, Hq, topk), score order
+    if sink_pages:
+        assert sink_pages == 1
+        ids[..., -1] = torch.where((ids == 0).any(-1), ids[..., -1], torch.zeros_like(ids[..., -1]))
+    sel = torch.zeros(b, hq, n_pages, dtype=torch.bool).scatter_(-1, ids, True)
+    union = sel.view(b, hkv, group, n_pages).any(2)                      # (B, Hkv, n_pages)
+    n_max = int(union.sum(-1).max())
+    order = torch.where(union, torch.arange(n_pages), torch.full((), n_pages)).sort(-1).values[..., :n_max]
+    out = block_sparse_attention_torch(q, k, v, order, block_size=page)
+    return out, union
+
+
+def build_c2_host(seed: int, n_q: int, batch: int, threads: int):
+    """The config-2 workload built on the host (numpy, no GPU): the same construction
+    as ``build_c2`` (N(0,1) K/V rounded to bf16, 1% needle pages with
+    0.3*sqrt(D)*(unit group q direction) added to their keys, queries around a base
+    query) from host generators; contiguous ``(B, H_kv, T, D)`` fp32 tensors holding
+    bf16 values, the reference's layout (it has no page table)."""
+    c = C2
+    b, hq, hkv, d, t, p = batch, c["Hq"], c["Hkv"], c["D"], c["T"], c["P"]
+    group = hq // hkv
+    n_pages = t // p
+
+    def bf16_round(x):
+        u = x.view(np.uint32)
+        u += np.uint32(0x7FFF) + ((u >> 16) & np.uint32(1))
+        u &= np.uint32(0xFFFF0000)
+        return x
+
+    seqs = np.random.SeedSequence(seed).spawn(2 * b * hkv + 1)
+    kv = np.empty((2, b, hkv, t, d), dtype=np.float32)
+
+    def fill(i):
+        x = kv.reshape(2 * b * hkv, t, d)[i]
+        np.random.default_rng(seqs[i]).standard_normal(out=x, dtype=np.float32)
+        bf16_round(x)
+    with ThreadPoolExecutor(threads) as ex:
+        list(ex.map(fill, range(2 * b * hkv)))
+    rng = np.random.default_rng(seqs[-1])
+    q0 = rng.standard_normal((b, hq, d), dtype=np.float32)
+    u = q0.reshape(b, hkv, group, d).sum(2)
+    u /= np.linalg.norm(u, axis=-1, keepdims=True)
+    n_needle = max(1, int(round(c["needle_frac"] * n_pages)))
+    k = kv[0]
+    for bi in range(b):
+        for pg in rng.permutation(n_pages)[:n_needle]:
+            blk = k[bi, :, pg * p:(pg + 1) * p]
+            blk += (0.3 * math.sqrt(d)) * u[bi][:, None, :]
+            bf16_round(blk)
+    qs = q0[None] + 0.25 * rng.standard_normal((n_q, b, hq, d), dtype=np.float32)
+    bf16_round(qs)
+    return (torch.from_numpy(kv[0]), torch.from_numpy(kv[1]),
+            torch.from_numpy(np.ascontiguousarray(qs)).view(n_q, b, hq, 1, d))
 
 
 def cpu_reference_step_fn(cache, q, n_seq: int, threads: int):
-    """Returns (fn, kind, description): fn() runs one CPU step over the sample.
-
-    Selection = the oracle's C restatement (oracle/c/oracle.c, the reference's page
-    selection is torch code); attention = the reference's own C kernel
-    ``paged_decode_tiled`` (src/linattn/kernels/c/decode_attn.c:72-133, compiled to
-    oracle/_ref) over each query head's union pages on fp32 contiguous K/V, the
-    layout that kernel takes.  Without oracle/_ref the C oracle does both ("port").
-    """
+    """Returns (fn, kind, description): fn() runs one CPU step over a sample of this
+    run's own config-2 data (sequences [0, n_seq), host copies in the reference's
+    contiguous fp32 layout).  With the reference installed (``baseline/_ref``) the step
+    is ``reference_quest_step`` (kind "reference"); without it, the oracle's C
+    restatement of the same step (kind "port")."""
     c = C2
     hq, hkv, d, p, t = c["Hq"], c["Hkv"], c["D"], c["P"], c["T"]
     n_pages = t // p
     group = hq // hkv
-    kp, vp, mn, mx, qh = _cpu_sample(cache, q, n_seq)
+    tab = cache.page_table[:n_seq].long().flatten()
+    kp = cache.k_pool[tab].float().cpu()                       # (n_seq*n_pages, Hkv, P, D)
+    vp = cache.v_pool[tab].float().cpu()
+    k = kp.view(n_seq, n_pages, hkv, p, d).transpose(1, 2).reshape(n_seq, hkv, t, d).contiguous()
+    v = vp.view(n_seq, n_pages, hkv, p, d).transpose(1, 2).reshape(n_seq, hkv, t, d).contiguous()
+    qf = q[:n_seq].float().cpu().contiguous()
+    ops = reference_ops()
+    torch.set_num_threads(threads)
+    if ops is not None:
+        mins, maxs = ops[0](k, p)
+
+        def reference():
+            reference_quest_step(ops, qf, k, v, mins, maxs, p, c["topk"], c["sink_pages"], group)
+        return reference, "reference", (
+            f"{n_seq} of 16 sequences per step through the reference's torch operators (page_select_torch with the "
+            f"sink forced, GQA union, block_sparse_attention_torch), fp32 on contiguous K/V, {threads} threads")
     ora = ctypes.CDLL(str(ROOT / "oracle" / "_build" / "liboracle.so"))
     ora.oracle_quest_decode.restype = ctypes.c_int
+    to_bits = lambda x: x.to(torch.bfloat16).view(torch.int16).numpy()  # noqa: E731
+    kb = to_bits(kp)
+    vb = to_bits(vp)
+    mn = to_bits(cache.meta_min[:n_seq].transpose(1, 2).contiguous().float().cpu())
+    mx = to_bits(cache.meta_max[:n_seq].transpose(1, 2).contiguous().float().cpu())
+    qh = to_bits(qf[:, :, 0].contiguous())
     table = np.arange(n_seq * n_pages, dtype=np.int32).reshape(n_seq, n_pages)
     lens = np.full(n_seq, t, dtype=np.int32)
     max_union = min(group * c["topk"], n_pages)
     out = np.zeros((n_seq, hq, d), dtype=np.float32)
     uids = np.zeros((n_seq, hkv, max_union), dtype=np.int32)
     ucnt = np.zeros((n_seq, hkv), dtype=np.int32)
-    scale = 1.0 / math.sqrt(d)
     P_ = ctypes.c_void_p
+    pool = ThreadPoolExecutor(threads)
 
-    def run_units(u0, u1):
-        return ora.oracle_quest_decode(2, P_(qh.ctypes.data), P_(kp.ctypes.data), P_(vp.ctypes.data),
+    def run_unit(u):
+        return ora.oracle_quest_decode(2, P_(qh.ctypes.data), P_(kb.ctypes.data), P_(vb.ctypes.data),
                                        P_(mn.ctypes.data), P_(mx.ctypes.data), P_(table.ctypes.data),
                                        P_(lens.ctypes.data), n_seq, hq, hkv, d, p, n_pages, c["topk"],
-                                       c["sink_pages"], ctypes.c_float(scale), P_(out.ctypes.data),
-                                       P_(uids.ctypes.data), P_(ucnt.ctypes.data), max_union, u0, u1)
+                                       c["sink_pages"], ctypes.c_float(1.0 / math.sqrt(d)), P_(out.ctypes.data),
+                                       P_(uids.ctypes.data), P_(ucnt.ctypes.data), max_union, u, u + 1)
 
-    pool = ThreadPoolExecutor(threads)
-    units = n_seq * hkv
-    ref_lib = ROOT / "oracle" / "_ref" / "libdecode_attn.so"
-    if not ref_lib.exists():
-        def port():
-            list(pool.map(lambda u: run_units(u, u + 1), range(units)))
-        return port, "port", (f"{n_seq} of 16 sequences per step, full selection + attention in the C oracle "
-                              f"(oracle/c/oracle.c), {threads} threads")
-    ref = ctypes.CDLL(str(ref_lib))
-    f32p = ctypes.POINTER(ctypes.c_float)
-    i32p = ctypes.POINTER(ctypes.c_int32)
-    ref.paged_decode_tiled.argtypes = [f32p, f32p, f32p, i32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
-                                       ctypes.c_int, ctypes.c_float, f32p]
-    # the reference kernel's storage: fp32 contiguous (T, D) per (sequence, kv head)
-    def bf16_to_f32(a):
-        return (a.astype(np.uint16).astype(np.uint32) << 16).view(np.float32)
-
-    kf = bf16_to_f32(kp).reshape(n_seq, n_pages, hkv, p, d).transpose(0, 2, 1, 3, 4).reshape(n_seq, hkv, t, d).copy()
-    vf = bf16_to_f32(vp).reshape(n_seq, n_pages, hkv, p, d).transpose(0, 2, 1, 3, 4).reshape(n_seq, hkv, t, d).copy()
-    qf = bf16_to_f32(qh).reshape(n_seq, hq, d).copy()
-    out_ref = np.zeros((n_seq, hq, d), dtype=np.float32)
-
-    def ref_head(idx):
-        bi, h = divmod(idx, hq)
-        kh = h // group
-        ids = np.ascontiguousarray(uids[bi, kh, : ucnt[bi, kh]])
-        ref.paged_decode_tiled(qf[bi, h].ctypes.data_as(f32p), kf[bi, kh].ctypes.data_as(f32p),
-                               vf[bi, kh].ctypes.data_as(f32p), ids.ctypes.data_as(i32p), int(ids.size), p, d, t,
-                               ctypes.c_float(scale), out_ref[bi, h].ctypes.data_as(f32p))
-
-    ora.oracle_quest_select.restype = ctypes.c_int
-
-    def select_units(u0, u1):
-        return ora.oracle_quest_select(2, P_(qh.ctypes.data), P_(mn.ctypes.data), P_(mx.ctypes.data),
-                                       P_(table.ctypes.data), P_(lens.ctypes.data), n_seq, hq, hkv, d, p, n_pages,
-                                       c["topk"], c["sink_pages"], P_(uids.ctypes.data), P_(ucnt.ctypes.data),
-                                       max_union, u0, u1)
-
-    def reference():
-        list(pool.map(lambda u: select_units(u, u + 1), range(units)))  # page selection (C oracle)
-        list(pool.map(ref_head, range(n_seq * hq)))                      # the reference's C decode kernel
-
-    return reference, "reference", (
-        f"{n_seq} of 16 sequences per step; page selection in the C oracle (oracle/c/oracle.c, the reference's "
-        f"selection is torch code) and attention with the reference's own paged_decode_tiled (decode_attn.c, "
-        f"compiled from the reference source into oracle/_ref) on fp32 contiguous K/V, one call per query head; "
-        f"{threads} threads")
+    def port():
+        list(pool.map(run_unit, range(n_seq * hkv)))
+    return port, "port", (f"{n_seq} of 16 sequences per step, selection + attention in the C oracle "
+                          f"(oracle/c/oracle.c), {threads} threads")
 
 
 def time_cpu(fn, min_seconds: float, max_iters: int = 1000):
@@ -899,21 +950,72 @@ def run_c5(args, rank, world, local_rank):
     }
 
 
+def _cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def reference_bench_decode(threads: int):
+    """The reference's ``bench/bench_decode.py`` as shipped (from its copy in
+    ``baseline/_ref``; it pins min(4, threads) torch threads itself), its printed
+    records parsed."""
+    import subprocess
+
+    script = REF_DIR / "bench" / "bench_decode.py"
+    if not script.exists():
+        return {"unavailable": "baseline/_ref/bench/bench_decode.py not installed"}
+    env = dict(os.environ, PYTHONPATH=str(REF_DIR), OMP_NUM_THREADS=str(threads))
+    res = subprocess.run([sys.executable, str(script)], capture_output=True, text=True, env=env, timeout=600)
+    import re
+
+    recs = []
+    pat = re.compile(r"^(\S+)\s+entries=\s*(\d+)\s+bytes=\s*([\d.]+) MiB\s+([\d.]+) ms\s+([\d.]+) GiB/s")
+    for line in res.stdout.splitlines():
+        m = pat.match(line.strip())
+        if m:
+            recs.append({"policy": m.group(1), "kv_entries": int(m.group(2)), "mib": float(m.group(3)),
+                         "ms": float(m.group(4)), "gib_s": float(m.group(5))})
+    return {"cmd": "python bench/bench_decode.py (defaults: --seq 65536 --dim 64 --page 16 --budgets 256 1024 2048 "
+                   "8192 --repeat 5)", "rc": res.returncode, "torch_threads": min(4, threads), "records": recs}
+
+
 def run_reference(args):
-    """Reference arm: the reference's CPU path on the host cores, bounded samples."""
-    device = torch.device("cuda", 0)
+    """Reference arm: the reference's own CPU torch path for the config-2 step on the
+    host cores (all of them), over the whole config (16 sequences of 65536 tokens),
+    with inputs built on the host; this library is not imported in this process."""
+    ops = reference_ops()
     c = C2
-    cache, qs = build_c2(device, 1234, args.warmup + args.steps)
     threads = os.cpu_count() or 1
-    n_seq = 2
-    fn, kind, desc = cpu_reference_step_fn(cache, qs[0], n_seq, threads)
-    for _ in range(args.warmup):
-        fn()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        fn()
-    sec = (time.perf_counter() - t0) / args.steps
-    value = n_seq / sec
+    if ops is None:
+        return {"impl": "reference", "unavailable": "the reference is not installed in baseline/_ref"}
+    torch.set_num_threads(threads)
+    t_build = time.perf_counter()
+    k, v, qs = build_c2_host(1234, args.warmup + args.steps, c["B"], threads)
+    mins, maxs = ops[0](k, c["P"])  # maintained on append in a serving loop: outside the step
+    build_s = time.perf_counter() - t_build
+    group = c["Hq"] // c["Hkv"]
+
+    def step(i):
+        return reference_quest_step(ops, qs[i], k, v, mins, maxs, c["P"], c["topk"], c["sink_pages"], group)
+    for i in range(args.warmup):
+        step(i)
+    times = []
+    pages = []
+    for i in range(args.steps):
+        t0 = time.perf_counter()
+        _, union = step(args.warmup + i)
+        times.append(time.perf_counter() - t0)
+        pages.append(float(union.sum()) / (c["B"] * c["Hkv"]))
+    sec = statistics.mean(times)
+    value = c["B"] / sec
+    desc = (f"the whole config-2 step (16 sequences) per timed step through the reference's torch operators: "
+            f"page_select_torch (own page forced, sink page forced in its place), the GQA union, "
+            f"block_sparse_attention_torch; fp32 on contiguous K/V holding bf16 values; {threads} torch threads")
     return {
         "impl": "reference",
         "metric": METRIC,
@@ -926,13 +1028,21 @@ def run_reference(args):
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "bf16",
-        "data": "synthetic (same generator and seed as the CUDA arm)",
-        "config": {"workload": "quest_decode_c2", "batch_per_gpu": c["B"], "seq_len": c["T"], "page_size": c["P"],
-                   "n_heads": c["Hq"], "n_kv_heads": c["Hkv"], "head_dim": c["D"], "budget_pages": c["topk"],
-                   "sample_sequences_per_step": n_seq},
-        "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": threads, "kind": kind, "sample": desc},
+        "dtype": "fp32 (bf16 values widened exactly)",
+        "data": "synthetic, built on the host: the CUDA arm's construction (N(0,1) bf16 K/V, 1% needle pages, "
+                "queries around a base query) from numpy generators; contiguous layout (the reference has no page "
+                "table)",
+        "config": {"workload": "quest_decode_c2", "batch_per_gpu": c["B"], "global_batch": c["B"], "seq_len": c["T"],
+                   "page_size": c["P"], "n_heads": c["Hq"], "n_kv_heads": c["Hkv"], "head_dim": c["D"],
+                   "budget_pages": c["topk"], "sink_pages": c["sink_pages"], "parallelism": "host cores"},
+        "pages_per_kv_head": round(statistics.mean(pages), 2),
+        "build_s": round(build_s, 1),
+        "host": {"cpu": _cpu_model(), "cores": threads, "torch_threads": torch.get_num_threads()},
+        "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": threads,
+                         "kind": "reference (torch: page_select_torch + block_sparse_attention_torch)",
+                         "sample": desc},
         "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "bench_decode_as_shipped": reference_bench_decode(threads),
     }
 
 

@@ -2,7 +2,9 @@
  * linattn_b200 — C ABI of the B200 (sm_100a) sparse-attention hot path.
  *
  * Plain pointers and sizes only.  Every buffer is device memory owned by the
- * caller; the library allocates nothing.  Kernels are enqueued on the caller's
+ * caller, workspaces included; the library allocates nothing on a call.  The one
+ * exception is linattn_sparse_attention_noalloc, whose scratch is a fixed
+ * library-owned device array (see its declaration).  Kernels are enqueued on the caller's
  * `stream` (a cudaStream_t passed as void*; NULL = legacy default stream).
  * Functions return LINATTN_OK or an error code; linattn_last_error() gives the
  * message (thread-local).  Device-side problems (a page id outside the page
@@ -319,8 +321,9 @@ int64_t linattn_sparse_attention_noalloc_limit(void);
  * invisible keys score -inf; causal = 2: the same inside each 64-key tile that holds a
  * visible key, while tiles after every query of a 64-query block are left unwritten
  * (for a causal top-k, which never reads them).  H_I * D <= 512.  16-bit queries
- * with fp8 keys (or keys of the query's type), D in {32, 64, 128}, H_I * D <= 256 and
- * contiguous (B, T_k, H_I, D) keys run on the tensor cores.  status: device
+ * with fp8 keys (or keys of the query's type) run on the tensor cores for
+ * (H_I, D) in {(1|2|4, 64), (1|2, 128), (4|8, 32), (4|8, 16)} with contiguous
+ * (B, T_k, H_I, D) keys.  status: device
  * status word (LINATTN_DEV_TIMEOUT if a tile copy never arrives), may be NULL.
  * Replaces indexer_scores_torch (src/linattn/kernels/triton/fused_indexer.py:52-60) and
  * the score pass of _indexer_block_max_kernel / _indexer_gather_kernel (:80-171).

@@ -13,7 +13,6 @@ ABI of ``include/linattn_b200.h``; there is no CPU fallback.
 from linattn_b200.block_sparse import block_sparse_attention, sparse_attention  # noqa: F401
 from linattn_b200.core import AttnConfig, AttentionVariant  # noqa: F401
 from linattn_b200.csa2 import CudaCSA2Attention, csa2_pool_quant  # noqa: F401
-from linattn_b200.csa2_stack import CrossLayerPlan, CSA2Stack, CSA2StackConfig, compare_share  # noqa: F401
 from linattn_b200.nsa import CudaNSAAttention, nsa_select  # noqa: F401
 from linattn_b200.indexer import indexer_scores, indexer_topk, quantize_keys_fp8, row_topk  # noqa: F401
 from linattn_b200.merge import lse_combine  # noqa: F401

@@ -250,7 +250,9 @@ __global__ void __launch_bounds__(320, 1)
     if (p.counts) cnt = lmin(cnt, static_cast<int64_t>(p.counts[b * p.cs_b + h * p.cs_h + lr * p.cs_r]));
     // last visible block: key j is visible iff j * c <= pos + c - 1 (c = p.causal; c = 1 is
     // j <= pos)
-    const int64_t vis = p.causal ? (pos < 0 ? -1 : ((pos + p.causal - 1) / p.causal) / PK) : p.n_kb - 1;
+    // (so for c > 1 key 0 is already visible from -c < pos < 0)
+    const int64_t vis =
+        p.causal ? (pos + p.causal - 1 < 0 ? -1 : ((pos + p.causal - 1) / p.causal) / PK) : p.n_kb - 1;
     for (int64_t i0 = 0; i0 < cnt && my_n < PLMAX; i0 += 8) {
       int32_t blk8[8];  // eight independent loads in flight
 #pragma unroll
@@ -420,7 +422,8 @@ __global__ void __launch_bounds__(320, 1)
     const int pos32 = static_cast<int>(lmax(lmin(pos, int64_t(1) << 30), -(int64_t(1) << 30)));
     // keys visible from this row under the causal rule (the first lim32 of them), and
     // with a window the first key it reads
-    const int lim32 = pos32 < 0 ? 0 : (pos32 + (p.causal > 0 ? p.causal : 1) - 1) / (p.causal > 0 ? p.causal : 1) + 1;
+    const int cc = p.causal > 0 ? p.causal : 1;
+    const int lim32 = pos32 + cc - 1 < 0 ? 0 : (pos32 + cc - 1) / cc + 1;
     const int wlo32 = p.window > 0 ? pos32 - p.window + 1 : 0;
     for (int j = 0; j < n_steps; ++j) {
       const int sb = j & 1;

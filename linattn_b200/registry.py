@@ -3,8 +3,8 @@
 The reference builds backend-native variants by name through ``KERNEL_VARIANTS``
 (``<backend>_<variant>``, ``src/linattn/registry.py:139-146``) and ``build``
 (``registry.py:225-236``), today only for ``mlx_``.  This module provides the same
-API for the CUDA backend; ``INTEGRATION.md`` shows the three lines the reference
-registry needs to dispatch ``cuda_*`` names here.
+API for the CUDA backend: a reference registry dispatches a ``cuda_*`` name here by
+calling ``build_cuda(name, cfg)`` from its ``build`` when the prefix matches.
 """
 
 from __future__ import annotations

@@ -386,52 +386,17 @@ def make_nsa_variant(out):
     np.savez_compressed(out / "nsa_variant.npz", **rec)
 
 
-def make_csa2_stack(out):
-    import torch
-    from linattn.core import AttnConfig
-    from linattn.harness import structured_inputs
-    from linattn.kv.csa2 import CSA2Stack, CSA2StackConfig, compare_share
-
-    attn = AttnConfig(n_heads=4, n_kv_heads=2, head_dim=32, seed=5)
-    cfg = CSA2StackConfig(n_layers=4, layer_group=2, compress_ratio=8, bits=4, topk_groups=3, window=24)
-    # neighbouring layers correlated: a shared draw plus a per-layer perturbation
-    base = structured_inputs(1, 4, 96, 32, kv_heads=2, seed=21)
-    qs, ks, vs = [], [], []
-    for layer in range(4):
-        pert = structured_inputs(1, 4, 96, 32, kv_heads=2, seed=40 + layer)
-        qs.append(base[0] + 0.3 * pert[0])
-        ks.append(base[1] + 0.3 * pert[1])
-        vs.append(base[2] + 0.3 * pert[2])
-    q, k, v = (torch.stack(x).float() for x in (qs, ks, vs))
-    rec = {"fn": "CSA2Stack", "q": _np(q), "k": _np(k), "v": _np(v)}
-    stack = CSA2Stack(cfg, attn)
-    res = stack.run(q, k, v)
-    rec["out"] = _np(res["out"])
-    rec["reads_per_query"] = float(res["reads_per_query"])
-    rec["copies"] = int(res["copies"])
-    rec["bytes_per_token"] = float(res["bytes_per_token"])
-    rec["spec"] = np.array(res["spec"])
-    with torch.no_grad():
-        for layer in range(4):
-            src = stack.plan.representative(layer)
-            kc, _ = stack.layer.compressed_kv(k[src], v[src])
-            rec[f"scores_l{layer}"] = _np(stack.layer.indexer_scores(q[layer], kc))
-            kc_own, _ = stack.layer.compressed_kv(k[layer], v[layer])
-            rec[f"scores_own_l{layer}"] = _np(stack.layer.indexer_scores(q[layer], kc_own))
-    cmp = compare_share(cfg, attn, q, k, v)
-    for key, val in cmp.items():
-        rec[f"cmp_{key}"] = float(val)
-    np.savez_compressed(out / "csa2_stack.npz", **rec)
-
-
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("LINATTN_REF", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("LINATTN_REF"),
+                    help="root of the reference checkout (default: $LINATTN_REF)")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("the reference checkout is required: pass --ref or set LINATTN_REF")
     _import_reference(Path(args.ref))
     for fn in (make_page_bounds, make_page_select, make_topk_ties, make_quest_variant, make_block_sparse,
                make_indexer, make_dense, make_block_selectors, make_quant, make_paged_decode, make_dsa_variant,
-               make_csa2_variant, make_nsa_variant, make_csa2_stack):
+               make_csa2_variant, make_nsa_variant):
         fn(HERE)
         print("wrote", fn.__name__)
     return 0

@@ -1,12 +1,15 @@
-"""Block-mask coverage utilities (``linattn_b200.flex_mask``, after the reference's
-``kernels/flex_mask.py``): the reduction of a token mask is a superset of it, a
-dropped block is caught, and the oracle's block lists (configuration-4 windows, MoBA
-per-token routing) cover the token masks they stand for.  CPU only."""
+"""Block-mask coverage utilities (``linattn_b200.flex_mask``; the reference's
+``kernels/flex_mask.py:35-72`` names): the reduction of a token mask is a superset
+of it and equals the dense any-reduction, a dropped block is caught, the oracle's
+block lists (configuration-4 windows, MoBA per-token routing) cover the token masks
+they stand for, and the FlexAttention ``BlockMask`` built from lists holds the same
+cells.  CPU only."""
 import numpy as np
 import torch
 
 from oracle.blocks import block_mask_to_token_mask, moba_select, window_block_select
-from linattn_b200.flex_mask import check_block_mask, check_lists_cover, lists_to_block_mask, mask_to_block_mask
+from linattn_b200.flex_mask import (check_block_mask, check_lists_cover, flex_available, lists_to_block_mask,
+                                   mask_to_block_mask, to_block_mask)
 
 
 def test_reduction_is_superset_and_drop_is_caught():
@@ -21,6 +24,20 @@ def test_reduction_is_superset_and_drop_is_caught():
     broken = reduced.clone()
     broken[bb, hh, qb, kb] = False
     assert not check_block_mask(mask, broken, 64, 32)[0]
+    # the same cells as a dense any-reduction over padded 64 x 32 tiles
+    pad = torch.zeros(2, 3, 192, 224, dtype=torch.bool)
+    pad[..., :150, :200] = mask
+    assert torch.equal(reduced, pad.view(2, 3, 3, 64, 7, 32).any(3).any(-1))
+
+
+def test_flex_block_mask_from_lists():
+    if not flex_available():
+        return
+    gen = torch.Generator().manual_seed(3)
+    mask = torch.rand(1, 2, 256, 256, generator=gen) < 0.01
+    reduced = mask_to_block_mask(mask, 64, 64)
+    bm = to_block_mask(mask, 64, 64)
+    assert torch.equal(bm.to_dense().bool(), reduced)
 
 
 def test_window_lists_cover_their_token_mask():

@@ -234,7 +234,7 @@ def test_indexer_zero_weights_all_ties(cuda):
 
 @pytest.mark.parametrize("h,d,kdt", [(2, 128, torch.bfloat16), (8, 32, "fp8"), (1, 64, torch.float16),
                                      (4, 32, torch.bfloat16), (2, 64, "fp8"), (4, 16, torch.bfloat16),
-                                     (8, 16, torch.float16)])
+                                     (8, 16, torch.float16), (8, 16, "fp8"), (4, 16, "fp8")])
 @pytest.mark.parametrize("tk", [333, 1024])
 def test_indexer_tensor_core_shapes(cuda, h, d, kdt, tk):
     """Every tensor-core instantiation class, ragged T_k (odd row stride), B = 2, causal."""

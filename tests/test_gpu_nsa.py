@@ -165,10 +165,34 @@ def test_cuda_nsa_bf16_paths(cuda, d, block, selected):
     del o_slc_oracle
 
 
-@pytest.mark.parametrize("c,offset", [(3, 5), (16, 0), (1, 7)])
+@pytest.mark.parametrize("offset,t", [(37, 150), (200, 130)])
+def test_cuda_nsa_window_and_compression_at_offset(cuda, offset, t):
+    """The plugin's tensor-core window and compression branches for queries that start
+    mid-sequence (an offset that is not a multiple of 64, so the per-64-query block
+    ranges straddle key blocks), against float64 attention over the oracle's read sets."""
+    from linattn_b200 import build
+
+    gen = torch.Generator().manual_seed(offset + t)
+    b, hq, hkv, d = 1, 4, 2, 128
+    tk = offset + t
+    q = torch.randn(b, hq, t, d, generator=gen).bfloat16()
+    k, v = (torch.randn(b, hkv, tk, d, generator=gen).bfloat16() for _ in range(2))
+    var = build("cuda_nsa", _cfg(2, head_dim=d, block_size=64, window_size=40))
+    qn, kn, vn = (x.float().numpy() for x in (q, k, v))
+    o_cmp, _, o_win, _ = nsa_branches(qn, kn, vn, compress=8, block=64, selected=2, window=40, offset=offset,
+                                      dtype="bf16")
+    qc, kc, vc = q.to(cuda), k.to(cuda), v.to(cuda)
+    got_w = _np(var.branch_window(qc, kc, vc, offset))
+    got_c = _np(var.branch_compression(qc, kc, vc, offset))
+    assert np.all(np.abs(got_w - o_win) <= 2e-3 + 2.0 ** -8 * np.abs(o_win)), np.abs(got_w - o_win).max()
+    assert np.all(np.abs(got_c - o_cmp) <= 2e-3 + 2.0 ** -8 * np.abs(o_cmp)), np.abs(got_c - o_cmp).max()
+
+
+@pytest.mark.parametrize("c,offset", [(3, 5), (16, 0), (1, 7), (3, -2), (8, -5)])
 def test_prefill_pooled_causal_rule(cuda, c, offset):
     """``block_sparse_prefill(causal=c)``: key j read by the query at p iff
-    j * c <= p + c - 1 (c = 1: the usual causal rule), with a partial last block."""
+    j * c <= p + c - 1 (c = 1: the usual causal rule), with a partial last block; a
+    negative offset puts the first rows at -c < p < 0, where key 0 is already read."""
     from linattn_b200.blocks import block_sparse_prefill
 
     gen = torch.Generator().manual_seed(c + offset)
