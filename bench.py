@@ -280,7 +280,7 @@ def _time_events(fn_parts, steps: int, warmup: int, flush, stream):
     return [statistics.mean(ev[i][j].elapsed_time(ev[i][j + 1]) for i in range(steps)) for j in range(len(fn_parts))]
 
 
-def secondary_c4(device, steps: int, warmup: int, flush, stream, t: int = C4["T"]):
+def secondary_c4(device, steps: int, warmup: int, flush, stream, t: int = C4["T"], parity: bool = True):
     """Config 4 on this GPU: block selection + block-sparse causal prefill (tcgen05)."""
     from linattn_b200.blocks import block_select, block_sparse_prefill
 
@@ -297,6 +297,11 @@ def secondary_c4(device, steps: int, warmup: int, flush, stream, t: int = C4["T"
     def att():
         block_sparse_prefill(q, k, v, res["ids"], counts=res["cnt"], rows_per_list=c["block"], out=out)
     ms_sel, ms_att = _time_events([sel, att], steps, warmup, flush, stream)
+    par = None
+    if parity:
+        torch.cuda.synchronize(device)
+        par = parity_block_prefill(q, k, v, res["ids"], res["cnt"], out, c["block"], c["topk"], c["sink_blocks"],
+                                   c["window_blocks"])
     cnt = res["cnt"].long()
     bs, d = c["block"], c["D"]
     # allowed (query, key) pairs, causal-exact: full 64x64 blocks off the diagonal, a triangle on it
@@ -308,10 +313,10 @@ def secondary_c4(device, steps: int, warmup: int, flush, stream, t: int = C4["T"
             "prefill_ms": round(ms_att, 3), "prefill_tflops": round(tfl, 1), "frac_of_bf16_peak": round(tfl / peak, 4),
             "peak_kind": kind, "mean_blocks_per_query_block": round(cnt.float().mean().item(), 2),
             "algorithmic_flops": int(flops), "end_to_end_tflops": round(flops / ((ms_sel + ms_att) * 1e-3) / 1e12, 1),
-            "launches_per_step": 5}
+            "launches_per_step": 6, **({"parity": par} if par is not None else {})}
 
 
-def secondary_c3(device, steps: int, warmup: int, flush, stream, t: int = C3["T"]):
+def secondary_c3(device, steps: int, warmup: int, flush, stream, t: int = C3["T"], parity: bool = True):
     """Config 3 on this GPU: lightning indexer + causal top-2048 + token attention."""
     from linattn_b200 import indexer_topk
     from linattn_b200.dsa import token_sparse_attention
@@ -329,6 +334,10 @@ def secondary_c3(device, steps: int, warmup: int, flush, stream, t: int = C3["T"
     def att():
         token_sparse_attention(q, k, v, res["ids"].unsqueeze(1), causal=True, out=out)
     ms_sel, ms_att = _time_events([sel, att], steps, warmup, flush, stream)
+    par = None
+    if parity and t >= 4096:
+        torch.cuda.synchronize(device)
+        par = parity_dsa(q, k, v, q_idx, codes, scales, w, res["ids"], out, c["topk"], c["scale_group"])
     kk, d = c["topk"], c["D"]
     vis = sum(min(i + 1, kk) for i in range(t))  # selected tokens per query, causal
     gather = vis * c["Hkv"] * d * 2 * 2
@@ -338,7 +347,8 @@ def secondary_c3(device, steps: int, warmup: int, flush, stream, t: int = C3["T"
             "attention_gathered_gbs": round(gather / (ms_att * 1e-3) / 1e9, 1),
             "attention_gathered_frac_of_hbm": round(gather / (ms_att * 1e-3) / 1e9 / hbm, 4), "peak_kind": kind,
             "attention_tflops": round(4 * c["Hq"] * d * vis / (ms_att * 1e-3) / 1e12, 1),
-            "launches_per_step": 2 * -(-t // max(1, min(t, (1 << 29) // (t * 4)))) + 1}
+            "launches_per_step": 2 * -(-t // max(1, min(t, (1 << 29) // (t * 4)))) + 1,
+            **({"parity": par} if par is not None else {})}
 
 
 def run_prefill_workload(args):
@@ -355,7 +365,8 @@ def run_prefill_workload(args):
     with ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[0])) as clocks:
         if args.workload == "c4":
             t = args.seq_len or C4["T"]
-            r = secondary_c4(device, args.steps, args.warmup, flush, stream, t)
+            r = secondary_c4(device, args.steps, args.warmup, flush, stream, t, parity=not args.no_parity)
+            par = r.pop("parity", None)
             line = dict(base, metric="block-sparse causal prefill TFLOP/s", value=r["prefill_tflops"], unit="TFLOP/s",
                         ms_per_step=r["prefill_ms"],
                         config={"workload": "block_sparse_prefill_c4" if t == C4["T"] else f"block_sparse_prefill_c4_t{t}",
@@ -368,7 +379,8 @@ def run_prefill_workload(args):
             line["gpu_launches"] = r["launches_per_step"] * args.steps
         else:
             t = args.seq_len or C3["T"]
-            r = secondary_c3(device, args.steps, args.warmup, flush, stream, t)
+            r = secondary_c3(device, args.steps, args.warmup, flush, stream, t, parity=not args.no_parity)
+            par = r.pop("parity", None)
             line = dict(base, metric="DSA prefill tok/s", value=round(t / (r["total_ms"] * 1e-3), 1), unit="tok/s",
                         ms_per_step=r["total_ms"],
                         config={"workload": "dsa_indexer_attention_c3" if t == C3["T"] else f"dsa_c3_t{t}",
@@ -380,6 +392,8 @@ def run_prefill_workload(args):
                         detail=r)
             line["gpu_launches"] = r["launches_per_step"] * args.steps
     line["clocks"] = clocks.summary()
+    if par is not None:
+        line["parity"] = {line["config"]["workload"]: par}
     return line
 
 
@@ -477,6 +491,254 @@ def run_variants_workload(args):
                          "traffic": None},
             "detail": {"csa2": csa2, "nsa": nsa_r}, "gpu_launches": None, "clocks": clocks.summary()}
     return line
+
+
+# ---------------------------------------------------------------------------------
+# full-size parity: checker legs on samples of the benchmarked workloads, outside the
+# timed regions (the CPU oracle is the checker here, never the thing measured)
+# ---------------------------------------------------------------------------------
+TOL_16, TOL_FP8 = 2e-3, 1e-2  # north_star: bf16 / f16 inputs, fp8 KV (against the dequantised KV)
+
+
+def _out_errors(got_out: np.ndarray, ref: np.ndarray, tol: float, out_dtype, got32=None) -> dict:
+    """Errors against the float64 oracle: the fp32-domain result (when given) against the
+    bare tolerance, and the result in its output dtype against the tolerance plus half an
+    ulp of that dtype at |ref| (the one rounding to bf16 / f16 alone reaches that)."""
+    half = {torch.bfloat16: 2.0 ** -8, torch.float16: 2.0 ** -11}.get(out_dtype, 0.0)
+    e = np.abs(got_out - ref)
+    res = {"tol": tol, "max_abs_out": float(e.max()), "ok_out": bool(np.all(e <= tol + half * np.abs(ref)))}
+    if got32 is not None:
+        e32 = float(np.abs(got32 - ref).max())
+        res.update({"max_abs_fp32": e32, "ok_fp32": e32 <= tol})
+    return res
+
+
+def _union_attention_oracle(cache, qn, lens, uids, cnt, scale):
+    """Float64 oracle attention over each (sequence, kv head)'s union pages, one
+    (sequence, kv head) at a time with only its pages copied to the host (fp8 codes
+    decoded and scaled by the oracle), so the whole pool never leaves the device."""
+    import oracle
+
+    n, hq, d = qn.shape
+    hkv, p = cache.n_kv_heads, cache.page_size
+    group = hq // hkv
+    ref = np.zeros((n, hq, d))
+    for bi in range(n):
+        for kh in range(hkv):
+            pages = uids[bi, kh, : cnt[bi, kh]].astype(np.int64)
+            phys = cache.page_table[bi].long()[torch.from_numpy(pages).to(cache.device)]
+            kk = cache.k_pool[phys, kh]
+            vv = cache.v_pool[phys, kh]
+            if cache.fp8:
+                kk, vv = kk.view(torch.float8_e4m3fn), vv.view(torch.float8_e4m3fn)
+            kp = kk.float().cpu().numpy()[:, None]                  # (n_u, 1, P, D)
+            vp = vv.float().cpu().numpy()[:, None]
+            ks = cache.k_scale[phys, kh].cpu().numpy()[:, None] if cache.fp8 else None
+            vs = cache.v_scale[phys, kh].cpu().numpy()[:, None] if cache.fp8 else None
+            table = np.zeros((1, int(pages.max()) + 1 if pages.size else 1), dtype=np.int64)
+            table[0, pages] = np.arange(pages.size)
+            ref[bi, kh * group:(kh + 1) * group] = oracle.paged_sparse_decode(
+                qn[bi:bi + 1, kh * group:(kh + 1) * group], kp, vp, table, lens[bi:bi + 1],
+                pages[None, None], np.array([[pages.size]]), page_size=p, scale=scale, k_scale=ks, v_scale=vs)[0]
+    return ref
+
+
+def parity_quest_decode(cache, q, topk: int, sink_pages: int, *, n_splits: int, force_last: bool = True,
+                        timed_out=None, n_check: int = 2, tol: float = TOL_16):
+    """The decode step at full size on sequences [0, n_check): the page bounds exactly
+    against the oracle (16-bit pools); the kernel's fp32 page scores against the float64
+    oracle on the stored bounds; the selected pages bit-exact against the oracle's
+    lowest-index top-k on the kernel's own scores; the GQA union; the attention over
+    the union against the float64 oracle (fp32 output against the bare tolerance, the
+    q-dtype output with half an ulp); and ``timed_out`` (the timed decoder's output for
+    the same q) equal to this checking decoder's."""
+    import oracle
+    from linattn_b200 import QuestDecoder
+    from linattn_b200.block_sparse import sparse_attention
+
+    hq = q.shape[1]
+    hkv, p, d = cache.n_kv_heads, cache.page_size, cache.head_dim
+    group = hq // hkv
+    chk = QuestDecoder(cache, hq, topk, sink_pages=sink_pages, q_dtype=q.dtype, keep_scores=True,
+                       force_last=force_last, n_splits=n_splits)
+    out_chk = chk.step(q).clone()
+    o32 = sparse_attention(q, cache.kv_desc(), chk._lists, scale=chk.scale,
+                           out=torch.empty(q.shape, dtype=torch.float32, device=q.device), n_splits=chk.n_splits)
+    torch.cuda.synchronize(q.device)
+    lens = cache.seq_lens[:n_check].cpu().numpy().astype(np.int64)
+    n_b = (lens + p - 1) // p
+    scores = chk.scores[:n_check].cpu().numpy().astype(np.float64)
+    ids = chk.ids[:n_check].cpu().numpy().astype(np.int64)
+    cnt = chk.union_count[:n_check, :, 0].cpu().numpy()
+    uids = chk.union_ids[:n_check, :, 0].cpu().numpy()
+    sets_equal, union_equal, bounds_exact, score_rel = True, True, True, 0.0
+    mins = cache.meta_min[:n_check].float().cpu().numpy()  # (n, H_kv, pages, D), logical order
+    maxs = cache.meta_max[:n_check].float().cpu().numpy()
+    qn = q[:n_check].float().cpu().numpy()
+    for bi in range(n_check):
+        kb = max(1, min(topk, int(n_b[bi])))
+        want = oracle.topk_lowest_index(scores[bi, :, :, : n_b[bi]], kb)
+        sets_equal &= bool(np.array_equal(ids[bi, :, :, :kb], want))
+        union = oracle.gqa_union(ids[bi:bi + 1, :, :, :kb], int(n_b[bi]), group)[0, :, 0]
+        for kh in range(hkv):
+            union_equal &= bool(np.array_equal(uids[bi, kh, : cnt[bi, kh]], np.nonzero(union[kh])[0]))
+        for kh in range(hkv):  # one kv head at a time (float64 temporaries stay small)
+            hs = slice(kh * group, (kh + 1) * group)
+            ref_s = oracle.page_scores(qn[bi:bi + 1, hs], mins[bi:bi + 1, kh:kh + 1, : n_b[bi]],
+                                       maxs[bi:bi + 1, kh:kh + 1, : n_b[bi]])[0]
+            got_s = scores[bi, hs, :, : n_b[bi]]
+            fin = np.isfinite(got_s)
+            score_rel = max(score_rel, float((np.abs(got_s - ref_s)[fin] / (np.abs(ref_s[fin]) + 1.0)).max()))
+        if not cache.fp8:
+            # page bounds: every page of the sequence, exact (min / max of 16-bit values)
+            tab = cache.page_table[bi, : n_b[bi]].long()
+            kk = cache.k_pool[tab].float().cpu().numpy()  # (pages, H_kv, P, D)
+            bn, bx = oracle.page_bounds(kk.transpose(1, 0, 2, 3).reshape(1, hkv, -1, d)[:, :, : lens[bi]], p)
+            bounds_exact &= bool(np.array_equal(bn[0], mins[bi, :, : n_b[bi]]) and
+                                 np.array_equal(bx[0], maxs[bi, :, : n_b[bi]]))
+    ref = _union_attention_oracle(cache, qn[:, :, 0], lens, uids, cnt, chk.scale)
+    res = {"sequences_checked": n_check, "sets_equal": sets_equal, "union_equal": union_equal,
+           "bounds_exact": bounds_exact if not cache.fp8 else None, "score_max_rel_err": score_rel,
+           "timed_output_equal": None if timed_out is None else bool(torch.equal(out_chk, timed_out))}
+    res.update(_out_errors(out_chk[:n_check, :, 0].float().cpu().numpy(), ref, tol, q.dtype,
+                           o32[:n_check, :, 0].cpu().numpy()))
+    if timed_out is not None:
+        # the timed decoder's own output for the same q, against the same oracle
+        res["timed_ok_out"] = _out_errors(timed_out[:n_check, :, 0].float().cpu().numpy(), ref, tol,
+                                          timed_out.dtype)["ok_out"]
+    res["ok"] = bool(sets_equal and union_equal and res["ok_out"] and res["ok_fp32"]
+                     and res.get("timed_ok_out", True) and (cache.fp8 or bounds_exact))
+    return res
+
+
+def parity_block_prefill(q, k, v, ids, cnt, out, block: int, topk: int, sink_blocks: int, window_blocks: int,
+                         n_qb_check: int = 8, tol: float = TOL_16):
+    """Config 4 at full size on ``n_qb_check`` query blocks spread over T (the first and
+    the last included), every (b, head): the block lists bit-exact against the oracle's
+    rule (sink + window + lowest-index top-k of the causal candidates) applied to the
+    kernel's own fp32 pooled scores (recorded for those rows by the same kernel); the
+    same rule on float64 pooled scores, where a row may differ only at a near tie
+    (k-th and (k+1)-th candidate within 1e-5 relative); and the prefill output against
+    float64 attention over the kernel's own lists with the causal rule."""
+    from linattn_b200.blocks import block_mean, block_score_topk
+
+    b, hq, t, d = q.shape
+    hkv = k.shape[1]
+    group = hq // hkv
+    n_qb = t // block
+    qbs = sorted(set(np.linspace(0, n_qb - 1, n_qb_check).round().astype(int).tolist()))
+    ids_h = ids.cpu().numpy()
+    cnt_h = cnt.cpu().numpy()
+    qp, kp = block_mean(q, block), block_mean(k, block)
+    kmean = kp.double().cpu().numpy()          # the fp32 means, as float64
+    exact_mismatch, f64_mismatch, near_ties, rows = 0, 0, 0, 0
+    err_max, ok_out = 0.0, True
+    half = 2.0 ** -8
+    for qb in qbs:
+        own_sc = torch.full((b, hq, 1, n_qb), float("-inf"), device=q.device)
+        block_score_topk(qp[:, :, qb:qb + 1], kp, topk, scale=1.0 / math.sqrt(d), first_pos=qb - window_blocks,
+                         key_block=1, skip=sink_blocks, merge_pos=qb, sink=sink_blocks, window=window_blocks,
+                         scores_out=own_sc)
+        own_sc = own_sc[:, :, 0].double().cpu().numpy()                            # (B, Hq, n_qb)
+        qmean = qp[:, :, qb].double().cpu().numpy()                                # (B, Hq, D)
+        sc64 = np.einsum("bhgd,bhkd->bhgk", qmean.reshape(b, hkv, group, d), kmean).reshape(b, hq, n_qb)
+        sc64 /= math.sqrt(d)
+        q_blk = q[:, :, qb * block:(qb + 1) * block].double().cpu().numpy()      # (B, Hq, 64, D)
+        kbi = np.arange(n_qb)
+        cand_ok = (kbi >= sink_blocks) & (kbi <= qb - window_blocks)
+        forced = ((kbi < sink_blocks) | (kbi > qb - window_blocks)) & (kbi <= qb)
+        for bi in range(b):
+            for h in range(hq):
+                got = np.sort(ids_h[bi, h, qb, : cnt_h[bi, h, qb]])
+                rows += 1
+                for scores, kind in ((own_sc[bi, h], "own"), (sc64[bi, h], "f64")):
+                    cand = np.where(cand_ok, scores, -np.inf)
+                    order = np.argsort(-cand, kind="stable")
+                    kk = min(topk, int(cand_ok.sum()))
+                    want = np.sort(np.concatenate([np.nonzero(forced)[0], order[:kk]]))
+                    if np.array_equal(got, want):
+                        continue
+                    if kind == "own":
+                        exact_mismatch += 1
+                    else:
+                        srt = cand[order]
+                        if kk < srt.size and np.isfinite(srt[kk]) and abs(srt[kk - 1] - srt[kk]) <= 1e-5 * (
+                                abs(srt[kk]) + 1e-6):
+                            near_ties += 1
+                        else:
+                            f64_mismatch += 1
+                kh = h // group
+                tok = (got[:, None] * block + np.arange(block)[None, :]).reshape(-1)
+                sel = torch.from_numpy(tok).to(k.device)
+                kk_ = k[bi, kh, sel].double().cpu().numpy()
+                vv_ = v[bi, kh, sel].double().cpu().numpy()
+                pos = qb * block + np.arange(block)
+                allow = tok[None, :] <= pos[:, None]
+                sco = (q_blk[bi, h] @ kk_.T) / math.sqrt(d)
+                sco = np.where(allow, sco, -np.inf)
+                sco -= sco.max(-1, keepdims=True)
+                pw = np.exp(sco)
+                ref = (pw @ vv_) / pw.sum(-1, keepdims=True)
+                got_o = out[bi, h, qb * block:(qb + 1) * block].float().cpu().numpy()
+                e = np.abs(got_o - ref)
+                err_max = max(err_max, float(e.max()))
+                ok_out &= bool(np.all(e <= tol + half * np.abs(ref)))
+    return {"query_blocks_checked": qbs, "rows_checked": rows, "sets_equal": exact_mismatch == 0,
+            "sets_mismatch_own_scores": exact_mismatch, "sets_mismatch_float64": f64_mismatch,
+            "near_tie_rows_float64": near_ties, "tol": tol, "max_abs_out": err_max, "ok_out": ok_out,
+            "ok": bool(ok_out and exact_mismatch == 0)}
+
+
+def parity_dsa(q, k, v, q_idx, codes, scales, w, ids, out, topk: int, scale_group: int, tol: float = TOL_16):
+    """Config 3 at full size on 64 query rows in runs of 8 spread over T (t < 2048,
+    across 2048 and t = T-1 included): the kernel's fp32 indexer scores for those rows
+    against the float64 oracle on the dequantised fp8 keys; the selected tokens
+    bit-exact against the oracle's lowest-index causal top-k on the kernel's own
+    scores; the attention against float64 attention over the selected tokens."""
+    import oracle
+    from linattn_b200 import indexer_scores
+
+    b, hq, t, d = q.shape
+    hkv = k.shape[1]
+    group = hq // hkv
+    starts = [0, 1000, 2044, 4100, 9000, 16380, 24000, t - 8]
+    kdq = codes.view(torch.uint8).cpu().numpy()
+    kdq = oracle.e4m3_decode(kdq).astype(np.float64)
+    sc_h = scales.cpu().numpy()
+    sets_equal, score_rel, err_max, ok_out, rows = True, 0.0, 0.0, True, 0
+    ids_h = ids.cpu().numpy()
+    for r0 in starts:
+        r1 = r0 + 8
+        s = indexer_scores(q_idx[:, r0:r1], codes, w[:, r0:r1], k_scale=scales, scale_group=scale_group,
+                           causal=True, offset=r0)
+        got_s = s.cpu().numpy().astype(np.float64)                                 # (B, 8, T)
+        ref_s = oracle.indexer_scores(q_idx[:, r0:r1].float().cpu().numpy(), kdq, w[:, r0:r1].float().cpu().numpy(),
+                                      k_scale=sc_h, group=scale_group)
+        for i in range(r1 - r0):
+            tq = r0 + i
+            vis = tq + 1
+            fin = got_s[0, i, :vis]
+            score_rel = max(score_rel, float((np.abs(fin - ref_s[0, i, :vis]) / (np.abs(ref_s[0, i, :vis]) + 1.0)).max()))
+            kk = min(topk, vis)
+            want = np.sort(oracle.topk_lowest_index(fin, kk))
+            got = np.sort(ids_h[0, tq][ids_h[0, tq] >= 0])
+            sets_equal &= bool(np.array_equal(got, want))
+            rows += 1
+            sel = torch.from_numpy(got).to(k.device)
+            qq = q[0, :, tq].double().cpu().numpy()                                # (Hq, D)
+            for kh in range(hkv):
+                kk_ = k[0, kh, sel].double().cpu().numpy()
+                vv_ = v[0, kh, sel].double().cpu().numpy()
+                sco = qq[kh * group:(kh + 1) * group] @ kk_.T / math.sqrt(d)
+                sco -= sco.max(-1, keepdims=True)
+                pw = np.exp(sco)
+                ref = pw @ vv_ / pw.sum(-1, keepdims=True)
+                got_o = out[0, kh * group:(kh + 1) * group, tq].float().cpu().numpy()
+                e = np.abs(got_o - ref)
+                err_max = max(err_max, float(e.max()))
+                ok_out &= bool(np.all(e <= tol + 2.0 ** -8 * np.abs(ref)))
+    return {"rows_checked": rows, "row_starts": starts, "sets_equal": sets_equal, "score_max_rel_err": score_rel,
+            "tol": tol, "max_abs_out": err_max, "ok_out": ok_out, "ok": bool(sets_equal and ok_out)}
 
 
 # ---------------------------------------------------------------------------------
@@ -783,12 +1045,19 @@ def run_ours(args, rank, world, local_rank):
         "gpu_launches": n_launch_step * args.steps,
         "clocks": clock,
     }
+    if world == 1 and not args.no_parity:
+        line["parity"] = {"quest_decode_c2": parity_quest_decode(cache, qs[args.warmup], c["topk"], c["sink_pages"],
+                                                                 n_splits=dec.n_splits,
+                                                                 timed_out=dec.step(qs[args.warmup]).clone())}
     if world == 1 and not args.no_secondary:
         sec_steps, sec_warm = max(3, min(args.steps, 10)), 3
         c4 = secondary_c4(device, sec_steps, sec_warm, flush, stream)
         line["prefill_tflops"] = c4["prefill_tflops"]
-        line["secondary"] = {"block_sparse_prefill_c4": c4,
-                             "dsa_c3": secondary_c3(device, sec_steps, sec_warm, flush, stream)}
+        c3 = secondary_c3(device, sec_steps, sec_warm, flush, stream)
+        line["secondary"] = {"block_sparse_prefill_c4": c4, "dsa_c3": c3}
+        for key, r in (("block_sparse_prefill_c4", c4), ("dsa_c3", c3)):
+            if "parity" in r:
+                line.setdefault("parity", {})[key] = r.pop("parity")
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
         fn, kind, desc = cpu_reference_step_fn(cache, qs[args.warmup], 2, threads)
@@ -826,7 +1095,7 @@ def run_c5(args, rank, world, local_rank):
         dec.candidates(box["q"])
 
     def phase_merge():
-        dec.merge_packed(exchange(dec.cand))
+        dec.merge_packed(exchange(dec.exchange_buf))
 
     def phase_attend():
         dec.partial(box["q"])
@@ -887,10 +1156,15 @@ def run_c5(args, rank, world, local_rank):
     torch.cuda.synchronize(device)
     e2e_ms = statistics.mean(e.elapsed_time(f) for e, f in e2e_ev)
 
+    par = None
+    if world == 1 and not args.no_parity:
+        q_chk = qs[args.warmup]
+        timed = dec.step(q_chk, exchange=exchange).clone()
+        par = parity_quest_decode(cache, q_chk, c["topk"], 0, n_splits=dec.n_splits, timed_out=timed, tol=TOL_FP8)
     n_loc = hi - lo
     meta_bytes = b * hkv * n_loc * 2 * d * 2
     score_bytes = 0  # the fused kernel keeps page scores on chip; candidates are (chunks, B, H_q, topk)
-    sel_bytes = meta_bytes + dec.cand.numel() * 4
+    sel_bytes = meta_bytes + dec.cand.numel() * 4 * (2 if dec.premerge else 1)
     # per selected (page, kv head): fp8 K and V rows and their two fp32 scales; plus q in and f32 (o, lse) out
     kv_bytes = pages_loc * (p * d * 2 + 8) + b * hq * d * 2 + b * hq * (d + 1) * 4
     achieved_sel = sel_bytes / (ph[0] * 1e-3) / 1e9
@@ -910,7 +1184,8 @@ def run_c5(args, rank, world, local_rank):
     kname = "quest_decode_candidates (fused page scoring + per-chunk top-k)" if dominant == "select" else \
         "sparse_attention (fp8 paged on tensor cores, f32 partial o + lse)"
     traffic = profile_traffic("quest_select_c5.md" if dominant == "select" else "sparse_attention_c5.md")
-    n_mine = 4 + (dec.n_splits > 1)  # candidates, merge, attention (+ its split merge), combine
+    # candidates (+ the shard's pre-merge), merge, attention (+ its split merge), combine
+    n_mine = 4 + (dec.n_splits > 1) + int(dec.premerge)
     return {
         "metric": METRIC,
         "value": round(b / (step_ms * 1e-3), 1),
@@ -947,6 +1222,7 @@ def run_c5(args, rank, world, local_rank):
                 "api": "linattn_b200.sharded.ShardedQuestDecoder.step"},
         "gpu_launches": n_mine * args.steps,
         "clocks": clocks.summary(),
+        **({"parity": {"sharded_decode_c5": par}} if par is not None else {}),
     }
 
 
@@ -1062,6 +1338,8 @@ def main(argv=None) -> int:
                          "prefill forward")
     ap.add_argument("--seq-len", type=int, default=None,
                     help="c3 / c4 / c5 only: a shorter sequence (profiling captures)")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the full-size parity checks (run outside the timed regions)")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the config-3 / config-4 legs reported beside the config-2 line")
     args = ap.parse_args(argv)
@@ -1101,6 +1379,21 @@ def main(argv=None) -> int:
             if args.batch is None:
                 args.batch = C2["B"]
             line = run_ours(args, rank, world, local_rank)
+            if not args.no_secondary:
+                # config 5 beside the headline at every N: the KV sequence split over the
+                # ranks (strong scaling), the one configuration with a data-path collective
+                torch.cuda.empty_cache()
+                c5_args = argparse.Namespace(**vars(args))
+                c5_args.batch, c5_args.seq_len = None, None
+                c5_args.steps, c5_args.warmup = max(3, min(args.steps, 10)), 3
+                c5 = run_c5(c5_args, rank, world, local_rank)
+                if rank == 0:
+                    keep = ("value", "unit", "n_gpus", "ms_per_step", "scaling", "dtype", "config",
+                            "step_breakdown_ms", "bytes_per_step_per_gpu", "selected_pages_per_kv_head_per_gpu",
+                            "select_chunks_per_gpu", "attend_splits", "roofline", "e2e", "gpu_launches", "clocks")
+                    line.setdefault("secondary", {})["sharded_decode_c5"] = {k: c5[k] for k in keep if k in c5}
+                    if "parity" in c5:
+                        line.setdefault("parity", {}).update(c5["parity"])
         if rank == 0:
             print(json.dumps(line), flush=True)
     finally:

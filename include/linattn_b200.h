@@ -407,6 +407,31 @@ int linattn_csa2_pool_quant(const void* x, int32_t dtype, int64_t B, int64_t H, 
                             void* stream);
 
 /*
+ * Block selection in one launch: scores, causal top-k and the forced-block merge.
+ * Row r of (b, h) (a (B, H_q, R, D), element strides, f32 / f16 / bf16) is scored
+ * against the candidates of its kv head h / (H_q / H_kv) (bm (B, H_kv, NC, D)):
+ * s(r, c) = scale * sum_d a[r, d] * bm[c, d] in fp32, channel order 0 .. D-1.  Row r
+ * takes candidates [skip, min(floor((first_pos + r) / key_block), NC - 1)] and keeps
+ * the top k (1 <= k <= 32) by (score desc, index asc); these are merged as
+ * linattn_merge_block_lists does with own = min(floor((merge_pos + r) / own_div),
+ * NC - 1), sink and window, into out (B, H_q, R, n_max) ascending, -1 padded, and
+ * counts (B, H_q, R).  Optional: topk_out (B, H_q, R, k), the top k in score order
+ * (-1 padded); scores_out (B, H_q, R, NC), the fp32 scores the selection ranked
+ * (entries outside a row's candidate range are left unwritten).  D 64 or 128.
+ * Replaces the pooled block scores, torch.topk and the boolean unions of
+ * MInferenceAttention._block_sparse (src/linattn/variants/selection.py:339-353),
+ * MoBAAttention.select (:635-649) and NSAAttention's selection branch
+ * (src/linattn/variants/native_sparse.py:78-92), and builds the sink + window +
+ * top-k lists of the block-sparse prefill.
+ */
+int linattn_block_score_topk(const void* a, int32_t a_dtype, const int64_t* a_strides /*[4]*/, const void* bm,
+                             int32_t b_dtype, const int64_t* b_strides /*[4]*/, int64_t B, int64_t Hq, int64_t Hkv,
+                             int64_t R, int64_t NC, int64_t D, float scale, int64_t k, int64_t first_pos,
+                             int64_t key_block, int64_t skip, int64_t merge_pos, int64_t own_div, int64_t sink,
+                             int64_t window, int32_t force_own, int32_t* out, int64_t n_max, int32_t* counts,
+                             int32_t* topk_out, float* scores_out, void* stream);
+
+/*
  * Block lists from a top-k selection: for each of `rows` rows, the ascending union
  * (duplicates removed) of its top-k ids (int32, -1 padded, rows of k) with the forced
  * blocks [0, sink) and [own - window + 1, own], plus `own` itself with force_own, all
@@ -474,11 +499,14 @@ int linattn_prefill_v_to_f16(const void* v, int64_t heads, int64_t per_head, voi
  * next in both scores and ids (0 = B * H_q * K, dense), so a gathered buffer holding
  * each rank's [scores | ids] pair is read in place.  union_tokens (B, H_kv), when not
  * NULL, receives the tokens of the union pages: sum over pages g of
- * clamp(seq_lens[b] - g * page_size, 0, page_size), g the global page.
+ * clamp(seq_lens[b] - g * page_size, 0, page_size), g the global page.  sel_scores
+ * (B, H_q, topk), when not NULL, receives the scores of sel (-inf past the last).  With
+ * union_ids NULL no union is built (sel required): a shard merging its own chunks
+ * before the exchange, so that it sends one sorted block of K instead of one per chunk.
  */
 int linattn_shard_merge(const float* scores, const int32_t* ids, int64_t R, int64_t B, int64_t Hq, int64_t K,
                         int64_t rank_stride, int64_t topk, int64_t n_kv_heads, const int32_t* page_lo, const int32_t* page_hi,
-                        int64_t max_local, int32_t* sel, int32_t* union_ids, int32_t* union_count,
+                        int64_t max_local, int32_t* sel, float* sel_scores, int32_t* union_ids, int32_t* union_count,
                         int64_t max_union, const int32_t* seq_lens, int64_t page_size, int32_t* union_tokens,
                         void* stream);
 

@@ -2,14 +2,17 @@
 
 * ``block_mean``: mean-pooled blocks of queries / keys (``block_reduce``,
   ``src/linattn/core.py:103-120``), a CUDA kernel.
+* ``block_score_topk``: one kernel for the rest of every block selector: the fp32
+  block scores of each row against its kv head's candidates, the causal top-k
+  (lowest-index ties) and the ascending merge with the forced blocks, never writing
+  the score matrix (``linattn_block_score_topk``).
 * ``pooled_block_scores``: ``mean(q_blk) . mean(k_blk) / sqrt(D)`` per (b, q-head,
   q-block, k-block) (``MInferenceAttention._block_sparse``,
-  ``src/linattn/variants/selection.py:339-347``): the pooling kernel, then a plain
-  batched GEMM (cuBLAS through ``torch.matmul``).
-* ``block_select``: per q-block lists = the top-k causal candidate blocks (radix-select
-  kernel, lowest-index ties) united with forced blocks: the own block (MInference,
-  ``selection.py:350-351``) and/or sink blocks and a window of blocks (the block-sparse
-  prefill's sink + window + top-k).
+  ``src/linattn/variants/selection.py:339-347``) as a full matrix, from the same kernel
+  (for inspection and tests; the selection itself does not materialise it).
+* ``block_select``: per q-block lists = the top-k causal candidate blocks united with
+  forced blocks: the own block (MInference, ``selection.py:350-351``) and/or sink
+  blocks and a window of blocks (the block-sparse prefill's sink + window + top-k).
 * ``moba_select``: per-token lists of ``MoBAAttention.select`` (``selection.py:635-649``):
   gate ``q . mean(k_blk) / sqrt(D)``, top-k over blocks that start at or before the
   query, plus the own block.
@@ -23,9 +26,8 @@ from typing import Optional, Tuple, Union
 import torch
 
 from linattn_b200 import _lib as L
-from linattn_b200.indexer import row_topk
 
-__all__ = ["block_mean", "pooled_block_scores", "block_select", "moba_select", "merge_block_lists",
+__all__ = ["block_mean", "block_score_topk", "pooled_block_scores", "block_select", "moba_select", "merge_block_lists",
            "block_sparse_prefill"]
 
 
@@ -40,17 +42,43 @@ def block_mean(x: torch.Tensor, block: int) -> torch.Tensor:
     return out
 
 
+def block_score_topk(a: torch.Tensor, bm: torch.Tensor, k: int, *, scale: float, first_pos: int, key_block: int = 1,
+                     skip: int = 0, merge_pos: int, own_div: int = 1, sink: int = 0, window: int = 0,
+                     force_own: bool = True, n_max: int = 0, topk_out: bool = False,
+                     scores_out: Optional[torch.Tensor] = None):
+    """Rows ``a (B, H_q, R, D)`` against candidates ``bm (B, H_kv, NC, D)`` (see
+    ``linattn_block_score_topk``): returns ``(ids (B, H_q, R, n_max) int32 ascending,
+    -1 padded, counts (B, H_q, R) int32)`` and, with ``topk_out``, the top k in score
+    order ``(B, H_q, R, k)``.  ``scores_out`` (B, H_q, R, NC) fp32, if given, receives
+    the scores the selection ranked (other entries untouched)."""
+    L.require_cuda(a, bm)
+    b, hq, r, d = a.shape
+    hkv, nc = bm.shape[1], bm.shape[2]
+    kk = max(1, min(int(k), nc))
+    n_max = n_max or (kk + max(sink, 0) + max(window, 1))
+    out = torch.empty(b, hq, r, n_max, dtype=torch.int32, device=a.device)
+    counts = torch.empty(b, hq, r, dtype=torch.int32, device=a.device)
+    tk = torch.empty(b, hq, r, kk, dtype=torch.int32, device=a.device) if topk_out else None
+    if scores_out is not None and (scores_out.shape != (b, hq, r, nc) or scores_out.dtype != torch.float32
+                                   or not scores_out.is_contiguous()):
+        raise ValueError("scores_out must be a contiguous fp32 (B, H_q, R, NC) tensor")
+    L.check(L.lib().linattn_block_score_topk(
+        a.data_ptr(), L.dtype_code(a), L.strides4(a), bm.data_ptr(), L.dtype_code(bm), L.strides4(bm), b, hq, hkv, r,
+        nc, d, float(scale), kk, first_pos, key_block, skip, merge_pos, own_div, sink, window, int(force_own),
+        out.data_ptr(), n_max, counts.data_ptr(), L.ptr(tk), L.ptr(scores_out), L.stream_of(a)))
+    return (out, counts, tk) if topk_out else (out, counts)
+
+
 def pooled_block_scores(q: torch.Tensor, k: torch.Tensor, block: int) -> torch.Tensor:
-    """``(B,H_q,n_qb,n_kb)`` fp32 pooled block scores with the GQA repeat of ``k``."""
+    """``(B,H_q,n_qb,n_kb)`` fp32 pooled block scores with the GQA repeat of ``k``: the
+    scores ``block_select`` ranks (computed by the same kernel; entries past a row's
+    own block are -inf)."""
     b, hq, _, d = q.shape
-    hkv = k.shape[1]
-    # the 1/sqrt(D) factor goes on the pooled queries (n_qb x D per head) rather than
-    # on the n_qb x n_kb scores: one small pass instead of one over the score matrix
-    qp = block_mean(q, block).mul_(1.0 / math.sqrt(d))
-    kp = block_mean(k, block)
-    g = hq // hkv
-    s = torch.matmul(qp.view(b, hkv, g, qp.shape[2], d), kp.view(b, hkv, 1, kp.shape[2], d).transpose(-1, -2))
-    return s.view(b, hq, qp.shape[2], kp.shape[2])
+    qp, kp = block_mean(q, block), block_mean(k, block)
+    nqb, nkb = qp.shape[2], kp.shape[2]
+    s = torch.full((b, hq, nqb, nkb), float("-inf"), dtype=torch.float32, device=q.device)
+    block_score_topk(qp, kp, 1, scale=1.0 / math.sqrt(d), first_pos=0, merge_pos=0, scores_out=s)
+    return s
 
 
 def merge_block_lists(topk_ids: torch.Tensor, *, period: int, first_pos: int, own_div: int, n_blocks: int,
@@ -79,34 +107,25 @@ def block_select(q: torch.Tensor, k: torch.Tensor, block: int, topk: int, *, off
     top ``topk`` of their pooled scores are united with ``[0, sink_blocks)``, the window
     ``[qb - window_blocks + 1, qb]`` and, with ``force_own``, ``qb``.
     ``window_blocks = sink_blocks = 0, force_own`` is MInference's block-sparse pattern."""
-    scores = pooled_block_scores(q, k, block)
-    b, hq, nqb, nkb = scores.shape
+    b, hq, _, d = q.shape
+    qp, kp = block_mean(q, block), block_mean(k, block)
     qb0 = offset // block
-    kk = max(1, min(topk, nkb))
-    # causal candidates: the first (qb - window_blocks + 1) entries of each row, minus the sink
-    _, ids = row_topk(scores.view(-1, nkb), kk, sorted=False, causal=True, first_pos=qb0 - window_blocks,
-                      period=nqb, skip=sink_blocks, index_dtype=torch.int32)
-    return merge_block_lists(ids.view(b, hq, nqb, kk), period=nqb, first_pos=qb0, own_div=1, n_blocks=nkb,
-                             sink=sink_blocks, window=window_blocks, force_own=force_own,
-                             n_max=kk + sink_blocks + max(window_blocks, 1))
+    kk = max(1, min(topk, kp.shape[2]))
+    # causal candidates of row i: [sink_blocks, qb0 + i - window_blocks]
+    return block_score_topk(qp, kp, kk, scale=1.0 / math.sqrt(d), first_pos=qb0 - window_blocks, key_block=1,
+                            skip=sink_blocks, merge_pos=qb0, own_div=1, sink=sink_blocks, window=window_blocks,
+                            force_own=force_own, n_max=kk + sink_blocks + max(window_blocks, 1))
 
 
 def moba_select(q: torch.Tensor, k: torch.Tensor, block: int, topk: int, *,
                 offset: int = 0) -> Tuple[torch.Tensor, torch.Tensor]:
     """Per (b, q-head, query) block lists of MoBA (``selection.py:635-649``)."""
     b, hq, tq, d = q.shape
-    hkv = k.shape[1]
     kp = block_mean(k, block)
-    nkb = kp.shape[2]
-    g = hq // hkv
-    gates = torch.matmul(q.float().reshape(b, hkv, g * tq, d), kp.transpose(-1, -2)).view(b, hq, tq, nkb)
-    gates.mul_(1.0 / math.sqrt(d))
-    kk = max(1, min(topk, nkb))
+    kk = max(1, min(topk, kp.shape[2]))
     # a query never routes to a block that starts after it: block j visible iff j * block <= pos
-    _, ids = row_topk(gates.view(-1, nkb), kk, sorted=False, causal=True, first_pos=offset, key_block=block,
-                      period=tq, index_dtype=torch.int32)
-    return merge_block_lists(ids.view(b, hq, tq, kk), period=tq, first_pos=offset, own_div=block, n_blocks=nkb,
-                             force_own=True, n_max=kk + 1)
+    return block_score_topk(q, kp, kk, scale=1.0 / math.sqrt(d), first_pos=offset, key_block=block,
+                            merge_pos=offset, own_div=block, force_own=True, n_max=kk + 1)
 
 
 def block_sparse_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ids: torch.Tensor, *,

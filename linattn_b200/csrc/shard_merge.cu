@@ -10,7 +10,10 @@
 // writes them so) and the blocks hold disjoint pages, so a candidate's rank is its
 // position in its block plus a binary search in every other block.  The first k go
 // to `sel`, and those in this shard's range [page_lo_b, page_hi_b) to a bitmap that
-// compacts to the ascending local page list the attention reads.  No counterpart in the reference (it
+// compacts to the ascending local page list the attention reads.  With the union
+// left out (union_ids NULL) the kernel is a shard's pre-merge of its own chunks: its
+// top-k ids and scores, in key order, form the one block of K the shard exchanges.
+// No counterpart in the reference (it
 // never shards the KV sequence); the selection equals page_select_torch's top-k
 // (src/linattn/kernels/triton/quest_pages.py:57-78) over the union of the shards' pages
 // whenever each shard's k candidates include its share of the global top-k, which
@@ -31,7 +34,8 @@ struct ShardMergeParams {
   const int32_t* page_hi;  // (B) one past its last
   int64_t max_local;       // local pages (bitmap size)
   int32_t* sel;            // (B, Hq, topk) global ids, (score desc, id asc), -1 padded; or NULL
-  int32_t* union_ids;      // (B, Hkv, max_union) local ids ascending, -1 padded
+  float* sel_scores;       // (B, Hq, topk) their scores (-inf past the last), or NULL
+  int32_t* union_ids;      // (B, Hkv, max_union) local ids ascending, -1 padded; NULL: no union
   int32_t* union_count;    // (B, Hkv)
   int64_t max_union;
   const int32_t* seq_lens;  // (B) tokens of each sequence (for union_tokens)
@@ -92,6 +96,7 @@ __global__ void __launch_bounds__(256) shard_merge_kernel(const ShardMergeParams
         if (khi == hmax && klo == lmax) {     // the unique winner
           const int32_t id = static_cast<int32_t>(~lmax);
           if (p.sel) p.sel[(b * p.Hq + h) * p.topk + i] = id;
+          if (p.sel_scores) p.sel_scores[(b * p.Hq + h) * p.topk + i] = key_float(hmax);
           if (id >= lo && id < hi && id - lo < p.max_local)
             atomicOr(&bits[(id - lo) >> 5], 1u << ((id - lo) & 31));
           if (k0 > k1) ++p0;
@@ -100,6 +105,8 @@ __global__ void __launch_bounds__(256) shard_merge_kernel(const ShardMergeParams
       }
       if (p.sel)
         for (int64_t r = i + lane; r < p.topk; r += 32) p.sel[(b * p.Hq + h) * p.topk + r] = -1;
+      if (p.sel_scores)
+        for (int64_t r = i + lane; r < p.topk; r += 32) p.sel_scores[(b * p.Hq + h) * p.topk + r] = -INFINITY;
       __syncwarp();
     }
   } else {
@@ -136,17 +143,20 @@ __global__ void __launch_bounds__(256) shard_merge_kernel(const ShardMergeParams
       if (rank < p.topk) {
         const int32_t id = static_cast<int32_t>(~static_cast<uint32_t>(kx & 0xffffffffull));
         if (p.sel) p.sel[(b * p.Hq + h) * p.topk + rank] = id;
+        if (p.sel_scores) p.sel_scores[(b * p.Hq + h) * p.topk + rank] = key_float(static_cast<uint32_t>(kx >> 32));
         if (id >= lo && id < hi && id - lo < p.max_local) atomicOr(&bits[(id - lo) >> 5], 1u << ((id - lo) & 31));
       }
     }
     atomicAdd(&sh_valid, my_valid);
     __syncthreads();
-    if (p.sel)
-      for (int64_t r = lmin(static_cast<int64_t>(sh_valid), p.topk) + tid; r < p.topk; r += 256)
-        p.sel[(b * p.Hq + h) * p.topk + r] = -1;
+    for (int64_t r = lmin(static_cast<int64_t>(sh_valid), p.topk) + tid; r < p.topk; r += 256) {
+      if (p.sel) p.sel[(b * p.Hq + h) * p.topk + r] = -1;
+      if (p.sel_scores) p.sel_scores[(b * p.Hq + h) * p.topk + r] = -INFINITY;
+    }
   }
   }
   __syncthreads();
+  if (p.union_ids == nullptr) return;  // top-k only (a shard's pre-merge of its own chunks)
   // ascending local union: popcount scan over the bitmap words
   const int64_t per = (nwords + 255) / 256;
   const int64_t w0 = lmin(nwords, tid * per), w1 = lmin(nwords, w0 + per);
@@ -184,10 +194,11 @@ using namespace linattn;
 
 extern "C" int linattn_shard_merge(const float* scores, const int32_t* ids, int64_t R, int64_t B, int64_t Hq,
                                    int64_t K, int64_t rank_stride, int64_t topk, int64_t n_kv_heads, const int32_t* page_lo,
-                                   const int32_t* page_hi, int64_t max_local, int32_t* sel, int32_t* union_ids,
+                                   const int32_t* page_hi, int64_t max_local, int32_t* sel, float* sel_scores,
+                                   int32_t* union_ids,
                                    int32_t* union_count, int64_t max_union, const int32_t* seq_lens,
                                    int64_t page_size, int32_t* union_tokens, void* stream) {
-  if (!scores || !ids || !page_lo || !page_hi || !union_ids || !union_count)
+  if (!scores || !ids || !page_lo || !page_hi || (union_ids && !union_count) || (!union_ids && !sel))
     return set_error(LINATTN_EINVAL, "shard_merge: NULL pointer");
   if (R < 1 || K < 1 || topk < 1 || n_kv_heads < 1 || Hq % n_kv_heads || max_local < 1 || max_union < 1)
     return set_error(LINATTN_EINVAL, "shard_merge: bad sizes");
@@ -198,7 +209,7 @@ extern "C" int linattn_shard_merge(const float* scores, const int32_t* ids, int6
   ShardMergeParams p;
   p.scores = scores; p.ids = ids; p.R = R; p.B = B; p.Hq = Hq; p.K = K;
   p.rs = rank_stride ? rank_stride : B * Hq * K; p.topk = topk; p.G = Hq / n_kv_heads;
-  p.page_lo = page_lo; p.page_hi = page_hi; p.max_local = max_local; p.sel = sel;
+  p.page_lo = page_lo; p.page_hi = page_hi; p.max_local = max_local; p.sel = sel; p.sel_scores = sel_scores;
   p.union_ids = union_ids; p.union_count = union_count; p.max_union = max_union;
   if (union_tokens && (!seq_lens || page_size < 1))
     return set_error(LINATTN_EINVAL, "shard_merge: union_tokens needs seq_lens and page_size");

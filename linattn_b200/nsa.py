@@ -11,9 +11,9 @@ keys (``extras["compress_ratio"]``, ``["selected_blocks"]``, ``["gate_mode"]``,
   reads are a prefix (those starting at or before ``p + c - 1``): the tcgen05 prefill
   kernel with its pooled causal rule (``causal = c``) at head size 128 in bf16 / f16,
   otherwise the shared ids ``0 .. G-1`` with a per-query count;
-* selection (``:78-98``): block means of k (cache dtype), fp32 scores of every query
-  against them (a cuBLAS GEMM: 16-bit operands with fp32 accumulation and output), the row top-k kernel over the blocks starting at or
-  before the query, the own block merged in by ``merge_block_lists``; the selected
+* selection (``:78-98``): block means of k (cache dtype), then one kernel for the fp32
+  scores of every query against them, the top-k over the blocks starting at or before
+  the query and the merge with the own block (``block_score_topk``); the selected
   blocks are read whole (no causal cut, as the reference's mask): the tcgen05 prefill
   kernel for 64-token blocks at head size 128 in bf16 / f16, the general sparse kernel
   otherwise;
@@ -37,11 +37,10 @@ import torch
 
 from linattn_b200 import _lib as L
 from linattn_b200.block_sparse import kv_contiguous, lists_desc, sparse_attention
-from linattn_b200.blocks import block_sparse_prefill, merge_block_lists
+from linattn_b200.blocks import block_score_topk, block_sparse_prefill
 from linattn_b200.core import AttentionVariant
 from linattn_b200.csa2 import csa2_pool_quant
 from linattn_b200.dsa import token_sparse_attention
-from linattn_b200.indexer import row_topk
 
 __all__ = ["CudaNSAAttention", "nsa_select"]
 
@@ -55,27 +54,13 @@ def nsa_select(q: torch.Tensor, k: torch.Tensor, block: int, selected: int, *,
     """Per (b, q-head, query) block lists of NSA's selection branch
     (``native_sparse.py:78-92``): ``(ids (B, Hq, Tq, kk + 1) int32 ascending -1 padded,
     counts (B, Hq, Tq) int32)``."""
-    b, hq, tq, d = q.shape
-    hkv = k.shape[1]
+    d = q.shape[-1]
     kp = csa2_pool_quant(k, block, 16)  # block_reduce in the cache dtype
-    nkb = kp.shape[2]
-    g = hq // hkv
-    if q.dtype in (torch.bfloat16, torch.float16) and kp.dtype == q.dtype:
-        # 16-bit operands, fp32 accumulation and output on the tensor cores: the products
-        # of two 16-bit values are exact in fp32, so the scores are the fp32 GEMM's up to
-        # the order of the sums
-        scores = torch.bmm(q.reshape(b * hkv, g * tq, d), kp.reshape(b * hkv, nkb, d).transpose(1, 2),
-                           out_dtype=torch.float32).view(b, hq, tq, nkb)
-    else:
-        scores = torch.matmul(q.float().reshape(b, hkv, g * tq, d),
-                              kp.float().transpose(-1, -2)).view(b, hq, tq, nkb)
-    scores.mul_(1.0 / math.sqrt(d))
-    kk = max(1, min(selected, nkb))
-    # block j is allowed for the query at p iff j * block <= p
-    _, ids = row_topk(scores.view(-1, nkb), kk, sorted=False, causal=True, first_pos=offset, key_block=block,
-                      period=tq, index_dtype=torch.int32)
-    return merge_block_lists(ids.view(b, hq, tq, kk), period=tq, first_pos=offset, own_div=block, n_blocks=nkb,
-                             force_own=True, n_max=kk + 1)
+    kk = max(1, min(selected, kp.shape[2]))
+    # block j is allowed for the query at p iff j * block <= p; scores in fp32 (16-bit
+    # products are exact in fp32), ranked and merged with the own block in one kernel
+    return block_score_topk(q, kp, kk, scale=1.0 / math.sqrt(d), first_pos=offset, key_block=block,
+                            merge_pos=offset, own_div=block, force_own=True, n_max=kk + 1)
 
 
 class CudaNSAAttention(AttentionVariant):

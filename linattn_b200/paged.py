@@ -210,13 +210,15 @@ _SMEM_TWO_PER_SM = 113 * 1024
 
 
 def plan_select_chunks(n: int, g: int, topk: int, d: int, units: int, device, chunks: Optional[int] = None,
-                       ranks: int = 1, mma: bool = True, cand_only: bool = False):
+                       ranks: int = 1, mma: bool = True, cand_only: bool = False, premerge: bool = False):
     """(pages per CTA, chunks) for the fused selection over `n` pages and `units`
     (sequence, kv head) pairs.  One chunk (the single-CTA form, no merge) when the
     pairs alone fill the GPU and the whole sequence's scores fit in shared memory;
     else chunks small enough for two CTAs per SM and numerous enough for two CTAs per
     SM.  Returns 0 chunks when the merge's bound (4096 candidates per head across the
-    chunks of all `ranks`) or shared memory rules the fused kernel out."""
+    chunks of all `ranks`; with `premerge`, each rank first merges its own chunks, so
+    across the chunks of one rank and across the ranks) or shared memory rules the
+    fused kernel out."""
     sms = torch.cuda.get_device_properties(device).multi_processor_count
     if chunks is None:
         if not cand_only and units >= 0.8 * sms and fused_select_smem(n, g, topk, d, mma, False) <= _SMEM_MAX:
@@ -233,7 +235,8 @@ def plan_select_chunks(n: int, g: int, topk: int, d: int, units: int, device, ch
         chunk = -(-chunk // 2)
         single = False
     chunks = -(-n // chunk)
-    if chunks * ranks * topk > 4096 or fused_select_smem(chunk, g, topk, d, mma, not single) > _SMEM_MAX:
+    n_cand = max(chunks, ranks) * topk if premerge else chunks * ranks * topk
+    if n_cand > 4096 or fused_select_smem(chunk, g, topk, d, mma, not single) > _SMEM_MAX:
         return chunk, 0
     return chunk, chunks
 
@@ -312,7 +315,7 @@ class QuestDecoder:
                 L.ptr(self.scores), status.data_ptr(), stream))
             L.check(lib.linattn_shard_merge(
                 self.cand.data_ptr(), self.cand[:, 1].data_ptr(), self.chunks, b, hq, self.topk, 2 * bhk, self.topk,
-                c.n_kv_heads, self.page_zero.data_ptr(), c.n_pages_b.data_ptr(), c.max_pages, self.ids.data_ptr(),
+                c.n_kv_heads, self.page_zero.data_ptr(), c.n_pages_b.data_ptr(), c.max_pages, self.ids.data_ptr(), None,
                 self.union_ids.data_ptr(), self.union_count.data_ptr(), self.max_union, c.seq_lens.data_ptr(),
                 c.page_size, self.union_tokens.data_ptr(), stream))
             return QuestSelection(self.ids, self.scores, self.union_ids, self.union_count, self.union_tokens)

@@ -6,8 +6,10 @@ the slice, pages ``[page_lo_b, page_hi_b)`` of sequence ``b``).  One decode step
 1. local selection (the candidates form of the fused Quest kernel) gives each query
    head the top-K pages of each chunk of the shard with their scores; only the rank
    holding a sequence's last page forces it in, only the rank holding page 0 forces
-   the sink pages;
-2. the (score, global page) candidates are all-gathered (rank-major);
+   the sink pages; with several ranks the shard merges its chunks into its own top-K
+   (``linattn_shard_merge`` without the union), one sorted block of K per head;
+2. the (score, global page) candidates are all-gathered (rank-major): R blocks of K
+   per head, whatever the number of chunks;
 3. every rank takes the same global top-K per head (``linattn_shard_merge``: score
    desc, lowest page on ties, as the single-cache selection) and keeps the GQA union
    of the selected pages it owns;
@@ -113,7 +115,7 @@ class ShardedQuestDecoder:
                                       "group of 1, 2, 4 or 8 query heads")
         self.chunk_pages, self.chunks = plan_select_chunks(cache.max_pages, g, topk, d, b * hkv, dev, select_chunks,
                                                            ranks=n_ranks, mma=q_dtype == cache.meta_dtype,
-                                                           cand_only=True)
+                                                           cand_only=True, premerge=n_ranks > 1)
         if self.chunks == 0:
             raise NotImplementedError(f"sharded decode: {n_ranks} ranks x topk {topk} exceed the merge kernel's 4096 "
                                       "candidates per head")
@@ -125,6 +127,11 @@ class ShardedQuestDecoder:
         self.union_tokens = torch.empty(b, hkv, 1, dtype=torch.int32, device=dev)
         self.sel = torch.empty(b, n_heads, topk, dtype=torch.int32, device=dev)
         self.cand = torch.empty(self.chunks, 2, b, n_heads, topk, dtype=torch.int32, device=dev)
+        # with several ranks each one first merges its own chunks into one sorted block of
+        # K ([score bits | ids], the same layout), so the exchange and the global merge
+        # see R blocks instead of R * chunks
+        self.premerge = n_ranks > 1 and self.chunks > 1
+        self.block = torch.empty(2, b, n_heads, topk, dtype=torch.int32, device=dev) if self.premerge else None
         rows = b * n_heads
         self.rows = rows
         self.part = torch.empty(rows * d + rows, dtype=torch.float32, device=dev)
@@ -151,7 +158,19 @@ class ShardedQuestDecoder:
             c.n_kv_heads, c.max_pages, c.n_pages_b.data_ptr(), self.topk, self.sink_pages, int(self.force_last),
             self.chunk_pages, self.page_lo.data_ptr(), self.cand.data_ptr(), self.cand[:, 1].data_ptr(), 2 * bhk,
             None, status.data_ptr(), L.stream_of(q)))
+        if self.premerge:
+            L.check(L.lib().linattn_shard_merge(
+                self.cand.data_ptr(), self.cand[:, 1].data_ptr(), self.chunks, b, hq, self.topk, 2 * bhk, self.topk,
+                c.n_kv_heads, self.page_lo.data_ptr(), self.page_hi.data_ptr(), c.max_pages,
+                self.block[1].data_ptr(), self.block[0].data_ptr(), None, None, 0, None, 0, None, L.stream_of(q)))
+            return self.block[0].view(torch.float32).unsqueeze(0), self.block[1].unsqueeze(0)
         return self.cand[:, 0].view(torch.float32), self.cand[:, 1]
+
+    @property
+    def exchange_buf(self) -> torch.Tensor:
+        """The candidates buffer a step exchanges: ``(2, B, H_q, topk)`` after the
+        pre-merge, else ``cand (chunks, 2, B, H_q, topk)``."""
+        return self.block if self.premerge else self.cand
 
     def merge(self, all_scores: torch.Tensor, all_ids: torch.Tensor) -> None:
         """Global top-``topk`` of the gathered candidates ``(R, B, H_q, K)`` (R blocks,
@@ -164,12 +183,12 @@ class ShardedQuestDecoder:
         L.check(L.lib().linattn_shard_merge(
             all_scores.data_ptr(), all_ids.data_ptr(), r, b, hq, k, all_scores.stride(0) if r > 1 else 0, self.topk,
             self.cache.n_kv_heads, self.page_lo.data_ptr(), self.page_hi.data_ptr(), self.cache.max_pages,
-            self.sel.data_ptr(), self.union_ids.data_ptr(), self.union_count.data_ptr(), self.max_union,
+            self.sel.data_ptr(), None, self.union_ids.data_ptr(), self.union_count.data_ptr(), self.max_union,
             self.cache.seq_lens.data_ptr(), self.cache.page_size, self.union_tokens.data_ptr(),
             L.stream_of(all_scores)))
 
     def merge_packed(self, allc: torch.Tensor) -> None:
-        """``merge`` over gathered ``cand`` buffers ``(R, chunks, 2, B, H_q, topk)``."""
+        """``merge`` over gathered ``exchange_buf`` buffers ``(R, [chunks,] 2, B, H_q, topk)``."""
         blocks = allc.reshape(-1, *allc.shape[-4:])  # (R * chunks, 2, B, H_q, topk)
         self.merge(blocks[:, 0].view(torch.float32), blocks[:, 1])
 
@@ -206,6 +225,6 @@ class ShardedQuestDecoder:
         (default: ``exchange_packed`` on the process group)."""
         exchange = exchange or (lambda t: exchange_packed(t, self.group))
         self.candidates(q)
-        self.merge_packed(exchange(self.cand))
+        self.merge_packed(exchange(self.exchange_buf))
         self.partial(q)
         return self.combine_packed(exchange(self.part))

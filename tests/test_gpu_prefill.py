@@ -168,8 +168,10 @@ def test_block_select_vs_oracle(cuda, sink_b, window_b, topk):
     qd, kd = q.cuda(), k.cuda()
     ids, counts = block_select(qd, kd, 64, topk, sink_blocks=sink_b, window_blocks=window_b)
     scores = pooled_block_scores(qd, kd, 64).cpu().numpy()
-    # pooled scores themselves against the oracle
-    assert np.allclose(scores, oracle.blocks.pooled_block_scores(_np(q), _np(k), 64), atol=1e-4)
+    # pooled scores themselves against the oracle, on the causal part the kernel ranks
+    tri = np.tril(np.ones(scores.shape[-2:], bool))
+    assert np.all(np.isneginf(scores[..., ~tri]))
+    assert np.allclose(scores[..., tri], oracle.blocks.pooled_block_scores(_np(q), _np(k), 64)[..., tri], atol=1e-4)
     exp_ids, exp_cnt = _expected_lists(scores, topk, sink_b, window_b, own=True)
     got = ids.cpu().numpy()
     assert np.array_equal(counts.cpu().numpy(), exp_cnt)
@@ -202,3 +204,66 @@ def test_moba_select_vs_oracle(cuda):
     got = token_mask(ids.cpu().numpy(), counts.cpu().numpy(), 1, 320, 320, 0, causal=True)
     ref = oracle.moba_select(q.numpy(), k.numpy(), 64, 2) & np.tril(np.ones((320, 320), bool))
     assert (got == ref).mean() > 0.999
+
+
+def _merge_expected(topk_ids, own, sink, window, force_own):
+    """The ascending union the selection kernels build (``linattn_merge_block_lists``)."""
+    if own < 0:
+        return []
+    s_end = min(sink, own + 1)
+    w_lo = max(s_end, own - window + 1) if window > 0 else own + 1
+    if force_own and w_lo > own:
+        w_lo = max(s_end, own)
+    sel = set(range(s_end)) | set(range(w_lo, own + 1)) | {int(x) for x in topk_ids if 0 <= x <= own}
+    return sorted(sel)
+
+
+@pytest.mark.parametrize("case", [
+    # (a dtype, b dtype, hq, hkv, R, NC, D, k, first_pos, key_block, skip, merge_pos, own_div, sink, window)
+    ("f32", "f32", 8, 2, 300, 300, 128, 16, -16, 1, 1, 0, 1, 1, 16),     # config-4 lists (sink + window + top-16)
+    ("bf16", "bf16", 4, 2, 777, 13, 128, 4, 37, 64, 0, 37, 64, 0, 0),    # NSA: token rows, pooled 16-bit keys
+    ("bf16", "f32", 3, 1, 200, 4, 64, 2, 0, 64, 0, 0, 64, 0, 0),         # MoBA at G = 3, D = 64
+    ("f16", "f32", 16, 2, 150, 150, 64, 20, -3, 1, 2, 5, 1, 2, 3),      # k > 16 (32-entry rows), G = 8
+])
+def test_block_score_topk_exact_on_own_scores(cuda, case):
+    """The fused score + top-k + merge kernel: its fp32 scores against float64, and its
+    lists bit-exact against the oracle's lowest-index top-k of the candidates on those
+    very scores, merged with the forced blocks; the score-order top k as well."""
+    from linattn_b200.blocks import block_score_topk
+
+    adt, bdt, hq, hkv, r, nc, d, k, first_pos, key_block, skip, merge_pos, own_div, sink, window = case
+    dt = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}
+    gen = torch.Generator().manual_seed(r + nc + k)
+    a = torch.randn(2, hq, r, d, generator=gen).to(dt[adt])
+    bm = torch.randn(2, hkv, nc, d, generator=gen).to(dt[bdt])
+    # a few exact ties between candidates, to exercise the lowest-index rule
+    bm[:, :, 3] = bm[:, :, 1]
+    scale = 1.0 / math.sqrt(d)
+    s_out = torch.full((2, hq, r, nc), float("nan"), device=cuda)
+    ids, counts, tk = block_score_topk(a.to(cuda), bm.to(cuda), k, scale=scale, first_pos=first_pos,
+                                       key_block=key_block, skip=skip, merge_pos=merge_pos, own_div=own_div,
+                                       sink=sink, window=window, topk_out=True, scores_out=s_out)
+    sc = s_out.cpu().numpy().astype(np.float64)
+    ids, counts, tk = ids.cpu().numpy(), counts.cpu().numpy(), tk.cpu().numpy()
+    g = hq // hkv
+    ref = np.einsum("bhrd,bhcd->bhrc", a.double().numpy(), np.repeat(bm.double().numpy(), g, axis=1)) * scale
+    kk = min(k, nc)
+    for bi in range(2):
+        for h in range(hq):
+            for ri in range(r):
+                lim = min((first_pos + ri) // key_block, nc - 1)
+                cand = np.arange(skip, lim + 1)
+                row = sc[bi, h, ri]
+                if cand.size:
+                    assert np.all(np.isfinite(row[cand]))
+                    assert np.allclose(row[cand], ref[bi, h, ri, cand], rtol=1e-5, atol=1e-5)
+                order = cand[np.argsort(-row[cand], kind="stable")][:kk] if cand.size else np.array([], int)
+                want_tk = np.full(kk, -1)
+                want_tk[: order.size] = order
+                assert np.array_equal(tk[bi, h, ri], want_tk), (bi, h, ri)
+                pos = merge_pos + ri
+                own = -1 if pos < 0 else min(pos // own_div, nc - 1)
+                want = _merge_expected(order, own, sink, window, True)
+                assert counts[bi, h, ri] == len(want), (bi, h, ri)
+                assert np.array_equal(ids[bi, h, ri, : len(want)], want), (bi, h, ri)
+                assert np.all(ids[bi, h, ri, len(want):] == -1)

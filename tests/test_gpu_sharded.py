@@ -95,7 +95,8 @@ def test_sharded_decode_matches_single_cache(cuda, dtype, world):
 def test_sharded_decode_packed_exchange(cuda, world, chunks):
     """The packed path of ``step``: one gathered [scores | ids] buffer and one gathered
     [o | lse] buffer per rank, read in place by the merge and combine kernels through
-    their rank strides; several chunks per shard."""
+    their rank strides; several chunks per shard (merged by the shard before the
+    exchange when there are several ranks)."""
     from linattn_b200 import QuestDecoder
     from linattn_b200.sharded import ShardedQuestDecoder
 
@@ -112,7 +113,9 @@ def test_sharded_decode_packed_exchange(cuda, world, chunks):
     else:
         for dec in decs:
             dec.candidates(q)
-        allc = torch.stack([dec.cand for dec in decs])
+        # each rank exchanges one sorted block of K per head once it merged its chunks
+        assert all(dec.premerge == (dec.chunks > 1) for dec in decs)
+        allc = torch.stack([dec.exchange_buf for dec in decs])
         for dec in decs:
             dec.merge_packed(allc)
         for dec in decs:
