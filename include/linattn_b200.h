@@ -417,7 +417,7 @@ int linattn_csa2_pool_quant(const void* x, int32_t dtype, int64_t B, int64_t H, 
  * NC - 1), sink and window, into out (B, H_q, R, n_max) ascending, -1 padded, and
  * counts (B, H_q, R).  Optional: topk_out (B, H_q, R, k), the top k in score order
  * (-1 padded); scores_out (B, H_q, R, NC), the fp32 scores the selection ranked
- * (entries outside a row's candidate range are left unwritten).  D 64 or 128.
+ * (entries outside a row's candidate range are left unwritten).  D <= 256.
  * Replaces the pooled block scores, torch.topk and the boolean unions of
  * MInferenceAttention._block_sparse (src/linattn/variants/selection.py:339-353),
  * MoBAAttention.select (:635-649) and NSAAttention's selection branch

@@ -200,7 +200,8 @@ extern "C" int linattn_shard_merge(const float* scores, const int32_t* ids, int6
                                    int64_t page_size, int32_t* union_tokens, void* stream) {
   if (!scores || !ids || !page_lo || !page_hi || (union_ids && !union_count) || (!union_ids && !sel))
     return set_error(LINATTN_EINVAL, "shard_merge: NULL pointer");
-  if (R < 1 || K < 1 || topk < 1 || n_kv_heads < 1 || Hq % n_kv_heads || max_local < 1 || max_union < 1)
+  if (R < 1 || K < 1 || topk < 1 || n_kv_heads < 1 || Hq % n_kv_heads || max_local < 1 ||
+      (union_ids && max_union < 1))
     return set_error(LINATTN_EINVAL, "shard_merge: bad sizes");
   if (rank_stride != 0 && rank_stride < B * Hq * K) return set_error(LINATTN_EINVAL, "shard_merge: rank_stride");
   if (R * K > 4096 || max_local > (int64_t(1) << 20))

@@ -224,6 +224,8 @@ def _merge_expected(topk_ids, own, sink, window, force_own):
     ("bf16", "bf16", 4, 2, 777, 13, 128, 4, 37, 64, 0, 37, 64, 0, 0),    # NSA: token rows, pooled 16-bit keys
     ("bf16", "f32", 3, 1, 200, 4, 64, 2, 0, 64, 0, 0, 64, 0, 0),         # MoBA at G = 3, D = 64
     ("f16", "f32", 16, 2, 150, 150, 64, 20, -3, 1, 2, 5, 1, 2, 3),      # k > 16 (32-entry rows), G = 8
+    ("f32", "f32", 4, 2, 96, 12, 32, 3, 0, 8, 0, 0, 8, 0, 0),           # D = 32 (the runtime-D form)
+    ("bf16", "bf16", 2, 2, 70, 9, 72, 2, 5, 8, 0, 5, 8, 1, 2),          # D = 72, G = 1
 ])
 def test_block_score_topk_exact_on_own_scores(cuda, case):
     """The fused score + top-k + merge kernel: its fp32 scores against float64, and its
