@@ -100,53 +100,69 @@ struct DecodeSelectParams {
 // form, (score, page) candidates.
 // Ranks the kb taken entries (sel_idx / sel_key) by (score desc, index asc) and
 // writes the ids (marking the union bitmap) or the candidates.
+// The entries of two lists (A: na entries, B: nb_ entries; B may be empty) ranked
+// together by (score desc, index asc); the first kb by rank are written as ids (and
+// marked in the union bitmap) or, in the candidates form, as (score, page) candidates.
+__device__ __forceinline__ void write_selection2(const DecodeSelectParams& p, const float* srow,
+                                                 const uint32_t* idx_a, const uint32_t* key_a, int64_t na,
+                                                 const uint32_t* idx_b, const uint32_t* key_b, int64_t nb_,
+                                                 int64_t kb, uint32_t* bitmap, int64_t pg0, int64_t b, int64_t h,
+                                                 int lane) {
+  const uint32_t neg_inf_key = float_key(-INFINITY);
+  const int64_t n = na + nb_;
+  const bool cand = p.cand_scores != nullptr;
+  const int64_t off = cand ? static_cast<int64_t>(blockIdx.y) * p.cand_stride + (b * p.Hq + h) * p.topk
+                           : (b * p.Hq + h) * p.topk;
+  const int64_t id0 = pg0 + (p.page_base ? static_cast<int64_t>(p.page_base[b]) : 0);
+  for (int64_t i = lane; i < n; i += 32) {
+    const uint32_t ki = i < na ? key_a[i] : key_b[i - na], ii = i < na ? idx_a[i] : idx_b[i - na];
+    int rank = 0;
+    for (int64_t j = 0; j < na; ++j) {
+      const uint32_t kj = key_a[j], ij = idx_a[j];
+      rank += (kj > ki || (kj == ki && ij < ii)) ? 1 : 0;
+    }
+    for (int64_t j = 0; j < nb_; ++j) {
+      const uint32_t kj = key_b[j], ij = idx_b[j];
+      rank += (kj > ki || (kj == ki && ij < ii)) ? 1 : 0;
+    }
+    if (rank >= kb) continue;
+    if (cand) {
+      p.cand_scores[off + rank] = srow[ii];
+      p.cand_ids[off + rank] = static_cast<int32_t>(id0 + ii);
+    } else {
+      p.ids[off + rank] = static_cast<int32_t>(ii);
+      if (ki > neg_inf_key) atomicOr(&bitmap[ii >> 5], 1u << (ii & 31u));
+    }
+  }
+  for (int64_t r = kb + lane; r < p.topk; r += 32) {
+    if (cand) {
+      p.cand_scores[off + r] = -INFINITY;
+      p.cand_ids[off + r] = -1;
+    } else {
+      p.ids[off + r] = -1;
+    }
+  }
+}
+
 __device__ __forceinline__ void write_selection(const DecodeSelectParams& p, const float* srow,
                                                 const uint32_t* sel_idx, const uint32_t* sel_key, int64_t kb,
                                                 uint32_t* bitmap, int64_t pg0, int64_t b, int64_t h, int lane) {
-  const uint32_t neg_inf_key = float_key(-INFINITY);
-  if (p.cand_scores) {
-    const int64_t off = static_cast<int64_t>(blockIdx.y) * p.cand_stride + (b * p.Hq + h) * p.topk;
-    const int64_t id0 = pg0 + (p.page_base ? static_cast<int64_t>(p.page_base[b]) : 0);
-    for (int64_t i = lane; i < kb; i += 32) {
-      const uint32_t ki = sel_key[i], ii = sel_idx[i];
-      int rank = 0;
-      for (int64_t j = 0; j < kb; ++j) {
-        const uint32_t kj = sel_key[j], ij = sel_idx[j];
-        rank += (kj > ki || (kj == ki && ij < ii)) ? 1 : 0;
-      }
-      p.cand_scores[off + rank] = srow[ii];
-      p.cand_ids[off + rank] = static_cast<int32_t>(id0 + ii);
-    }
-    for (int64_t r = kb + lane; r < p.topk; r += 32) {
-      p.cand_scores[off + r] = -INFINITY;
-      p.cand_ids[off + r] = -1;
-    }
-  } else {
-    int32_t* out = p.ids + (b * p.Hq + h) * p.topk;
-    for (int64_t i = lane; i < kb; i += 32) {
-      const uint32_t ki = sel_key[i], ii = sel_idx[i];
-      int rank = 0;
-      for (int64_t j = 0; j < kb; ++j) {
-        const uint32_t kj = sel_key[j], ij = sel_idx[j];
-        rank += (kj > ki || (kj == ki && ij < ii)) ? 1 : 0;
-      }
-      out[rank] = static_cast<int32_t>(ii);
-      if (ki > neg_inf_key) atomicOr(&bitmap[ii >> 5], 1u << (ii & 31u));
-    }
-    for (int64_t r = kb + lane; r < p.topk; r += 32) out[r] = -1;
-  }
+  write_selection2(p, srow, sel_idx, sel_key, kb, nullptr, nullptr, 0, kb, bitmap, pg0, b, h, lane);
 }
 
 // Register form for nb <= 32 * ITEMS: lane holds keys i = j * 32 + lane; the k-th
 // largest key is found by a binary search over the key range with warp-wide counts
 // (no shared-memory histogram, no atomics), then the same gather and ranking.
+// With idx_off >= 0 the selection is only gathered (its indices shifted by idx_off,
+// in this warp's slot of `sel`) for a merge with another warp's; otherwise written.
 template <int ITEMS>
 __device__ __forceinline__ void select_head_reg(const DecodeSelectParams& p, const float* srow, uint32_t* sel,
                                                 uint32_t* bitmap, int64_t nb, int64_t pg0, int64_t b, int64_t h,
-                                                int warp, int lane) {
+                                                int warp, int lane, int64_t idx_off = -1) {
   const int64_t kb = nb > 0 ? lmax(1, lmin(p.topk, nb)) : 0;
   uint32_t* sel_idx = sel + warp * 2 * p.topk;
   uint32_t* sel_key = sel_idx + p.topk;
+  const uint32_t shift = idx_off > 0 ? static_cast<uint32_t>(idx_off) : 0u;
   uint32_t key[ITEMS];
   uint32_t kmax = 0u, kmin = 0xffffffffu;
 #pragma unroll
@@ -201,7 +217,7 @@ __device__ __forceinline__ void select_head_reg(const DecodeSelectParams& p, con
 #pragma unroll
     for (int j = 0; j < ITEMS; ++j) {
       if (key[j] >= kstar && j * 32 + lane < nb) {
-        sel_idx[pos] = static_cast<uint32_t>(j * 32 + lane);
+        sel_idx[pos] = static_cast<uint32_t>(j * 32 + lane) + shift;
         sel_key[pos] = key[j];
         ++pos;
       }
@@ -222,7 +238,7 @@ __device__ __forceinline__ void select_head_reg(const DecodeSelectParams& p, con
       const unsigned take_mask = __ballot_sync(0xffffffffu, take);
       if (take) {
         const uint32_t pos = n_sel + __popc(take_mask & ((1u << lane) - 1u));
-        sel_idx[pos] = static_cast<uint32_t>(i);
+        sel_idx[pos] = static_cast<uint32_t>(i) + shift;
         sel_key[pos] = key[j];
       }
       n_sel += __popc(take_mask);
@@ -230,13 +246,50 @@ __device__ __forceinline__ void select_head_reg(const DecodeSelectParams& p, con
     }
   }
   __syncwarp();
-  write_selection(p, srow, sel_idx, sel_key, kb, bitmap, pg0, b, h, lane);
+  if (idx_off < 0) write_selection(p, srow, sel_idx, sel_key, kb, bitmap, pg0, b, h, lane);
+}
+
+// Split form (G <= 4, so every head has two of the eight consumer warps): warp g and
+// warp g + G each select the top kb of one half of head g's scores, and after a CTA
+// barrier warp g ranks the two halves' picks together (a pick of the head's top kb is
+// in its half's top kb, ties included, since its half holds no more keys that beat it).
+// Every thread of the CTA calls this (the split form has a CTA-wide barrier).
+template <int G, int ITEMS>
+__device__ __forceinline__ void select_heads_split(const DecodeSelectParams& p, const float* sc, uint32_t* bitmap,
+                                                   uint32_t* sel, int64_t nb, int64_t pg0, int64_t b, int64_t kvh,
+                                                   int warp, int lane) {
+  const int64_t kb = lmax(1, lmin(p.topk, nb));
+  const int g = warp % G, half = warp / G;
+  const int64_t n0 = (nb + 1) / 2;
+  const float* srow = sc + g * p.chunk;
+  const int64_t h = kvh * G + g;
+  if (warp < 2 * G) {
+    if (p.scores && half == 0) {
+      float* dst = p.scores + (b * p.Hq + h) * p.max_pages + pg0;
+      const int64_t span = lmin(p.chunk, p.max_pages - pg0);
+      for (int64_t i = lane; i < span; i += 32) dst[i] = i < nb ? srow[i] : -INFINITY;
+    }
+    const int64_t off = half ? n0 : 0, n = half ? nb - n0 : n0;
+    select_head_reg<ITEMS>(p, srow + off, sel, bitmap, n, pg0, b, h, warp, lane, off);
+  }
+  __syncthreads();
+  if (warp < G) {
+    const uint32_t* a = sel + g * 2 * p.topk;
+    const uint32_t* c = sel + (g + G) * 2 * p.topk;
+    write_selection2(p, srow, a, a + p.topk, lmin(kb, n0), c, c + p.topk, lmin(kb, nb - n0), kb, bitmap, pg0, b, h,
+                     lane);
+  }
 }
 
 template <int G>
 __device__ __forceinline__ void select_heads(const DecodeSelectParams& p, const float* sc, uint32_t* hist,
                                              uint32_t* bitmap, uint32_t* sel, int64_t nb, int64_t pg0, int64_t b,
                                              int64_t kvh, int warp, int lane) {
+  if constexpr (G <= 4) {
+    // CTA-uniform choice (nb is the CTA's page count)
+    if (nb > 512 && nb <= 1024) return select_heads_split<G, 16>(p, sc, bitmap, sel, nb, pg0, b, kvh, warp, lane);
+    if (nb > 1024 && nb <= 2048) return select_heads_split<G, 32>(p, sc, bitmap, sel, nb, pg0, b, kvh, warp, lane);
+  }
   if (warp >= G) return;
   const int64_t kb = nb > 0 ? lmax(1, lmin(p.topk, nb)) : 0;
   const int g = warp;
