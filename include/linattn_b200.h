@@ -492,7 +492,7 @@ int linattn_prefill_v_to_f16(const void* v, int64_t heads, int64_t per_head, voi
  * desc, page asc) is taken (written to sel (B, H_q, topk), -1 padded, when sel is not
  * NULL); the pages of this shard, [page_lo[b], page_hi[b]), selected by any head of a
  * kv head's group go to union_ids (B, H_kv, max_union) as ascending LOCAL ids
- * (page - page_lo[b]), -1 padded, with union_count (B, H_kv).  R * K <= 4096.
+ * (page - page_lo[b]), -1 padded, with union_count (B, H_kv).  R <= 64, R * K <= 4096.
  * No counterpart in the reference (which never shards the KV sequence); the selection
  * equals page_select_torch's (src/linattn/kernels/triton/quest_pages.py:57-78) over
  * the whole cache.  rank_stride: elements from one shard's (B, H_q, K) block to the

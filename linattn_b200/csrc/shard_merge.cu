@@ -7,8 +7,8 @@
 // candidates by a 64-bit key (order-preserving score, then the bitwise complement of
 // the page id, so equal scores go to the lowest page: the single-cache top-k's
 // tie-break); each block of K arrives sorted by that key (the candidates kernel
-// writes them so) and the blocks hold disjoint pages, so a candidate's rank is its
-// position in its block plus a binary search in every other block.  The first k go
+// writes them so) and the blocks hold disjoint pages, so a k-way merge of the block
+// heads yields the global order.  The first k go
 // to `sel`, and those in this shard's range [page_lo_b, page_hi_b) to a bitmap that
 // compacts to the ascending local page list the attention reads.  With the union
 // left out (union_ids NULL) the kernel is a shard's pre-merge of its own chunks: its
@@ -44,116 +44,90 @@ struct ShardMergeParams {
 };
 
 __device__ __forceinline__ unsigned long long cand_key(const ShardMergeParams& p, int64_t off) {
-  const int32_t id = p.ids[off];
-  return id >= 0 ? (static_cast<unsigned long long>(float_key(p.scores[off])) << 32) |
+  // both loads issued together (the score is read even for an empty slot)
+  const int32_t id = __ldcg(p.ids + off);
+  const float sc = __ldcg(p.scores + off);
+  return id >= 0 ? (static_cast<unsigned long long>(float_key(sc)) << 32) |
                        static_cast<unsigned long long>(~static_cast<uint32_t>(id))
                  : 0ull;  // empty slots rank last
 }
 
-// WARP: one warp per head merges the R sorted blocks (at most 64, two per lane): each
-// step the warp takes the largest block head (two 32-bit warp max-reductions over the
-// unique 64-bit keys) and its lane advances, so the top-k come out in order after k
-// steps.  Heads run in waves of `hpw` warps, each staging its head's keys in its own
-// shared-memory slice.  Otherwise: all threads rank every candidate by binary search.
-template <bool WARP>
+// The keys of `hpw` heads at a time are staged in shared memory by all threads
+// (eight loads in flight per thread: the staging is latency-bound otherwise); then one
+// warp per head merges the R sorted blocks (R <= 64, two per lane): each step the warp
+// takes the largest block head (two 32-bit warp max-reductions over the unique 64-bit
+// keys) and that block advances, so the top-k come out in order after k steps.
 __global__ void __launch_bounds__(256) shard_merge_kernel(const ShardMergeParams p, int hpw) {
   extern __shared__ unsigned long long msm[];
   const int64_t n = p.R * p.K;
-  unsigned long long* keys = msm;                                    // [R * K] or [hpw][R * K]
-  uint32_t* bits = reinterpret_cast<uint32_t*>(keys + (WARP ? hpw : 1) * n);  // [(max_local + 31) / 32]
+  unsigned long long* keys = msm;                                   // [hpw][R * K]
+  uint32_t* bits = reinterpret_cast<uint32_t*>(keys + hpw * n);     // [(max_local + 31) / 32]
   __shared__ uint32_t scratch[256 / 32 + 1];
-  __shared__ uint32_t sh_tokens, sh_valid;
-  const int tid = threadIdx.x;
+  __shared__ uint32_t sh_tokens;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (tid == 0) sh_tokens = 0u;
   const int64_t bk = blockIdx.x;  // (b, kv head)
   const int64_t Hkv = p.Hq / p.G;
   const int64_t kvh = bk % Hkv, b = bk / Hkv;
   const int64_t lo = p.page_lo[b], hi = p.page_hi[b];
   const int64_t nwords = (p.max_local + 31) / 32;
-  for (int64_t i = tid; i < nwords; i += 256) bits[i] = 0u;
-  __syncthreads();
-  if constexpr (WARP) {
-    const int warp = tid >> 5, lane = tid & 31;
-    unsigned long long* kw = keys + warp * n;
-    for (int64_t g = warp; g < p.G && warp < hpw; g += hpw) {
-      const int64_t h = kvh * p.G + g;
-      for (int64_t i = lane; i < n; i += 32) {
-        const int64_t r = i / p.K, e = i % p.K;
-        kw[i] = cand_key(p, r * p.rs + (b * p.Hq + h) * p.K + e);
-      }
-      __syncwarp();
-      const int64_t r0 = lane, r1 = lane + 32;
-      int64_t p0 = 0, p1 = 0;
-      int64_t i = 0;
-      for (; i < p.topk; ++i) {
-        const unsigned long long k0 = (r0 < p.R && p0 < p.K) ? kw[r0 * p.K + p0] : 0ull;
-        const unsigned long long k1 = (r1 < p.R && p1 < p.K) ? kw[r1 * p.K + p1] : 0ull;
-        const unsigned long long mine = k0 > k1 ? k0 : k1;
-        const uint32_t khi = static_cast<uint32_t>(mine >> 32), klo = static_cast<uint32_t>(mine);
-        const uint32_t hmax = __reduce_max_sync(0xffffffffu, khi);
-        const uint32_t lmax = __reduce_max_sync(0xffffffffu, khi == hmax ? klo : 0u);
-        if (hmax == 0u && lmax == 0u) break;  // every block exhausted (warp-uniform)
-        if (khi == hmax && klo == lmax) {     // the unique winner
-          const int32_t id = static_cast<int32_t>(~lmax);
-          if (p.sel) p.sel[(b * p.Hq + h) * p.topk + i] = id;
-          if (p.sel_scores) p.sel_scores[(b * p.Hq + h) * p.topk + i] = key_float(hmax);
-          if (id >= lo && id < hi && id - lo < p.max_local)
-            atomicOr(&bits[(id - lo) >> 5], 1u << ((id - lo) & 31));
-          if (k0 > k1) ++p0;
-          else ++p1;
+  if (p.union_ids)
+    for (int64_t i = tid; i < nwords; i += 256) bits[i] = 0u;
+  const int K = static_cast<int>(p.K);
+  for (int64_t g0 = 0; g0 < p.G; g0 += hpw) {
+    const int ng = static_cast<int>(lmin(hpw, p.G - g0));
+    __syncthreads();
+    // ---- stage: eight candidates in flight per thread; 32-bit index arithmetic
+    const int total = ng * static_cast<int>(n);
+    const int n32 = static_cast<int>(n);
+    const bool pow2 = (K & (K - 1)) == 0;
+    const int k_shift = __ffs(K) - 1;
+    for (int i0 = tid; i0 < total; i0 += 8 * 256) {
+      unsigned long long kx[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + u * 256;
+        kx[u] = 0ull;
+        if (i < total) {
+          const int g = i / n32, j = i - g * n32;
+          const int r = pow2 ? j >> k_shift : j / K, e = j - r * K;
+          kx[u] = cand_key(p, r * p.rs + (b * p.Hq + kvh * p.G + g0 + g) * p.K + e);
         }
       }
-      if (p.sel)
-        for (int64_t r = i + lane; r < p.topk; r += 32) p.sel[(b * p.Hq + h) * p.topk + r] = -1;
-      if (p.sel_scores)
-        for (int64_t r = i + lane; r < p.topk; r += 32) p.sel_scores[(b * p.Hq + h) * p.topk + r] = -INFINITY;
-      __syncwarp();
-    }
-  } else {
-  for (int64_t g = 0; g < p.G; ++g) {
-    const int64_t h = kvh * p.G + g;
-    __syncthreads();
-    if (tid == 0) sh_valid = 0u;
-    for (int64_t i = tid; i < n; i += 256) {
-      const int64_t r = i / p.K, e = i % p.K;
-      keys[i] = cand_key(p, r * p.rs + (b * p.Hq + h) * p.K + e);
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (i0 + u * 256 < total) keys[i0 + u * 256] = kx[u];
     }
     __syncthreads();
-    // Every block is sorted by key, descending, empty slots last, and keys are unique,
-    // so a candidate's global rank is its position in its own block plus, for every
-    // other block, the number of keys there above it (a binary search).
-    uint32_t my_valid = 0u;
-    for (int64_t i = tid; i < n; i += 256) {
-      const unsigned long long kx = keys[i];
-      if (kx == 0ull) continue;
-      ++my_valid;
-      const int64_t r = i / p.K;
-      int64_t rank = i - r * p.K;
-      for (int64_t r2 = 0; r2 < p.R && rank < p.topk; ++r2) {
-        if (r2 == r) continue;
-        const unsigned long long* blk = keys + r2 * p.K;
-        int64_t a = 0, z = p.K;
-        while (a < z) {
-          const int64_t mid = (a + z) >> 1;
-          if (blk[mid] > kx) a = mid + 1;
-          else z = mid;
-        }
-        rank += a;
-      }
-      if (rank < p.topk) {
-        const int32_t id = static_cast<int32_t>(~static_cast<uint32_t>(kx & 0xffffffffull));
-        if (p.sel) p.sel[(b * p.Hq + h) * p.topk + rank] = id;
-        if (p.sel_scores) p.sel_scores[(b * p.Hq + h) * p.topk + rank] = key_float(static_cast<uint32_t>(kx >> 32));
-        if (id >= lo && id < hi && id - lo < p.max_local) atomicOr(&bits[(id - lo) >> 5], 1u << ((id - lo) & 31));
+    if (warp >= ng) continue;
+    // ---- warp `warp` merges head g0 + warp
+    const int64_t h = kvh * p.G + g0 + warp;
+    const unsigned long long* kw = keys + warp * n;
+    const int64_t r0 = lane, r1 = lane + 32;
+    int64_t p0 = 0, p1 = 0;
+    int64_t i = 0;
+    for (; i < p.topk; ++i) {
+      const unsigned long long k0 = (r0 < p.R && p0 < p.K) ? kw[r0 * p.K + p0] : 0ull;
+      const unsigned long long k1 = (r1 < p.R && p1 < p.K) ? kw[r1 * p.K + p1] : 0ull;
+      const unsigned long long mine = k0 > k1 ? k0 : k1;
+      const uint32_t khi = static_cast<uint32_t>(mine >> 32), klo = static_cast<uint32_t>(mine);
+      const uint32_t hmax = __reduce_max_sync(0xffffffffu, khi);
+      const uint32_t lmax = __reduce_max_sync(0xffffffffu, khi == hmax ? klo : 0u);
+      if (hmax == 0u && lmax == 0u) break;  // every block exhausted (warp-uniform)
+      if (khi == hmax && klo == lmax) {     // the unique winner
+        const int32_t id = static_cast<int32_t>(~lmax);
+        if (p.sel) p.sel[(b * p.Hq + h) * p.topk + i] = id;
+        if (p.sel_scores) p.sel_scores[(b * p.Hq + h) * p.topk + i] = key_float(hmax);
+        if (p.union_ids && id >= lo && id < hi && id - lo < p.max_local)
+          atomicOr(&bits[(id - lo) >> 5], 1u << ((id - lo) & 31));
+        if (k0 > k1) ++p0;
+        else ++p1;
       }
     }
-    atomicAdd(&sh_valid, my_valid);
-    __syncthreads();
-    for (int64_t r = lmin(static_cast<int64_t>(sh_valid), p.topk) + tid; r < p.topk; r += 256) {
+    for (int64_t r = i + lane; r < p.topk; r += 32) {
       if (p.sel) p.sel[(b * p.Hq + h) * p.topk + r] = -1;
       if (p.sel_scores) p.sel_scores[(b * p.Hq + h) * p.topk + r] = -INFINITY;
     }
-  }
   }
   __syncthreads();
   if (p.union_ids == nullptr) return;  // top-k only (a shard's pre-merge of its own chunks)
@@ -204,8 +178,8 @@ extern "C" int linattn_shard_merge(const float* scores, const int32_t* ids, int6
       (union_ids && max_union < 1))
     return set_error(LINATTN_EINVAL, "shard_merge: bad sizes");
   if (rank_stride != 0 && rank_stride < B * Hq * K) return set_error(LINATTN_EINVAL, "shard_merge: rank_stride");
-  if (R * K > 4096 || max_local > (int64_t(1) << 20))
-    return set_error(LINATTN_EUNSUPPORTED, "shard_merge: at most 4096 candidates and 2^20 local pages");
+  if (R * K > 4096 || R > 64 || max_local > (int64_t(1) << 20))
+    return set_error(LINATTN_EUNSUPPORTED, "shard_merge: at most 64 blocks, 4096 candidates and 2^20 local pages");
   if (B * n_kv_heads == 0) return LINATTN_OK;
   ShardMergeParams p;
   p.scores = scores; p.ids = ids; p.R = R; p.B = B; p.Hq = Hq; p.K = K;
@@ -215,21 +189,17 @@ extern "C" int linattn_shard_merge(const float* scores, const int32_t* ids, int6
   if (union_tokens && (!seq_lens || page_size < 1))
     return set_error(LINATTN_EINVAL, "shard_merge: union_tokens needs seq_lens and page_size");
   p.seq_lens = seq_lens; p.P = page_size; p.union_tokens = union_tokens;
-  const size_t bits_bytes = static_cast<size_t>((max_local + 31) / 32) * 4;
+  const size_t bits_bytes = union_ids ? static_cast<size_t>((max_local + 31) / 32) * 4 : 0;
   const size_t head_bytes = static_cast<size_t>(R * K) * 8;
-  // the warp merge for up to 64 blocks, with as many heads per wave as 160 KiB hold
-  const int hpw = static_cast<int>(lmin(lmin(8, p.G), static_cast<int64_t>((160 * 1024) / head_bytes)));
-  const bool warp = R <= 64 && hpw >= 1;
-  const size_t smem = (warp ? hpw : 1) * head_bytes + bits_bytes;
+  // as many heads per pass as 160 KiB hold (at most 8: the per-head counters)
+  const int hpw = static_cast<int>(lmax(1, lmin(lmin(8, p.G), static_cast<int64_t>((160 * 1024) / head_bytes))));
+  const size_t smem = hpw * head_bytes + bits_bytes;
   if (smem > 200 * 1024) return set_error(LINATTN_EUNSUPPORTED, "shard_merge: shared memory");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  cudaError_t e = warp ? cudaFuncSetAttribute(shard_merge_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              static_cast<int>(smem))
-                       : cudaFuncSetAttribute(shard_merge_kernel<false>,
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  cudaError_t e = cudaFuncSetAttribute(shard_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
   if (e == cudaSuccess) {
-    if (warp) shard_merge_kernel<true><<<static_cast<unsigned>(B * n_kv_heads), 256, smem, st>>>(p, hpw);
-    else shard_merge_kernel<false><<<static_cast<unsigned>(B * n_kv_heads), 256, smem, st>>>(p, 1);
+    shard_merge_kernel<<<static_cast<unsigned>(B * n_kv_heads), 256, smem, st>>>(p, hpw);
     e = cudaGetLastError();
   }
   if (e != cudaSuccess) {

@@ -215,8 +215,8 @@ def plan_select_chunks(n: int, g: int, topk: int, d: int, units: int, device, ch
     (sequence, kv head) pairs.  One chunk (the single-CTA form, no merge) when the
     pairs alone fill the GPU and the whole sequence's scores fit in shared memory;
     else chunks small enough for two CTAs per SM and numerous enough for two CTAs per
-    SM.  Returns 0 chunks when the merge's bound (4096 candidates per head across the
-    chunks of all `ranks`; with `premerge`, each rank first merges its own chunks, so
+    SM.  Returns 0 chunks when the merge's bound (64 blocks and 4096 candidates per head
+    across the chunks of all `ranks`; with `premerge`, each rank first merges its own chunks, so
     across the chunks of one rank and across the ranks) or shared memory rules the
     fused kernel out."""
     sms = torch.cuda.get_device_properties(device).multi_processor_count
@@ -235,8 +235,8 @@ def plan_select_chunks(n: int, g: int, topk: int, d: int, units: int, device, ch
         chunk = -(-chunk // 2)
         single = False
     chunks = -(-n // chunk)
-    n_cand = max(chunks, ranks) * topk if premerge else chunks * ranks * topk
-    if n_cand > 4096 or fused_select_smem(chunk, g, topk, d, mma, not single) > _SMEM_MAX:
+    n_blocks = max(chunks, ranks) if premerge else chunks * ranks  # blocks of topk one merge takes
+    if n_blocks * topk > 4096 or n_blocks > 64 or fused_select_smem(chunk, g, topk, d, mma, not single) > _SMEM_MAX:
         return chunk, 0
     return chunk, chunks
 
