@@ -176,7 +176,9 @@ class CudaNSAAttention(AttentionVariant):
         L.require_cuda(q)
         outs = self._branch_outputs(q, state["k"], state["v"], offset)
         g = self._gate_weights(q.dtype, q.device)
-        mixed = torch.einsum("nbhtd,hn->bhtd", outs, g)
+        # three gated terms per head, elementwise (no library GEMV for a 3-term sum)
+        gt = g.t()[:, None, :, None, None]  # (3, 1, H, 1, 1)
+        mixed = (outs[0] * gt[0] + outs[1] * gt[1]) + outs[2] * gt[2]
         return mixed.to(q.dtype)
 
     def stats(self) -> Dict[str, float]:
