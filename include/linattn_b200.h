@@ -407,6 +407,17 @@ int linattn_csa2_pool_quant(const void* x, int32_t dtype, int64_t B, int64_t H, 
                             void* stream);
 
 /*
+ * Measurement utility: reads `bytes` (a multiple of 16, 16-byte aligned) of device
+ * memory `reps` times with a persistent grid of up to min(2 x SMs, sink_words) CTAs,
+ * folding the data into sink[0 .. grid) (uint32 device words, xor-accumulated) so the
+ * loads cannot be elided.  Timed with events, bytes * reps / time is the read roof of a
+ * buffer that stays in L2 (<= ~100 MB) or of HBM (larger).  No counterpart in the
+ * reference: it gives the L2-gather roofline of linattn_token_attention its denominator.
+ */
+int linattn_read_bandwidth(const void* buf, int64_t bytes, int32_t reps, uint32_t* sink, int64_t sink_words,
+                           void* stream);
+
+/*
  * Block selection in one launch: scores, causal top-k and the forced-block merge.
  * Row r of (b, h) (a (B, H_q, R, D), element strides, f32 / f16 / bf16) is scored
  * against the candidates of its kv head h / (H_q / H_kv) (bm (B, H_kv, NC, D)):

@@ -124,6 +124,7 @@ def _declare(lib: ctypes.CDLL) -> None:
                                                  c_vp, c_vp, P(c_i64), c_i64, c_i64, P(c_i64), c_i64, c_i32, c_i64,
                                                  c_i64, ctypes.c_float, c_vp, P(c_i64), c_vp, c_vp, c_vp, c_vp, c_vp]
     lib.linattn_prefill_v_to_f16.argtypes = [c_vp, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp]
+    lib.linattn_read_bandwidth.argtypes = [c_vp, c_i64, c_i32, c_vp, c_i64, c_vp]
     lib.linattn_block_score_topk.argtypes = [c_vp, c_i32, P(c_i64), c_vp, c_i32, P(c_i64), c_i64, c_i64, c_i64,
                                              c_i64, c_i64, c_i64, ctypes.c_float, c_i64, c_i64, c_i64, c_i64, c_i64,
                                              c_i64, c_i64, c_i64, c_i32, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp]
@@ -133,7 +134,7 @@ def _declare(lib: ctypes.CDLL) -> None:
                                                     c_i64, c_vp, c_i64, c_i32, c_i32, c_i64, c_vp, c_vp, c_vp, c_i64,
                                                     c_vp, c_vp, c_vp]
     lib.linattn_lse_combine_strided.argtypes = [c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_i32, c_vp, c_vp]
-    for name in ("linattn_block_score_topk", "linattn_shard_merge", "linattn_quest_decode_candidates", "linattn_lse_combine_strided", "linattn_block_sparse_prefill", "linattn_prefill_v_to_f16", "linattn_block_mean", "linattn_csa2_pool_quant", "linattn_merge_block_lists", "linattn_token_attention", "linattn_indexer_scores", "linattn_row_topk", "linattn_page_bounds", "linattn_paged_page_bounds", "linattn_paged_append", "linattn_quest_scores", "linattn_page_topk",
+    for name in ("linattn_read_bandwidth", "linattn_block_score_topk", "linattn_shard_merge", "linattn_quest_decode_candidates", "linattn_lse_combine_strided", "linattn_block_sparse_prefill", "linattn_prefill_v_to_f16", "linattn_block_mean", "linattn_csa2_pool_quant", "linattn_merge_block_lists", "linattn_token_attention", "linattn_indexer_scores", "linattn_row_topk", "linattn_page_bounds", "linattn_paged_page_bounds", "linattn_paged_append", "linattn_quest_scores", "linattn_page_topk",
                  "linattn_sparse_attention", "linattn_lse_combine", "linattn_lse_combine_strided"):
         getattr(lib, name).restype = ctypes.c_int
 
