@@ -116,12 +116,16 @@ __device__ __forceinline__ void write_selection2(const DecodeSelectParams& p, co
   const int64_t id0 = pg0 + (p.page_base ? static_cast<int64_t>(p.page_base[b]) : 0);
   for (int64_t i = lane; i < n; i += 32) {
     const uint32_t ki = i < na ? key_a[i] : key_b[i - na], ii = i < na ? idx_a[i] : idx_b[i - na];
+    // unrolled so that eight independent shared loads are in flight per step
     int rank = 0;
-    for (int64_t j = 0; j < na; ++j) {
+    const int na32 = static_cast<int>(na), nb32 = static_cast<int>(nb_);
+#pragma unroll 8
+    for (int j = 0; j < na32; ++j) {
       const uint32_t kj = key_a[j], ij = idx_a[j];
       rank += (kj > ki || (kj == ki && ij < ii)) ? 1 : 0;
     }
-    for (int64_t j = 0; j < nb_; ++j) {
+#pragma unroll 8
+    for (int j = 0; j < nb32; ++j) {
       const uint32_t kj = key_b[j], ij = idx_b[j];
       rank += (kj > ki || (kj == ki && ij < ii)) ? 1 : 0;
     }
