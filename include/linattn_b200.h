@@ -368,14 +368,18 @@ int linattn_row_topk(const float* scores, int64_t rows, int64_t n, int64_t row_s
  * aligned); q / K / V bf16 or f16 (one type), D in {64, 128}.  lse_out (B, H_q, T_q)
  * and reads_out (B, H_q, T_q, tokens read) optional.  A query with nothing to read
  * reads token min(offset + t, Tk - 1) with `diag_fallback` (the reference's empty-row
- * rule, selection.py:100-107), else gets o = 0, lse = -inf.
+ * rule, selection.py:100-107), else gets o = 0, lse = -inf.  v_unscale (NULL for a V of
+ * q's type): with bf16 q / K, `v` may instead be an f16 copy of V scaled by a power of
+ * two per (b, kv head) (linattn_prefill_v_to_f16 writes it), v_unscale[b * Hkv + kvh]
+ * the factor that undoes it; P V then takes one f16 P part.
  * Replaces the masked attention of BlockSelectionAttention.attend
  * (src/linattn/variants/selection.py:86-116) for the DSA selection
  * (DSAAttention.select, :738-763), and block_sparse_attention_torch with block_size 1
  * (src/linattn/kernels/triton/block_sparse.py:40-75).
  */
 int linattn_token_attention(const void* q, int32_t dtype, int64_t B, int64_t Hq, int64_t Tq,
-                            const int64_t* q_strides /*[4]*/, const void* k, const void* v, int64_t Hkv, int64_t Tk,
+                            const int64_t* q_strides /*[4]*/, const void* k, const void* v, const float* v_unscale,
+                            int64_t Hkv, int64_t Tk,
                             int64_t D, const int64_t* kv_strides /*[3]*/, const linattn_lists_t* lists, int64_t block,
                             int64_t sink, int64_t window, int32_t causal, int64_t offset, float scale,
                             int32_t diag_fallback, void* out, const int64_t* out_strides /*[4]*/, float* lse_out,

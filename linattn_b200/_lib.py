@@ -112,7 +112,7 @@ def _declare(lib: ctypes.CDLL) -> None:
                                            c_i64, c_i64, c_vp, c_i64, c_vp, c_vp]
     lib.linattn_row_topk.argtypes = [c_vp, c_i64, c_i64, c_i64, c_i64, c_i32, c_i64, c_i64, c_i64, c_i64, c_i32, c_vp,
                                      c_vp, c_vp, c_i64, c_i64, c_vp]
-    lib.linattn_token_attention.argtypes = [c_vp, c_i32, c_i64, c_i64, c_i64, P(c_i64), c_vp, c_vp, c_i64, c_i64,
+    lib.linattn_token_attention.argtypes = [c_vp, c_i32, c_i64, c_i64, c_i64, P(c_i64), c_vp, c_vp, c_vp, c_i64, c_i64,
                                             c_i64, P(c_i64), P(Lists), c_i64, c_i64, c_i64, c_i32, c_i64,
                                             ctypes.c_float, c_i32, c_vp, P(c_i64), c_vp, c_vp, c_vp, c_vp]
     lib.linattn_block_mean.argtypes = [c_vp, c_i32, c_i64, c_i64, c_i64, c_i64, P(c_i64), c_i64, c_vp, c_vp]

@@ -20,7 +20,9 @@
 // cp.async.mbarrier.arrive.noinc (32 arrivals per phase).  The math is the
 // transposed formulation of the paged decode kernel: S^T = K Q^T and O^T += V^T P^T
 // with mma.sync m16n8k16, heads as the N = 8 side, online softmax per head in the
-// log2 domain, P split into 16-bit hi + lo parts.
+// log2 domain (hardware ex2), P split into 16-bit hi + lo parts, or one f16 part when V
+// is given as an f16 copy (a bf16 V scaled by a power of two per (b, kv head), undone
+// on the output).
 #include <cstdio>
 
 #include "launchers.cuh"
@@ -46,6 +48,7 @@ struct TokenAttnParams {
   float* lse_out;
   int32_t* reads_out;  // (B, H_q, T_q) tokens read per query, or NULL
   int diag_fallback;   // a query with nothing to read reads token min(offset + t, T_k - 1)
+  const float* v_unscale;  // non-NULL: V is an f16 copy scaled per (b, kv head); o is multiplied back
   int32_t* status;
   int64_t heads_per_kv, heads_per_list, chunk_heads, n_items;
 };
@@ -73,7 +76,15 @@ __device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
 
 }  // namespace
 
-template <typename T, int D>
+__device__ __forceinline__ float tok_ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// VF16: V arrives as an f16 copy (exact for a bf16 V scaled by a power of two per
+// (b, kv head)), so P V takes one f16 P part instead of 16-bit hi + lo parts.
+template <typename T, int D, bool VF16>
 __global__ void __launch_bounds__(32 * TNW, 1) token_attention_kernel(const TokenAttnParams p) {
   using S = MmaShape<D>;
   using M = MmaOp<T>;
@@ -272,15 +283,15 @@ __global__ void __launch_bounds__(32 * TNW, 1) token_attention_kernel(const Toke
       tB = fmaxf(tB, __shfl_xor_sync(0xffffffffu, tB, off));
     }
     const float nA = fmaxf(mA, tA), nB = fmaxf(mB, tB);
-    const float aA = nA == -INFINITY ? 1.f : exp2f(mA - nA);
-    const float aB = nB == -INFINITY ? 1.f : exp2f(mB - nB);
+    const float aA = nA == -INFINITY ? 1.f : tok_ex2(mA - nA);
+    const float aB = nB == -INFINITY ? 1.f : tok_ex2(mB - nB);
     float sA = 0.f, sB = 0.f;
 #pragma unroll
     for (int mt = 0; mt < S::MT; ++mt) {
-      sc[mt][0] = nA == -INFINITY ? 0.f : exp2f(sc[mt][0] - nA);
-      sc[mt][2] = nA == -INFINITY ? 0.f : exp2f(sc[mt][2] - nA);
-      sc[mt][1] = nB == -INFINITY ? 0.f : exp2f(sc[mt][1] - nB);
-      sc[mt][3] = nB == -INFINITY ? 0.f : exp2f(sc[mt][3] - nB);
+      sc[mt][0] = nA == -INFINITY ? 0.f : tok_ex2(sc[mt][0] - nA);
+      sc[mt][2] = nA == -INFINITY ? 0.f : tok_ex2(sc[mt][2] - nA);
+      sc[mt][1] = nB == -INFINITY ? 0.f : tok_ex2(sc[mt][1] - nB);
+      sc[mt][3] = nB == -INFINITY ? 0.f : tok_ex2(sc[mt][3] - nB);
       sA += sc[mt][0] + sc[mt][2];
       sB += sc[mt][1] + sc[mt][3];
     }
@@ -302,6 +313,18 @@ __global__ void __launch_bounds__(32 * TNW, 1) token_attention_kernel(const Toke
     }
 #pragma unroll
     for (int mt = 0; mt < S::MT; ++mt) {
+      if constexpr (VF16) {
+        using MH = MmaOp<__half>;
+        const uint32_t bh0 = movmatrix_t(MH::pack(sc[mt][0], sc[mt][1]));
+        const uint32_t bh1 = movmatrix_t(MH::pack(sc[mt][2], sc[mt][3]));
+#pragma unroll
+        for (int dm = 0; dm < S::KS; ++dm) {
+          uint32_t a[4];
+          ldsm_x4_t(vst + swz<D>(mt * 16 + (mi >> 1) * 8 + ri, dm * 2 + (mi & 1)), a[0], a[1], a[2], a[3]);
+          MH::mma(o[dm], a, bh0, bh1);
+        }
+        continue;
+      }
       const uint32_t h0p = M::pack(sc[mt][0], sc[mt][1]);
       const uint32_t h1p = M::pack(sc[mt][2], sc[mt][3]);
       const float2 r0 = M::unpack(h0p), r1 = M::unpack(h1p);
@@ -327,7 +350,8 @@ __global__ void __launch_bounds__(32 * TNW, 1) token_attention_kernel(const Toke
     return;
   }
   // ---- (o, lse) of the item's heads
-  const float iA = lA > 0.f ? 1.f / lA : 0.f, iB = lB > 0.f ? 1.f / lB : 0.f;
+  const float vs = VF16 ? p.v_unscale[b * (p.Hq / p.heads_per_kv) + kvh] : 1.f;
+  const float iA = lA > 0.f ? vs / lA : 0.f, iB = lB > 0.f ? vs / lB : 0.f;
   const float lseA = lA > 0.f ? (mA + log2f(lA)) * 0.69314718055994531f : -INFINITY;
   const float lseB = lB > 0.f ? (mB + log2f(lB)) * 0.69314718055994531f : -INFINITY;
 #pragma unroll
@@ -352,7 +376,7 @@ namespace {
 template <typename T, int D>
 cudaError_t launch_tok(const TokenAttnParams& p, cudaStream_t st) {
   constexpr size_t smem = 1024 + static_cast<size_t>(TNW) * TSTG * MmaShape<D>::STAGE_BYTES;
-  auto kern = token_attention_kernel<T, D>;
+  auto kern = p.v_unscale ? token_attention_kernel<T, D, true> : token_attention_kernel<T, D, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   const unsigned grid = static_cast<unsigned>((p.n_items + TNW - 1) / TNW);
@@ -363,6 +387,7 @@ cudaError_t launch_tok(const TokenAttnParams& p, cudaStream_t st) {
 }  // namespace
 
 cudaError_t launch_token_attention(const TokenAttnParams& p, int dtype, int D, cudaStream_t st) {
+  if (p.v_unscale && dtype != LINATTN_BF16) return cudaErrorInvalidValue;
   if (dtype == LINATTN_BF16) {
     if (D == 128) return launch_tok<__nv_bfloat16, 128>(p, st);
     if (D == 64) return launch_tok<__nv_bfloat16, 64>(p, st);
@@ -378,7 +403,8 @@ cudaError_t launch_token_attention(const TokenAttnParams& p, int dtype, int D, c
 using namespace linattn;
 
 extern "C" int linattn_token_attention(const void* q, int32_t dtype, int64_t B, int64_t Hq, int64_t Tq,
-                                       const int64_t* q_strides, const void* k, const void* v, int64_t Hkv,
+                                       const int64_t* q_strides, const void* k, const void* v,
+                                       const float* v_unscale, int64_t Hkv,
                                        int64_t Tk, int64_t D, const int64_t* kv_strides,
                                        const linattn_lists_t* lists, int64_t block, int64_t sink, int64_t window,
                                        int32_t causal,
@@ -389,6 +415,8 @@ extern "C" int linattn_token_attention(const void* q, int32_t dtype, int64_t B, 
     return set_error(LINATTN_EINVAL, "token_attention: NULL pointer");
   if (dtype != LINATTN_BF16 && dtype != LINATTN_F16)
     return set_error(LINATTN_EUNSUPPORTED, "token_attention: q / K / V must be bf16 or f16 (one type)");
+  if (v_unscale && dtype != LINATTN_BF16)
+    return set_error(LINATTN_EINVAL, "token_attention: an f16 V copy (v_unscale) goes with bf16 q / K");
   if (D != 64 && D != 128) return set_error(LINATTN_EUNSUPPORTED, "token_attention: head_dim must be 64 or 128");
   if (Hkv < 1 || Hq % Hkv) return set_error(LINATTN_EINVAL, "token_attention: H_q must be a multiple of H_kv");
   if (lists->n_heads < 1 || Hq % lists->n_heads)
@@ -412,6 +440,7 @@ extern "C" int linattn_token_attention(const void* q, int32_t dtype, int64_t B, 
   p.sink = sink; p.window = window; p.block = block; p.causal = causal; p.offset = offset;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.out = out; p.lse_out = lse_out; p.reads_out = reads_out; p.diag_fallback = diag_fallback ? 1 : 0;
+  p.v_unscale = v_unscale;
   p.status = status;
   p.heads_per_kv = hpk; p.heads_per_list = hpl;
   // a chunk: consecutive heads sharing a kv head and a list, at most 8 (a divisor of both)

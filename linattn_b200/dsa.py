@@ -31,12 +31,13 @@ def token_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, id
                            scale: Optional[float] = None, counts: Optional[torch.Tensor] = None,
                            diag_fallback: bool = True, lse_out: Optional[torch.Tensor] = None,
                            reads_out: Optional[torch.Tensor] = None,
-                           out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                           out: Optional[torch.Tensor] = None, v_f16: bool = True) -> torch.Tensor:
     """``q (B,H_q,T_q,D)`` over ``k, v (B,H_kv,T_k,D)``; ``ids (B,H_l,T_q,N)`` (or
     ``(B,H_l,N)`` shared by all queries) with ``H_q % H_l == 0``; negative ids are padding.
     ``diag_fallback``: a query with nothing to read reads its own position (the
     reference's empty-row rule); ``reads_out`` (B,H_q,T_q) int32 receives the number of
-    tokens each query read."""
+    tokens each query read.  ``v_f16`` (bf16 inputs, contiguous K / V): P V on an f16
+    copy of V with one f16 P part (one extra pass over V)."""
     dev = L.require_cuda(q, k, v, ids, counts, lse_out, reads_out)
     if q.dim() != 4 or k.dim() != 4 or k.shape != v.shape:
         raise ValueError("q must be (B,H_q,T_q,D) and k, v (B,H_kv,T_k,D) of one shape")
@@ -55,8 +56,18 @@ def token_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, id
         out = torch.empty_like(q, memory_format=torch.contiguous_format)
     scale = (1.0 / math.sqrt(d)) if scale is None else float(scale)
     status = L.status_word(dev)
+    v_arg, v_unscale = v, None
+    if q.dtype == torch.bfloat16 and v_f16 and v.is_contiguous() and k.stride() == v.stride():
+        # an f16 copy of V, scaled by a power of two per (b, kv head), so that P V takes
+        # one f16 P part (the scale is undone on the output)
+        v_arg = torch.empty(v.shape, dtype=torch.float16, device=dev)
+        v_unscale = torch.empty(b * hkv, dtype=torch.float32, device=dev)
+        amax = torch.empty(b * hkv, dtype=torch.int32, device=dev)
+        L.check(L.lib().linattn_prefill_v_to_f16(v.data_ptr(), b * hkv, tk * d, v_arg.data_ptr(),
+                                                 v_unscale.data_ptr(), amax.data_ptr(), L.stream_of(q)))
     L.check(L.lib().linattn_token_attention(
-        q.data_ptr(), L.dtype_code(q), b, hq, tq, L.strides4(q), k.data_ptr(), v.data_ptr(), hkv, tk, d,
+        q.data_ptr(), L.dtype_code(q), b, hq, tq, L.strides4(q), k.data_ptr(), v_arg.data_ptr(), L.ptr(v_unscale),
+        hkv, tk, d,
         (L.c_i64 * 3)(k.stride(0), k.stride(1), k.stride(2)), lists, block, sink, window, int(causal), offset, scale,
         int(diag_fallback), out.data_ptr(), L.strides4(out), L.ptr(lse_out), L.ptr(reads_out), status.data_ptr(),
         L.stream_of(q)))

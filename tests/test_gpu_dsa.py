@@ -79,11 +79,14 @@ def test_token_attention_vs_oracle(cuda, dtype, d, hq, hkv, hl):
     ids = torch.stack([torch.randperm(tk, generator=g)[:n] for _ in range(b * hl * tq)]).view(b, hl, tq, n)
     ids[..., -3:] = -1
     ids = ids.to(torch.int32)
-    for sink, window in ((0, 0), (3, 16)):
+    # bf16: P V on an f16 copy of V with one P part (the default) and on V itself with
+    # hi + lo P parts
+    for (sink, window), vf in [(sw, vf) for sw in ((0, 0), (3, 16))
+                               for vf in ((True, False) if dtype == torch.bfloat16 else (True,))]:
         reads = torch.empty(b, hq, tq, dtype=torch.int32, device=cuda)
         lse = torch.empty(b, hq, tq, dtype=torch.float32, device=cuda)
         out = token_sparse_attention(q.to(cuda), k.to(cuda), v.to(cuda), ids.to(cuda), sink=sink, window=window,
-                                     offset=offset, reads_out=reads, lse_out=lse)
+                                     offset=offset, reads_out=reads, lse_out=lse, v_f16=vf)
         mask = read_mask(ids.numpy(), 1, sink, window, tq, tk, offset, hq)
         assert_close_16(out, _oracle(q, k, v, mask), dtype)
         assert np.array_equal(reads.cpu().numpy(), mask.sum(-1))
