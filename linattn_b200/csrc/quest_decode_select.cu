@@ -258,6 +258,104 @@ __device__ __forceinline__ void select_head_reg(const DecodeSelectParams& p, con
 // barrier warp g ranks the two halves' picks together (a pick of the head's top kb is
 // in its half's top kb, ties included, since its half holds no more keys that beat it).
 // Every thread of the CTA calls this (the split form has a CTA-wide barrier).
+__device__ __forceinline__ void write_one(const DecodeSelectParams& p, const float* srow, int rank, uint32_t ki,
+                                          uint32_t ii, uint32_t neg_inf_key, int64_t off, int64_t id0,
+                                          uint32_t* bitmap) {
+  if (p.cand_scores) {
+    p.cand_scores[off + rank] = srow[ii];
+    p.cand_ids[off + rank] = static_cast<int32_t>(id0 + ii);
+  } else {
+    p.ids[off + rank] = static_cast<int32_t>(ii);
+    if (ki > neg_inf_key) atomicOr(&bitmap[ii >> 5], 1u << (ii & 31u));
+  }
+}
+
+// (score desc, index asc) as one descending 64-bit key: score key high, ~index low
+__device__ __forceinline__ unsigned long long pick_key(uint32_t key, uint32_t idx) {
+  return (static_cast<unsigned long long>(key) << 32) | static_cast<uint32_t>(~idx);
+}
+
+// A warp sorts its n <= 64 picks (sel_idx / sel_key) by (score desc, index asc) in
+// place: a bitonic network over 64 positions, two per lane (lane and lane + 32).
+__device__ __forceinline__ void sort_picks_desc(uint32_t* sel_idx, uint32_t* sel_key, int n, int lane) {
+  unsigned long long v[2];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int e = lane + 32 * r;
+    v[r] = e < n ? pick_key(sel_key[e], sel_idx[e]) : 0ull;  // empty slots sort last
+  }
+#pragma unroll
+  for (int k = 2; k <= 64; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j == 32) {  // k == 64: positions lane and lane + 32, the lower keeps the larger
+        const unsigned long long mx = v[0] > v[1] ? v[0] : v[1], mn = v[0] > v[1] ? v[1] : v[0];
+        v[0] = mx;
+        v[1] = mn;
+      } else {
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const int pos = lane + 32 * r;
+          const unsigned long long other = __shfl_xor_sync(0xffffffffu, v[r], j);
+          // descending overall: in a block sorted downwards the lower position keeps
+          // the larger key, in one sorted upwards the smaller
+          const bool keep_max = ((pos & j) == 0) == ((pos & k) == 0);
+          const unsigned long long mx = v[r] > other ? v[r] : other, mn = v[r] > other ? other : v[r];
+          v[r] = keep_max ? mx : mn;
+        }
+      }
+    }
+  }
+  __syncwarp();
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int e = lane + 32 * r;
+    if (e < n) {
+      sel_key[e] = static_cast<uint32_t>(v[r] >> 32);
+      sel_idx[e] = ~static_cast<uint32_t>(v[r]);
+    }
+  }
+  __syncwarp();
+}
+
+// Ranks of two lists each sorted by (score desc, index asc): an entry's rank is its
+// position in its own list plus the number of entries of the other list above it (a
+// binary search); the first kb by rank are written.
+__device__ __forceinline__ void write_sorted_pair(const DecodeSelectParams& p, const float* srow,
+                                                  const uint32_t* idx_a, const uint32_t* key_a, int na,
+                                                  const uint32_t* idx_b, const uint32_t* key_b, int nb_, int64_t kb,
+                                                  uint32_t* bitmap, int64_t pg0, int64_t b, int64_t h, int lane) {
+  const uint32_t neg_inf_key = float_key(-INFINITY);
+  const bool cand = p.cand_scores != nullptr;
+  const int64_t off = cand ? static_cast<int64_t>(blockIdx.y) * p.cand_stride + (b * p.Hq + h) * p.topk
+                           : (b * p.Hq + h) * p.topk;
+  const int64_t id0 = pg0 + (p.page_base ? static_cast<int64_t>(p.page_base[b]) : 0);
+  for (int e = lane; e < na + nb_; e += 32) {
+    const bool in_a = e < na;
+    const int i = in_a ? e : e - na;
+    const uint32_t ki = in_a ? key_a[i] : key_b[i], ii = in_a ? idx_a[i] : idx_b[i];
+    const unsigned long long me = pick_key(ki, ii);
+    const uint32_t* ok = in_a ? key_b : key_a;
+    const uint32_t* oi = in_a ? idx_b : idx_a;
+    int lo = 0, hi = in_a ? nb_ : na;  // first position of the other list below `me`
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (pick_key(ok[mid], oi[mid]) > me) lo = mid + 1;
+      else hi = mid;
+    }
+    const int rank = i + lo;
+    if (rank < kb) write_one(p, srow, rank, ki, ii, neg_inf_key, off, id0, bitmap);
+  }
+  for (int64_t r = kb + lane; r < p.topk; r += 32) {
+    if (cand) {
+      p.cand_scores[off + r] = -INFINITY;
+      p.cand_ids[off + r] = -1;
+    } else {
+      p.ids[off + r] = -1;
+    }
+  }
+}
+
 template <int G, int ITEMS>
 __device__ __forceinline__ void select_heads_split(const DecodeSelectParams& p, const float* sc, uint32_t* bitmap,
                                                    uint32_t* sel, int64_t nb, int64_t pg0, int64_t b, int64_t kvh,
@@ -267,6 +365,7 @@ __device__ __forceinline__ void select_heads_split(const DecodeSelectParams& p, 
   const int64_t n0 = (nb + 1) / 2;
   const float* srow = sc + g * p.chunk;
   const int64_t h = kvh * G + g;
+  const bool sorted = kb <= 64;  // picks per half fit the 64-position sort
   if (warp < 2 * G) {
     if (p.scores && half == 0) {
       float* dst = p.scores + (b * p.Hq + h) * p.max_pages + pg0;
@@ -275,13 +374,21 @@ __device__ __forceinline__ void select_heads_split(const DecodeSelectParams& p, 
     }
     const int64_t off = half ? n0 : 0, n = half ? nb - n0 : n0;
     select_head_reg<ITEMS>(p, srow + off, sel, bitmap, n, pg0, b, h, warp, lane, off);
+    if (sorted) {
+      uint32_t* si = sel + warp * 2 * p.topk;
+      sort_picks_desc(si, si + p.topk, static_cast<int>(lmin(kb, n)), lane);
+    }
   }
   __syncthreads();
   if (warp < G) {
     const uint32_t* a = sel + g * 2 * p.topk;
     const uint32_t* c = sel + (g + G) * 2 * p.topk;
-    write_selection2(p, srow, a, a + p.topk, lmin(kb, n0), c, c + p.topk, lmin(kb, nb - n0), kb, bitmap, pg0, b, h,
-                     lane);
+    if (sorted)
+      write_sorted_pair(p, srow, a, a + p.topk, static_cast<int>(lmin(kb, n0)), c, c + p.topk,
+                        static_cast<int>(lmin(kb, nb - n0)), kb, bitmap, pg0, b, h, lane);
+    else
+      write_selection2(p, srow, a, a + p.topk, lmin(kb, n0), c, c + p.topk, lmin(kb, nb - n0), kb, bitmap, pg0, b,
+                       h, lane);
   }
 }
 
