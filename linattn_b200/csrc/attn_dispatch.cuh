@@ -65,9 +65,19 @@ static cudaError_t launch_mma_d(const AttnParams& p, const CUtensorMap& tmk, con
   }
   const int64_t want = (n_items + S::NW - 1) / S::NW;
   const int grid = static_cast<int>(lmax(1, lmin(sm_count(), want)));
-  sparse_attention_mma_kernel<T, D, NQT><<<grid, 32 * S::NW, S::SMEM_BYTES, stream>>>(p, tmk, tmv, box_rows,
-                                                                                  counter, n_items);
-  return cudaGetLastError();
+  // programmatic dependent launch: the CTAs may start (set-up only) while the
+  // previous kernel in the stream finishes; griddepcontrol.wait orders every read
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(32 * S::NW);
+  cfg.dynamicSmemBytes = S::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, sparse_attention_mma_kernel<T, D, NQT>, p, tmk, tmv, box_rows, counter, n_items);
 }
 
 template <typename T>

@@ -330,7 +330,9 @@ int linattn_sparse_attention_out(const void* q, int32_t q_dtype, int64_t B, int6
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e;
   if (mma_path) {
-    e = cudaMemsetAsync(counter, 0, sizeof(int), st);
+    // a kernel, not a memset node, so that the chain selection -> clear -> attention
+    // stays kernel to kernel (programmatic dependent launches)
+    e = launch_attn_counters_clear(counter, kWsHeader, st);
     if (e == cudaSuccess)
       e = kv->dtype == LINATTN_BF16  ? launch_sparse_attention_mma_bf16(p, tmk, tmv, box_rows, D, counter, blocks, st)
           : kv->dtype == LINATTN_F16 ? launch_sparse_attention_mma_f16(p, tmk, tmv, box_rows, D, counter, blocks, st)

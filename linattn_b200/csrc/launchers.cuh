@@ -45,6 +45,9 @@ cudaError_t launch_page_topk(const TopkParams& p, cudaStream_t stream);
 cudaError_t launch_lse_combine(const float* o_parts, const float* lse_parts, int64_t S, int64_t rows, int64_t D,
                                void* out, int out_dtype, int64_t H, int64_t Tq, const int64_t* os, float* lse_out,
                                cudaStream_t stream, int64_t o_part_stride = 0, int64_t lse_part_stride = 0);
+// Zeroes `bytes` (a multiple of 16) at `words` as a programmatic-dependent kernel that
+// ends after the stream's previous kernel (lse_combine.cu).
+cudaError_t launch_attn_counters_clear(void* words, int64_t bytes, cudaStream_t stream);
 cudaError_t launch_sparse_attention_f32(const AttnParams& p, int D, int G, unsigned grid, cudaStream_t stream);
 cudaError_t launch_sparse_attention_f16(const AttnParams& p, int D, int G, unsigned grid, cudaStream_t stream);
 cudaError_t launch_sparse_attention_bf16(const AttnParams& p, int D, int G, unsigned grid, cudaStream_t stream);

@@ -19,6 +19,8 @@ __global__ void __launch_bounds__(256) lse_combine_kernel(const float* __restric
                                                           void* out, int out_dtype,
                                                           int64_t H, int64_t Tq, int64_t os0, int64_t os1,
                                                           int64_t os2, int64_t os3, float* lse_out) {
+  // a programmatic dependent of the attention launch: the parts are its output
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int64_t row = blockIdx.x;
   const int c = threadIdx.x, lane = c & 31;
   float L = -INFINITY;
@@ -49,6 +51,32 @@ __global__ void __launch_bounds__(256) lse_combine_kernel(const float* __restric
   if (lse_out && c == 0) lse_out[row] = W > 0.f ? L + logf(W) : -INFINITY;
 }
 
+// Clears the tensor-core attention's work counter (the workspace header) in place of a
+// memset node, as a kernel that can itself start early behind the previous
+// kernel (programmatic dependent launch) and lets the attention launch behind it: it
+// clears, allows its dependents, then waits for its own prerequisite so that it ends
+// only after the previous kernel (whose results the attention reads) has ended.
+__global__ void __launch_bounds__(256) attn_counters_clear_kernel(int4* __restrict__ words, int n16) {
+  for (int i = threadIdx.x; i < n16; i += blockDim.x) words[i] = make_int4(0, 0, 0, 0);
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+cudaError_t launch_attn_counters_clear(void* words, int64_t bytes, cudaStream_t stream) {
+  if (bytes <= 0 || bytes % 16 || bytes > (int64_t{1} << 30)) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, attn_counters_clear_kernel, static_cast<int4*>(words), static_cast<int>(bytes / 16));
+}
+
 cudaError_t launch_lse_combine(const float* o_parts, const float* lse_parts, int64_t S, int64_t rows, int64_t D,
                                void* out, int out_dtype, int64_t H, int64_t Tq, const int64_t* os, float* lse_out,
                                cudaStream_t stream, int64_t o_part_stride, int64_t lse_part_stride) {
@@ -56,10 +84,18 @@ cudaError_t launch_lse_combine(const float* o_parts, const float* lse_parts, int
   const int threads = static_cast<int>(lmax(32, (D + 31) / 32 * 32));
   const int64_t o_ps = o_part_stride > 0 ? o_part_stride : rows * D;
   const int64_t l_ps = lse_part_stride > 0 ? lse_part_stride : rows;
-  lse_combine_kernel<<<static_cast<unsigned>(rows), threads, 0, stream>>>(o_parts, lse_parts, S, rows, D, o_ps,
-                                                                           l_ps, out, out_dtype, H, Tq, os[0],
-                                                                           os[1], os[2], os[3], lse_out);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(rows));
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, lse_combine_kernel, o_parts, lse_parts, S, rows, D, o_ps, l_ps, out, out_dtype, H,
+                            Tq, os[0], os[1], os[2], os[3], lse_out);
 }
 
 }  // namespace linattn

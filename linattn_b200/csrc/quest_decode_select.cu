@@ -549,6 +549,9 @@ __global__ void __launch_bounds__(256, 1) quest_decode_select_kernel(const Decod
   __shared__ uint32_t scan_tmp[9];
   __shared__ uint32_t sh_tokens;
 
+  // the attention launch that follows (a programmatic dependent) may start its set-up
+  // now; its reads of what this grid writes wait for this grid's end
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t kvh = blockIdx.x % p.Hkv, b = blockIdx.x / p.Hkv;
   const int64_t nb_all = lmin(p.n_pages_b[b], p.max_pages);  // the sequence's pages
@@ -723,6 +726,9 @@ __global__ void __launch_bounds__(288, 2) quest_select_mma_kernel(const DecodeSe
   __shared__ uint32_t scan_tmp[10];
   __shared__ uint32_t sh_tokens;
 
+  // the attention launch that follows (a programmatic dependent) may start its set-up
+  // now; its reads of what this grid writes wait for this grid's end
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t kvh = blockIdx.x % p.Hkv, b = blockIdx.x / p.Hkv;
   const int64_t nb_all = lmin(p.n_pages_b[b], p.max_pages);

@@ -209,6 +209,12 @@ __global__ void __launch_bounds__(32 * MmaShape<D, sizeof(T)>::NW, 1)
     reinterpret_cast<uint4*>(ring)[i] = make_uint4(0u, 0u, 0u, 0u);
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   __syncwarp();
+  // launched as a programmatic dependent: everything above is set-up; the lists, the
+  // counter and q may come from the previous kernel, so wait for it (a no-op when
+  // nothing is in flight before this launch).  The split merge behind this launch may
+  // start its own set-up now.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   const int64_t S_ = p.n_splits;
   const int64_t P = p.kv.page_size;
