@@ -52,11 +52,60 @@ __device__ __forceinline__ unsigned long long cand_key(const ShardMergeParams& p
                  : 0ull;  // empty slots rank last
 }
 
+// Merge-path tree over the R sorted blocks of one head (topk <= 256), one warp: level
+// by level, blocks j and j + s (s = 1, 2, 4, ...) merge into the top min(topk, La + Lb)
+// keys at block j's place.  Output o of a merge is found on its own: i = the number of
+// A keys among the first o outputs is the first mid in [max(0, o - Lb), min(o, La)]
+// with A[mid] < B[o - 1 - mid] (A wins ties, which only empty slots have: keys are
+// unique), and output o = max(A[i], B[o - i]).  A lane computes outputs lane, lane +
+// 32, ... into registers; they overwrite the blocks after the whole merge has read
+// them.  Returns the merged length; block 0 then holds the keys in order.
+__device__ __forceinline__ int tree_merge_blocks(unsigned long long* kw, int R, int K, int topk, int lane) {
+  const int L0 = K < topk ? K : topk;
+  // at level s, block j (a multiple of 2s) holds the merge of original blocks j ..
+  // min(R, j + s) - 1, truncated to topk
+  for (int s = 1; s < R; s <<= 1) {
+    for (int j = 0; j + s < R; j += 2 * s) {
+      const int na = s, nb = (R - j - s) < s ? (R - j - s) : s;
+      const int La = na * L0 < topk ? na * L0 : topk, Lb = nb * L0 < topk ? nb * L0 : topk;
+      const int Lo = La + Lb < topk ? La + Lb : topk;
+      const unsigned long long* A = kw + j * K;
+      const unsigned long long* B = kw + (j + s) * K;
+      unsigned long long out[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const int o = lane + 32 * c;
+        out[c] = 0ull;
+        if (o < Lo) {
+          int lo = o - Lb > 0 ? o - Lb : 0, hi = o < La ? o : La;
+          while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (A[mid] >= B[o - 1 - mid]) lo = mid + 1;
+            else hi = mid;
+          }
+          const unsigned long long a = lo < La ? A[lo] : 0ull, b = o - lo < Lb ? B[o - lo] : 0ull;
+          out[c] = a >= b ? a : b;
+        }
+      }
+      __syncwarp();
+      unsigned long long* dst = kw + j * K;
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        if (lane + 32 * c < Lo) dst[lane + 32 * c] = out[c];
+      __syncwarp();
+    }
+  }
+  return R * L0 < topk ? R * L0 : topk;
+}
+
 // The keys of `hpw` heads at a time are staged in shared memory by all threads
 // (eight loads in flight per thread: the staging is latency-bound otherwise); then one
-// warp per head merges the R sorted blocks (R <= 64, two per lane): each step the warp
-// takes the largest block head (two 32-bit warp max-reductions over the unique 64-bit
-// keys) and that block advances, so the top-k come out in order after k steps.
+// warp per head merges the R sorted blocks: up to 4 blocks by the merge-path tree, more
+// (R <= 64, two per lane) step by step: each step the warp takes the largest block head
+// (two 32-bit warp max-reductions over the unique 64-bit keys, the heads and the keys
+// after them held in registers) and that block advances, so the top-k come out in order
+// after k steps.
+template <bool TREE>
 __global__ void __launch_bounds__(256) shard_merge_kernel(const ShardMergeParams p, int hpw) {
   extern __shared__ unsigned long long msm[];
   const int64_t n = p.R * p.K;
@@ -100,28 +149,60 @@ __global__ void __launch_bounds__(256) shard_merge_kernel(const ShardMergeParams
     }
     __syncthreads();
     if (warp >= ng) continue;
-    // ---- warp `warp` merges head g0 + warp
+    // ---- warp `warp` merges head g0 + warp.  A lane holds the heads of its blocks
+    // (lane, lane + 32) and the key after each in registers: a step is the two
+    // reductions and the winner's advance, whose next load is off the step's chain.
     const int64_t h = kvh * p.G + g0 + warp;
     const unsigned long long* kw = keys + warp * n;
-    const int64_t r0 = lane, r1 = lane + 32;
-    int64_t p0 = 0, p1 = 0;
-    int64_t i = 0;
-    for (; i < p.topk; ++i) {
-      const unsigned long long k0 = (r0 < p.R && p0 < p.K) ? kw[r0 * p.K + p0] : 0ull;
-      const unsigned long long k1 = (r1 < p.R && p1 < p.K) ? kw[r1 * p.K + p1] : 0ull;
-      const unsigned long long mine = k0 > k1 ? k0 : k1;
+    const int R32 = static_cast<int>(p.R);
+    const bool has0 = lane < R32, has1 = lane + 32 < R32;
+    const unsigned long long* b0 = kw + (has0 ? lane * K : 0);
+    const unsigned long long* b1 = kw + (has1 ? (lane + 32) * K : 0);
+    int p0 = 0, p1 = 0;
+    unsigned long long h0 = has0 ? b0[0] : 0ull, h1 = has1 ? b1[0] : 0ull;
+    unsigned long long n0 = has0 && K > 1 ? b0[1] : 0ull, n1 = has1 && K > 1 ? b1[1] : 0ull;
+    const int topk = static_cast<int>(p.topk);
+    int32_t* sel_row = p.sel ? p.sel + (b * p.Hq + h) * p.topk : nullptr;
+    float* sc_row = p.sel_scores ? p.sel_scores + (b * p.Hq + h) * p.topk : nullptr;
+    int i = 0;
+    // TREE (up to 4 blocks, topk <= 256): block 0 ends up holding the top keys in order
+    if constexpr (TREE) {
+      unsigned long long* kwm = keys + warp * n;
+      const int m = tree_merge_blocks(kwm, R32, K, topk, lane);
+      int valid = 0;  // keys before the first empty slot
+      for (int o = lane; o < m; o += 32) {
+        const unsigned long long key = kwm[o];
+        valid += key != 0ull;
+        if (key == 0ull) continue;
+        const int32_t id = static_cast<int32_t>(~static_cast<uint32_t>(key));
+        if (sel_row) sel_row[o] = id;
+        if (sc_row) sc_row[o] = key_float(static_cast<uint32_t>(key >> 32));
+        if (p.union_ids && id >= lo && id < hi && id - lo < p.max_local)
+          atomicOr(&bits[(id - lo) >> 5], 1u << ((id - lo) & 31));
+      }
+      i = __reduce_add_sync(0xffffffffu, static_cast<uint32_t>(valid));
+    }
+    for (; i < topk && !TREE; ++i) {
+      const unsigned long long mine = h0 > h1 ? h0 : h1;
       const uint32_t khi = static_cast<uint32_t>(mine >> 32), klo = static_cast<uint32_t>(mine);
       const uint32_t hmax = __reduce_max_sync(0xffffffffu, khi);
       const uint32_t lmax = __reduce_max_sync(0xffffffffu, khi == hmax ? klo : 0u);
       if (hmax == 0u && lmax == 0u) break;  // every block exhausted (warp-uniform)
       if (khi == hmax && klo == lmax) {     // the unique winner
         const int32_t id = static_cast<int32_t>(~lmax);
-        if (p.sel) p.sel[(b * p.Hq + h) * p.topk + i] = id;
-        if (p.sel_scores) p.sel_scores[(b * p.Hq + h) * p.topk + i] = key_float(hmax);
+        if (sel_row) sel_row[i] = id;
+        if (sc_row) sc_row[i] = key_float(hmax);
         if (p.union_ids && id >= lo && id < hi && id - lo < p.max_local)
           atomicOr(&bits[(id - lo) >> 5], 1u << ((id - lo) & 31));
-        if (k0 > k1) ++p0;
-        else ++p1;
+        if (h0 > h1) {
+          h0 = n0;
+          ++p0;
+          n0 = p0 + 1 < K ? b0[p0 + 1] : 0ull;
+        } else {
+          h1 = n1;
+          ++p1;
+          n1 = p1 + 1 < K ? b1[p1 + 1] : 0ull;
+        }
       }
     }
     for (int64_t r = i + lane; r < p.topk; r += 32) {
@@ -196,10 +277,14 @@ extern "C" int linattn_shard_merge(const float* scores, const int32_t* ids, int6
   const size_t smem = hpw * head_bytes + bits_bytes;
   if (smem > 200 * 1024) return set_error(LINATTN_EUNSUPPORTED, "shard_merge: shared memory");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaFuncSetAttribute(shard_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
+  // few blocks: the merge-path tree (log2 R levels of parallel outputs); more blocks:
+  // the step-by-step k-way merge (the tree's work grows as R x topk: config 5's 8 ranks
+  // x 64 keys take the k-way merge 35 us, the tree as long; 16 chunks 54 us against 65)
+  const bool tree = topk <= 256 && R <= 4;
+  auto kern = tree ? shard_merge_kernel<true> : shard_merge_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e == cudaSuccess) {
-    shard_merge_kernel<<<static_cast<unsigned>(B * n_kv_heads), 256, smem, st>>>(p, hpw);
+    kern<<<static_cast<unsigned>(B * n_kv_heads), 256, smem, st>>>(p, hpw);
     e = cudaGetLastError();
   }
   if (e != cudaSuccess) {

@@ -444,11 +444,8 @@ __global__ void __launch_bounds__(32 * MmaShape<D, sizeof(T)>::NW, 1)
       continue;
     }
     const int s = cs;
-    if (!mbar_wait_bounded(&full_bar[w][s], cph)) {
-      report(p.status, LINATTN_DEV_TIMEOUT);
-      abort = true;
-      break;
-    }
+    // the stage record was written when the tile was issued: an item's q loads and
+    // set-up go out before the wait for its first tile, so their latency overlaps it
     const MmaStage sd = st[w][s];
     const bool first = (sd.h0nh >> 30) & 1u, last = sd.h0nh >> 31;
     if (first) {
@@ -519,6 +516,11 @@ __global__ void __launch_bounds__(32 * MmaShape<D, sizeof(T)>::NW, 1)
       for (int n = 0; n < S::KS; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
       mA = mB = -INFINITY;
       lA = lB = 0.f;
+    }
+    if (!mbar_wait_bounded(&full_bar[w][s], cph)) {
+      report(p.status, LINATTN_DEV_TIMEOUT);
+      abort = true;
+      break;
     }
     const uint32_t kst = ring_s + static_cast<uint32_t>(s) * S::STAGE_BYTES;
     const uint32_t vst = kst + S::TILE_BYTES;

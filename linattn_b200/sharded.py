@@ -89,13 +89,15 @@ class ShardedQuestDecoder:
     as ``cand (chunks, 2, B, H_q, topk)`` int32 (fp32 score bits, then global page ids)
     and the partials as ``part (rows * D + rows)`` fp32 (``o`` rows, then their lse), so
     a step costs two all-gathers; the merge and combine kernels read the gathered
-    buffers in place through their rank strides.
+    buffers in place through their rank strides.  ``select_chunks`` / ``n_splits``
+    override the planned chunk count of the local selection / the split-KV count of
+    the local attention.
     """
 
     def __init__(self, cache: PagedKVCache, n_heads: int, topk: int, page_lo, page_hi, *, sink_pages: int = 0,
                  last_here: bool, sink_here: bool, scale: Optional[float] = None, group=None,
                  q_dtype: torch.dtype = torch.bfloat16, n_ranks: Optional[int] = None,
-                 select_chunks: Optional[int] = None):
+                 select_chunks: Optional[int] = None, n_splits: Optional[int] = None):
         self.cache = cache
         self.n_heads = n_heads
         self.topk = topk
@@ -146,7 +148,8 @@ class ShardedQuestDecoder:
                               self.union_count.data_ptr(), *self.union_count.stride())
         kv_code = L.FP8E4M3 if cache.fp8 else L.dtype_code(cache.k_pool)
         q_code = {torch.float32: L.F32, torch.float16: L.F16, torch.bfloat16: L.BF16}[q_dtype]
-        self.n_splits = plan_splits(b, n_heads, 1, d, kv_code, q_code, hkv, self.max_union, cache.page_size, dev)
+        self.n_splits = n_splits or plan_splits(b, n_heads, 1, d, kv_code, q_code, hkv, self.max_union,
+                                                cache.page_size, dev)
         self._ws_bytes = L.lib().linattn_sparse_attention_workspace(b, n_heads, 1, d, self.n_splits)
         self._ws = torch.empty(max(1, (self._ws_bytes + 3) // 4), dtype=torch.float32, device=dev)
 
