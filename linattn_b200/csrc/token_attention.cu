@@ -20,7 +20,9 @@
 // cp.async.mbarrier.arrive.noinc (32 arrivals per phase).  The math is the
 // transposed formulation of the paged decode kernel: S^T = K Q^T and O^T += V^T P^T
 // with mma.sync m16n8k16, heads as the N = 8 side, online softmax per head in the
-// log2 domain (hardware ex2), P split into 16-bit hi + lo parts, or one f16 part when V
+// log2 domain (hardware ex2; the running maximum lazy, as in the paged kernel: it moves
+// only past a margin of 8, one warp vote per tile; row sums per lane until the end),
+// P split into 16-bit hi + lo parts, or one f16 part when V
 // is given as an f16 copy (a bf16 V scaled by a power of two per (b, kv head), undone
 // on the output).
 #include <cstdio>
@@ -265,7 +267,11 @@ __global__ void __launch_bounds__(32 * TNW, 1) token_attention_kernel(const Toke
     for (int mt = 0; mt < S::MT; ++mt)
 #pragma unroll
       for (int i = 0; i < 4; ++i) sc[mt][i] += sc2[mt][i];
-    float tA = -INFINITY, tB = -INFINITY;
+    // online softmax per head (column), the running maxima lazy: they move only when a
+    // score exceeds them by more than 8 (log2 units; one warp vote per tile), so P <=
+    // 2^8 and o is rescaled only then; the row sums are per-lane partials, summed over
+    // a head column's lanes once, after the last tile
+    bool over = false;
 #pragma unroll
     for (int mt = 0; mt < S::MT; ++mt) {
       const bool v0 = (rows >> (mt * 16 + tk)) & 1u;
@@ -274,42 +280,43 @@ __global__ void __launch_bounds__(32 * TNW, 1) token_attention_kernel(const Toke
       sc[mt][1] = v0 ? sc[mt][1] * sl2 : -INFINITY;
       sc[mt][2] = v1 ? sc[mt][2] * sl2 : -INFINITY;
       sc[mt][3] = v1 ? sc[mt][3] * sl2 : -INFINITY;
-      tA = fmaxf(tA, fmaxf(sc[mt][0], sc[mt][2]));
-      tB = fmaxf(tB, fmaxf(sc[mt][1], sc[mt][3]));
+      over |= fmaxf(sc[mt][0], sc[mt][2]) > mA + 8.f || fmaxf(sc[mt][1], sc[mt][3]) > mB + 8.f;
     }
+    if (__any_sync(0xffffffffu, over)) {
+      float tA = -INFINITY, tB = -INFINITY;
 #pragma unroll
-    for (int off = 4; off <= 16; off <<= 1) {
-      tA = fmaxf(tA, __shfl_xor_sync(0xffffffffu, tA, off));
-      tB = fmaxf(tB, __shfl_xor_sync(0xffffffffu, tB, off));
+      for (int mt = 0; mt < S::MT; ++mt) {
+        tA = fmaxf(tA, fmaxf(sc[mt][0], sc[mt][2]));
+        tB = fmaxf(tB, fmaxf(sc[mt][1], sc[mt][3]));
+      }
+#pragma unroll
+      for (int off = 4; off <= 16; off <<= 1) {
+        tA = fmaxf(tA, __shfl_xor_sync(0xffffffffu, tA, off));
+        tB = fmaxf(tB, __shfl_xor_sync(0xffffffffu, tB, off));
+      }
+      const float nA = fmaxf(mA, tA), nB = fmaxf(mB, tB);
+      const float aA = nA == -INFINITY ? 1.f : tok_ex2(mA - nA);
+      const float aB = nB == -INFINITY ? 1.f : tok_ex2(mB - nB);
+      lA *= aA;
+      lB *= aB;
+      mA = nA;
+      mB = nB;
+#pragma unroll
+      for (int n = 0; n < S::KS; ++n) {
+        o[n][0] *= aA;
+        o[n][1] *= aB;
+        o[n][2] *= aA;
+        o[n][3] *= aB;
+      }
     }
-    const float nA = fmaxf(mA, tA), nB = fmaxf(mB, tB);
-    const float aA = nA == -INFINITY ? 1.f : tok_ex2(mA - nA);
-    const float aB = nB == -INFINITY ? 1.f : tok_ex2(mB - nB);
-    float sA = 0.f, sB = 0.f;
 #pragma unroll
     for (int mt = 0; mt < S::MT; ++mt) {
-      sc[mt][0] = nA == -INFINITY ? 0.f : tok_ex2(sc[mt][0] - nA);
-      sc[mt][2] = nA == -INFINITY ? 0.f : tok_ex2(sc[mt][2] - nA);
-      sc[mt][1] = nB == -INFINITY ? 0.f : tok_ex2(sc[mt][1] - nB);
-      sc[mt][3] = nB == -INFINITY ? 0.f : tok_ex2(sc[mt][3] - nB);
-      sA += sc[mt][0] + sc[mt][2];
-      sB += sc[mt][1] + sc[mt][3];
-    }
-#pragma unroll
-    for (int off = 4; off <= 16; off <<= 1) {
-      sA += __shfl_xor_sync(0xffffffffu, sA, off);
-      sB += __shfl_xor_sync(0xffffffffu, sB, off);
-    }
-    lA = lA * aA + sA;
-    lB = lB * aB + sB;
-    mA = nA;
-    mB = nB;
-#pragma unroll
-    for (int n = 0; n < S::KS; ++n) {
-      o[n][0] *= aA;
-      o[n][1] *= aB;
-      o[n][2] *= aA;
-      o[n][3] *= aB;
+      sc[mt][0] = mA == -INFINITY ? 0.f : tok_ex2(sc[mt][0] - mA);
+      sc[mt][2] = mA == -INFINITY ? 0.f : tok_ex2(sc[mt][2] - mA);
+      sc[mt][1] = mB == -INFINITY ? 0.f : tok_ex2(sc[mt][1] - mB);
+      sc[mt][3] = mB == -INFINITY ? 0.f : tok_ex2(sc[mt][3] - mB);
+      lA += sc[mt][0] + sc[mt][2];
+      lB += sc[mt][1] + sc[mt][3];
     }
 #pragma unroll
     for (int mt = 0; mt < S::MT; ++mt) {
@@ -350,6 +357,11 @@ __global__ void __launch_bounds__(32 * TNW, 1) token_attention_kernel(const Toke
     return;
   }
   // ---- (o, lse) of the item's heads
+#pragma unroll
+  for (int off = 4; off <= 16; off <<= 1) {
+    lA += __shfl_xor_sync(0xffffffffu, lA, off);
+    lB += __shfl_xor_sync(0xffffffffu, lB, off);
+  }
   const float vs = VF16 ? p.v_unscale[b * (p.Hq / p.heads_per_kv) + kvh] : 1.f;
   const float iA = lA > 0.f ? vs / lA : 0.f, iB = lB > 0.f ? vs / lB : 0.f;
   const float lseA = lA > 0.f ? (mA + log2f(lA)) * 0.69314718055994531f : -INFINITY;
