@@ -115,10 +115,6 @@ class ShardedQuestDecoder:
                 and cache.meta_dtype in (torch.float16, torch.bfloat16)):
             raise NotImplementedError("sharded decode needs f16/bf16 page metadata, head_dim 64 or 128 and a GQA "
                                       "group of 1, 2, 4 or 8 query heads")
-        if select_chunks is None and n_ranks > 1 and cache.max_pages <= 2048:
-            # one chunk per (sequence, kv head): the candidates kernel then writes this
-            # rank's block of K itself, with no pre-merge launch
-            select_chunks = 1
         self.chunk_pages, self.chunks = plan_select_chunks(cache.max_pages, g, topk, d, b * hkv, dev, select_chunks,
                                                            ranks=n_ranks, mma=q_dtype == cache.meta_dtype,
                                                            cand_only=True, premerge=n_ranks > 1)
